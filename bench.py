@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""Throughput of the RF-DETR matcher step (fused cost kernel + exact batched LSAP) on B200.
+
+``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl rfm|reference]``
+
+A step is one full ``HungarianMatcher`` pass (cost matrix + every assignment
+problem + device unpack) over one batch of the ``sweep`` workload: 1024 images x
+13 query groups x 300 queries, 2 classes, T ~ Poisson(8) clipped to [1, 60]
+targets per image -> 13,312 [300 x T] problems per GPU.  Under torchrun each rank
+matches its own 1024-image shard (weak scaling, no collective on the data path)
+and ``value`` is all ranks' problems divided by the slowest rank's device time.
+
+Keys beyond the base contract:
+  e2e           the same metric through ``match_layers`` with pinned HOST inputs:
+                the step's input copies and the D2H of its packed index pairs are
+                inside the timed region;
+  roofline      the cost kernel, HBM-bound: algorithmic bytes per launch over its
+                CUDA-event duration, against the measured copy bandwidth;
+  lsap          the solver kernel's device time and problems/s;
+  cpu_baseline  the reference's CPU path (torch CPU op chain + SciPy on a thread
+                pool) on a bounded sample of the same workload, rank 0, N = 1.
+
+``--impl reference`` times that CPU path alone, with every host thread.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "matched problems/s (cost+LSAP) at 1/2/4/8 B200; cost-kernel HBM GB/s vs peak"
+UNIT = "problems/s"
+FALLBACK_HBM_GBS = 6650.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["rfm", "reference"], default="rfm")
+    ap.add_argument("--workload", default="sweep")
+    ap.add_argument("--images", type=int, default=None, help="images per rank (default: the workload's)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
+    ap.add_argument("--cpu-images", type=int, default=64, help="images in one CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def workload_config(wl) -> dict:
+    return {
+        "workload": (f"{wl.name}: {wl.images} images x {wl.group_detr} groups x {wl.queries // wl.group_detr} "
+                     f"queries x {wl.layers} layer(s), {wl.classes} classes, per-image T as documented "
+                     f"in workloads.py; {wl.num_problems} [300 x T] problems per GPU per step"),
+        "images_per_gpu": wl.images,
+        "group_detr": wl.group_detr,
+        "queries": wl.queries,
+        "layers": wl.layers,
+        "classes": wl.classes,
+        "targets_per_gpu": int(sum(wl.sizes)),
+        "problems_per_gpu_step": wl.num_problems,
+        "l2": "flushed between timed steps (256 MiB write outside the events)",
+    }
+
+
+# --------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.path = os.path.join("/tmp", f"rfm_clocks_{os.getpid()}.csv")
+        exe = shutil.which("nvidia-smi")
+        if exe is None:
+            return
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+        gpu_id = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        self.cmd = [exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i", gpu_id]
+
+    def start(self) -> None:
+        if not hasattr(self, "cmd"):
+            return
+        self.fh = open(self.path, "w")
+        self.proc = subprocess.Popen(self.cmd, stdout=self.fh, stderr=subprocess.DEVNULL)
+        time.sleep(0.3)
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        max_mhz = max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max_mhz,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- helpers
+
+
+def peak_hbm() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def cost_bytes(wl, ld: int) -> int:
+    """Algorithmic bytes of one rfm_cost launch: the compact output written once, each
+    prediction (box + logits row) and each target (box + int64 label) read once."""
+    L, B, Q, C = wl.layers, wl.images, wl.queries, wl.classes
+    return 4 * L * Q * ld + 16 * L * B * Q + 4 * L * B * Q * C + 24 * sum(wl.sizes) + 4 * (B + 1)
+
+
+def lsap_bytes(plan) -> int:
+    """Algorithmic bytes of one rfm_lsap launch: every problem's cost block read once, its
+    descriptor read, its int64 (query, target) pairs written."""
+    pr = plan.problems
+    return int((4 * pr["num_queries"].astype(np.int64) * pr["num_targets"]).sum()) + 40 * pr.shape[0] \
+        + 16 * plan.total_pairs
+
+
+def dist_init(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def traffic_per_launch() -> float | None:
+    """DRAM bytes of one cost-kernel launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "cost_kernel_sweep_traffic.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+# --------------------------------------------------------------------------- CPU path
+
+
+def cpu_path_rate(wl, images: int, budget_s: float, threads: int, min_reps: int = 1) -> dict:
+    """problems/s of the reference CPU path on the first ``images`` images, repeated for ~budget_s."""
+    from oracle.cpu_path import CpuMatcher
+
+    images = min(images, wl.images)
+    logits = wl.pred_logits[:, :images].contiguous()
+    boxes = wl.pred_boxes[:, :images].contiguous()
+    targets = wl.targets[:images]
+    problems = wl.layers * wl.group_detr * sum(1 for t in targets if t["labels"].shape[0])
+    m = CpuMatcher(threads=threads)
+    try:
+        m.match(logits, boxes, targets, wl.group_detr, wl.weights)  # warm
+        reps, t0 = 0, time.perf_counter()
+        while reps < min_reps or time.perf_counter() - t0 < budget_s:
+            m.match(logits, boxes, targets, wl.group_detr, wl.weights)
+            reps += 1
+        elapsed = time.perf_counter() - t0
+    finally:
+        m.close()
+    return {"value": problems * reps / elapsed, "unit": UNIT, "seconds": elapsed, "reps": reps,
+            "problems_per_rep": problems}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = dist_init(args)
+    if rank != 0:
+        return
+    from rfdetr_training_throughput_b200 import workloads
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    wl = workloads.make(args.workload, images=args.images)
+    images = min(args.cpu_images, wl.images)
+    sample = {"images": images}
+    from oracle.cpu_path import CpuMatcher
+
+    logits = wl.pred_logits[:, :images].contiguous()
+    boxes = wl.pred_boxes[:, :images].contiguous()
+    targets = wl.targets[:images]
+    problems = wl.layers * wl.group_detr * sum(1 for t in targets if t["labels"].shape[0])
+    m = CpuMatcher(threads=threads)
+    try:
+        for _ in range(args.warmup):
+            m.match(logits, boxes, targets, wl.group_detr, wl.weights)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            m.match(logits, boxes, targets, wl.group_detr, wl.weights)
+        elapsed = time.perf_counter() - t0
+    finally:
+        m.close()
+    value = problems * args.steps / elapsed
+    sample_desc = (f"first {images} images of the {wl.name} workload per step ({problems} problems): torch CPU "
+                   f"op chain + scipy.optimize.linear_sum_assignment on a {threads}-thread pool")
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 cost, fp64 LSAP",
+        "data": "synthetic", "config": workload_config(wl),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample_desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    line["config"]["cpu_sample"] = sample
+    print(json.dumps(line))
+
+
+# --------------------------------------------------------------------------- GPU path
+
+
+def run_rfm(args) -> None:
+    world, rank, local = dist_init(args)
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+
+    from rfdetr_training_throughput_b200 import _lib, matcher, workloads
+
+    wl = workloads.make(args.workload, shard=rank, images=args.images)
+    outputs = wl.outputs_list(device)
+    targets = wl.targets_on(device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def step(events=None, extras=None):
+        return matcher.match_layers(outputs, targets, wl.group_detr, weights=wl.weights, events=events,
+                                    extras=extras)
+
+    extras: dict = {}
+    for _ in range(max(args.warmup, 1)):
+        step(extras=extras)
+    plan = extras["plan"]
+    ld = extras["ld"]
+    torch.cuda.synchronize(device)
+
+    sampler = ClockSampler(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    kernel_events: dict = {}
+    barrier()
+    torch.cuda.synchronize(device)
+    sampler.start()
+    for k in range(args.steps):
+        starts[k].record()
+        step(events=kernel_events)
+        ends[k].record()
+        flush.zero_()
+    torch.cuda.synchronize(device)
+    barrier()
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = float(sum(step_ms))
+
+    def kernel_ms(name):
+        ev = kernel_events.get(name, [])
+        return [ev[i].elapsed_time(ev[i + 1]) for i in range(0, len(ev), 2)]
+
+    cost_ms = kernel_ms("cost")
+    lsap_ms = kernel_ms("lsap")
+    launches = len(cost_ms) + len(lsap_ms)
+
+    total_t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(total_t, op=torch.distributed.ReduceOp.MAX)
+    max_ms = float(total_t.item())
+    problems = wl.num_problems
+    value = world * problems * args.steps / (max_ms / 1e3)
+
+    # ---- end to end: pinned host inputs -> device -> match -> packed pairs back to host
+    e2e = None
+    if not args.no_e2e:
+        h_logits = wl.pred_logits.pin_memory()
+        h_boxes = wl.pred_boxes.pin_memory()
+        h_labels = torch.cat([t["labels"] for t in wl.targets]).pin_memory()
+        h_tboxes = torch.cat([t["boxes"] for t in wl.targets]).pin_memory()
+        sizes = wl.sizes
+        h_pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64).pin_memory()
+        h2d = sum(int(t.numel() * t.element_size()) for t in (h_logits, h_boxes, h_labels, h_tboxes))
+        d2h = int(h_pairs.numel() * h_pairs.element_size())
+
+        def e2e_step():
+            d_logits = h_logits.to(device, non_blocking=True)
+            d_boxes = h_boxes.to(device, non_blocking=True)
+            d_labels = h_labels.to(device, non_blocking=True)
+            d_tboxes = h_tboxes.to(device, non_blocking=True)
+            outs = [{"pred_logits": d_logits[l], "pred_boxes": d_boxes[l]} for l in range(wl.layers)]
+            tg = [{"labels": lb, "boxes": bx} for lb, bx in zip(torch.split(d_labels, sizes),
+                                                               torch.split(d_tboxes, sizes))]
+            ex: dict = {}
+            matcher.match_layers(outs, tg, wl.group_detr, weights=wl.weights, extras=ex)
+            h_pairs.copy_(ex["pairs"], non_blocking=True)
+
+        for _ in range(max(args.warmup, 1)):
+            e2e_step()
+        torch.cuda.synchronize(device)
+        e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize(device)
+        for k in range(args.steps):
+            e_s[k].record()
+            e2e_step()
+            e_e[k].record()
+            flush.zero_()
+        torch.cuda.synchronize(device)
+        barrier()
+        e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+        e2e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+        if world > 1:
+            torch.distributed.all_reduce(e2e_t, op=torch.distributed.ReduceOp.MAX)
+        e2e = {"value": world * problems * args.steps / (float(e2e_t.item()) / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": float(e2e_t.item()) / args.steps}
+
+    # ---- roofline of the cost kernel (HBM-bound) and the solver figures
+    peak, peak_kind = peak_hbm()
+    cb = cost_bytes(wl, ld)
+    cost_avg_s = statistics.mean(cost_ms) / 1e3 if cost_ms else float("nan")
+    achieved = cb / cost_avg_s / 1e9
+    traffic = traffic_per_launch()
+    roofline = {"kernel": "rfm cost_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                if peak_kind == "measured" else "fallback 6.65 TB/s", "traffic": traffic,
+                "algorithmic_bytes_per_launch": cb, "avg_launch_us": cost_avg_s * 1e6}
+    lb = lsap_bytes(plan)
+    lsap_avg_s = statistics.mean(lsap_ms) / 1e3 if lsap_ms else float("nan")
+    lsap = {"kernel": "rfm lsap_kernel", "avg_launch_us": lsap_avg_s * 1e6,
+            "problems_per_s": problems / lsap_avg_s, "algorithmic_bytes_per_launch": lb,
+            "achieved_gbs": lb / lsap_avg_s / 1e9, "share_of_step": (sum(lsap_ms) / total_ms) if total_ms else None,
+            "cols_per_lane": plan.plan.cols_per_lane, "tile_floats": plan.plan.tile_floats,
+            "workspace_bytes": int(plan.plan.workspace_bytes)}
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        threads = int(os.environ.get("LAP_THREADS", "8"))
+        r = cpu_path_rate(wl, args.cpu_images, args.cpu_seconds, threads)
+        cpu = {"value": r["value"], "unit": UNIT, "cores": max(threads, torch.get_num_threads()), "kind": "port",
+               "sample": (f"first {min(args.cpu_images, wl.images)} images of this workload "
+                          f"({r['problems_per_rep']} problems) x {r['reps']} reps in {r['seconds']:.1f} s: torch "
+                          f"CPU op chain ({torch.get_num_threads()} threads) + SciPy on a {threads}-thread pool")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 cost, fp64 LSAP duals", "data": "synthetic",
+            "config": workload_config(wl), "roofline": roofline, "lsap": lsap, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches, "clocks": clocks, "impl": "rfm",
+            "library": _lib.version(), "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms),
+                                                  "max": max(step_ms)},
+        }
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_rfm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,181 @@
+/*
+ * rfm.h - C ABI of the B200 (sm_100a) Hungarian-matching library for RF-DETR.
+ *
+ * The library replaces the two device stages of RF-DETR's HungarianMatcher:
+ *
+ *   rfm_cost   builds the compact detection cost matrix in one pass
+ *              (focal class cost, L1 box distance, GIoU, weighted sum).
+ *              Replaces the Triton launcher fused_matcher_cost
+ *              (kernels_matcher.py:179-234) as called by the patched
+ *              HungarianMatcher._compute_compact_detection_cost_matrix
+ *              (patches.py:123-149).
+ *
+ *   rfm_lsap   solves a batch of rectangular linear assignment problems read
+ *              in place from that matrix, one CTA per problem, with the exact
+ *              arithmetic and tie-breaking of SciPy's rectangular_lsap, and
+ *              writes the (query, target) index pairs straight into their
+ *              final packed position. Replaces batch_lap / lsap_kernel
+ *              (kernels_lap.py:271-305, :332-355) together with the device
+ *              unpack of the patched _assign_padded (patches.py:379-418).
+ *
+ *   rfm_lsap_dense  the same solver under the torch_linear_assignment
+ *              contract: cost [P, W, T] -> matching [P, W] (task or -1).
+ *              Replaces batch_lap (kernels_lap.py:332-355) behind the
+ *              cuda_lap patch (patches.py:291-327).
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are DEVICE pointers owned by the caller, except
+ *     where a comment says "host".  No entry point allocates device memory,
+ *     synchronises the stream or the device, or copies to the host.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is
+ *     the legacy default stream) on the current device.
+ *   - The return value reports argument and launch errors synchronously
+ *     (RFM_OK on success); rfm_error_string() names it.  Per-problem numeric
+ *     outcomes (infeasible or invalid costs) are written to the optional
+ *     device `status` array and are only visible after the stream completes.
+ *   - Calls are thread-compatible: concurrent calls on different streams are
+ *     safe as long as they write disjoint outputs.
+ */
+#ifndef RFM_H_
+#define RFM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes -------------------------------------------------------- */
+#define RFM_OK 0
+#define RFM_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, bad stride */
+#define RFM_ERR_UNSUPPORTED 2      /* outside the supported envelope */
+#define RFM_ERR_LAUNCH 3           /* CUDA reported an error at launch */
+#define RFM_ERR_NO_DEVICE 4        /* no usable CUDA device */
+
+/* ---- per-problem status codes written by the solvers --------------------- */
+#define RFM_STATUS_OK 0
+#define RFM_STATUS_INFEASIBLE 1    /* no finite assignment (SciPy: "cost matrix is infeasible") */
+#define RFM_STATUS_INVALID 2       /* NaN or -inf entry (SciPy: "matrix contains invalid numeric entries") */
+#define RFM_STATUS_NO_SINK 3       /* augmenting search hit its column bound (never expected) */
+
+/* Largest extent of the longer side of one assignment problem. */
+#define RFM_MAX_COLS 1024
+
+/*
+ * One assignment problem, read in place from a row-major cost matrix.
+ * Element (query q, target t) of problem p lives at
+ *     cost[cost_offset + q * ld + t],  0 <= q < num_queries, 0 <= t < num_targets.
+ * Its min(num_queries, num_targets) result pairs are written to
+ *     query_out[out_offset + k], target_out[out_offset + k]
+ * in SciPy's order (ascending query index), with query_base added to every
+ * emitted query index (the group offset g * group_width of Group DETR).
+ * scratch_offset is filled in by rfm_lsap_make_plan (-1: none needed).
+ */
+typedef struct rfm_problem {
+  int64_t cost_offset;
+  int64_t out_offset;
+  int64_t scratch_offset;
+  int32_t num_queries;
+  int32_t num_targets;
+  int32_t query_base;
+  int32_t reserved; /* must be 0 */
+} rfm_problem;
+
+/*
+ * Launch plan for one batch of problems, computed on the host from the
+ * problem sizes (which the caller knows without reading the device).
+ */
+typedef struct rfm_lsap_plan {
+  int32_t cols_per_lane;    /* kernel instantiation: max(rows, cols) <= 32 * cols_per_lane */
+  int32_t tile_floats;      /* on-chip cost tile per CTA, in floats */
+  int32_t max_rows;         /* largest min(num_queries, num_targets) in the batch */
+  int32_t num_problems;
+  int64_t workspace_bytes;  /* device scratch rfm_lsap needs for this batch */
+} rfm_lsap_plan;
+
+/* Library identification string (static storage). */
+const char* rfm_version(void);
+
+/* Human-readable name of a return code (static storage). */
+const char* rfm_error_string(int code);
+
+/*
+ * Compact detection cost matrix for L decoder layers sharing one set of
+ * targets:
+ *
+ *   out[l, q, off[b] + t] = cost_bbox  * L1(pred_box[l,b,q], tgt_box[off[b]+t])
+ *                         + cost_class * focal(pred_logit[l,b,q,label[off[b]+t]])
+ *                         + cost_giou  * -GIoU(xyxy(pred_box[l,b,q]), xyxy(tgt_box[off[b]+t]))
+ *
+ * for every layer l < num_layers, image b < num_images, query q < num_queries
+ * and target t < off[b+1] - off[b].  Row q of the matrix holds image b's
+ * targets in columns off[b] .. off[b+1]-1 and is evaluated against image b's
+ * query q; this is the [Q, sum T] layout produced by
+ * torch.cat([padded[b, :, :T_b] for b], -1) at patches.py:149.
+ *
+ *   pred_logits  [L, B, Q, C] float32, contiguous
+ *   pred_boxes   [L, B, Q, 4] float32 cxcywh, contiguous, 16-byte aligned
+ *   tgt_labels   [S] int64, clamped into [0, C-1] before use
+ *                (kernels_matcher.py:133-134)
+ *   tgt_boxes    [S, 4] float32 cxcywh, 16-byte aligned
+ *   tgt_offsets  [B + 1] int32, off[0] = 0, off[B] = S = sum_targets
+ *   out          [L, Q, ld] float32, ld >= S; columns S .. ld-1 are written
+ *                with 0.  ld % 4 == 0 with a 16-byte aligned `out` selects
+ *                128-bit stores (the fast path); any other ld is accepted.
+ *
+ * Focal cost with gamma 2 (kernels_matcher.py:49-50, 257-260):
+ *   p = sigmoid(x)
+ *   focal(x) = alpha (1-p)^2 (-logsigmoid(x)) - (1-alpha) p^2 (-logsigmoid(-x))
+ * GIoU with the 1e-7 clamps of kernels_matcher.py:121-127.
+ */
+int rfm_cost(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+             const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
+             int num_queries, int num_classes, int sum_targets, int64_t ld, float cost_class,
+             float cost_bbox, float cost_giou, float focal_alpha, float* out, void* stream);
+
+/*
+ * Host-side planning for rfm_lsap.  Reads the sizes of host_problems[0..n),
+ * writes each problem's scratch_offset (floats into the workspace, or -1)
+ * and fills *plan.  Pure host code: no CUDA call.
+ */
+int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, rfm_lsap_plan* plan);
+
+/*
+ * Batched exact rectangular assignment with SciPy's semantics
+ * (scipy.optimize.linear_sum_assignment, rectangular_lsap in SciPy 1.18.1):
+ * the problem is solved untransposed when num_targets >= num_queries and
+ * transposed (rows = targets) otherwise; duals and path costs are float64 on
+ * the float32 costs, and ties between equal path costs are broken exactly as
+ * SciPy's sequential scan breaks them.
+ *
+ *   cost        float32 matrix addressed by each problem's cost_offset and ld
+ *   problems    [num_problems] DEVICE copy of the planned rfm_problem array
+ *   plan        host pointer to the plan rfm_lsap_make_plan returned
+ *   query_out,
+ *   target_out  int64 outputs addressed by out_offset
+ *   status      [num_problems] int32 RFM_STATUS_* or NULL
+ *   workspace   device scratch of plan->workspace_bytes bytes (NULL if 0)
+ *
+ * Problems whose smaller side is 0 write nothing.  When a problem's status
+ * is not RFM_STATUS_OK its output slots are filled with -1.
+ */
+int rfm_lsap(const float* cost, int64_t ld, const rfm_problem* problems,
+             const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out, int32_t* status,
+             void* workspace, void* stream);
+
+/*
+ * torch_linear_assignment.batch_linear_assignment contract
+ * (kernels_lap.py:336-341): cost [P, W, T] float32 contiguous ->
+ * matching [P, W] int64 with the task of each worker, -1 when unassigned.
+ * Solved per problem with SciPy's semantics as in rfm_lsap.
+ * `workspace` must hold rfm_lsap_dense_workspace_bytes(P, W, T) bytes.
+ */
+int64_t rfm_lsap_dense_workspace_bytes(int num_problems, int num_workers, int num_tasks);
+int rfm_lsap_dense(const float* cost, int num_problems, int num_workers, int num_tasks,
+                   int64_t* matching, int32_t* status, void* workspace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RFM_H_ */

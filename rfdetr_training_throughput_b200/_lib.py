@@ -1,0 +1,139 @@
+"""ctypes binding of ``librfm.so``, the sm_100a C ABI declared in ``include/rfm.h``.
+
+There is no CPU fallback: if the library is missing or fails to load, every
+entry point raises.  The library is built in-tree by
+``python -m rfdetr_training_throughput_b200.build``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "librfm.so")
+
+RFM_OK = 0
+RFM_ERR_INVALID_ARGUMENT = 1
+RFM_ERR_UNSUPPORTED = 2
+RFM_ERR_LAUNCH = 3
+RFM_ERR_NO_DEVICE = 4
+
+STATUS_OK = 0
+STATUS_INFEASIBLE = 1
+STATUS_INVALID = 2
+STATUS_NO_SINK = 3
+
+MAX_COLS = 1024
+
+#: Every symbol include/rfm.h declares.
+EXPORTS = (
+    "rfm_version",
+    "rfm_error_string",
+    "rfm_cost",
+    "rfm_lsap_make_plan",
+    "rfm_lsap",
+    "rfm_lsap_dense_workspace_bytes",
+    "rfm_lsap_dense",
+)
+
+#: numpy mirror of ``struct rfm_problem`` (40 bytes).
+PROBLEM_DTYPE = np.dtype(
+    [
+        ("cost_offset", "<i8"),
+        ("out_offset", "<i8"),
+        ("scratch_offset", "<i8"),
+        ("num_queries", "<i4"),
+        ("num_targets", "<i4"),
+        ("query_base", "<i4"),
+        ("reserved", "<i4"),
+    ]
+)
+assert PROBLEM_DTYPE.itemsize == 40
+
+
+class LsapPlan(ctypes.Structure):
+    """Mirror of ``struct rfm_lsap_plan``."""
+
+    _fields_ = [
+        ("cols_per_lane", ctypes.c_int32),
+        ("tile_floats", ctypes.c_int32),
+        ("max_rows", ctypes.c_int32),
+        ("num_problems", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_int64),
+    ]
+
+
+class RfmError(RuntimeError):
+    """A non-zero return code from the C ABI."""
+
+    def __init__(self, func: str, code: int):
+        self.code = code
+        super().__init__(f"{func} failed: {error_string(code)} (code {code})")
+
+
+_lib: ctypes.CDLL | None = None
+
+_p = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+
+
+def load() -> ctypes.CDLL:
+    """Load ``librfm.so`` once; raise if it is missing or incomplete."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is not built; run `python -m rfdetr_training_throughput_b200.build` "
+            "(there is no CPU fallback)"
+        )
+    lib = ctypes.CDLL(LIB_PATH)
+    for name in EXPORTS:
+        if not hasattr(lib, name):
+            raise RuntimeError(f"{LIB_PATH} does not export {name}")
+    lib.rfm_version.restype = ctypes.c_char_p
+    lib.rfm_version.argtypes = []
+    lib.rfm_error_string.restype = ctypes.c_char_p
+    lib.rfm_error_string.argtypes = [_i32]
+    lib.rfm_cost.restype = _i32
+    lib.rfm_cost.argtypes = [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i64,
+                             _f32, _f32, _f32, _f32, _p, _p]
+    lib.rfm_lsap_make_plan.restype = _i32
+    lib.rfm_lsap_make_plan.argtypes = [_p, _i32, ctypes.POINTER(LsapPlan)]
+    lib.rfm_lsap.restype = _i32
+    lib.rfm_lsap.argtypes = [_p, _i64, _p, ctypes.POINTER(LsapPlan), _p, _p, _p, _p, _p]
+    lib.rfm_lsap_dense_workspace_bytes.restype = _i64
+    lib.rfm_lsap_dense_workspace_bytes.argtypes = [_i32, _i32, _i32]
+    lib.rfm_lsap_dense.restype = _i32
+    lib.rfm_lsap_dense.argtypes = [_p, _i32, _i32, _i32, _p, _p, _p, _p]
+    _lib = lib
+    return lib
+
+
+def error_string(code: int) -> str:
+    return load().rfm_error_string(code).decode()
+
+
+def version() -> str:
+    return load().rfm_version().decode()
+
+
+def check(func: str, code: int) -> None:
+    if code != RFM_OK:
+        raise RfmError(func, code)
+
+
+def make_plan(problems: np.ndarray) -> LsapPlan:
+    """Run the host-side planner over a ``PROBLEM_DTYPE`` array (fills scratch offsets in place)."""
+    if problems.dtype != PROBLEM_DTYPE or not problems.flags.c_contiguous:
+        raise ValueError("problems must be a contiguous PROBLEM_DTYPE array")
+    plan = LsapPlan()
+    check("rfm_lsap_make_plan",
+          load().rfm_lsap_make_plan(problems.ctypes.data if problems.size else None, problems.shape[0],
+                                    ctypes.byref(plan)))
+    return plan

@@ -1,0 +1,25 @@
+// Shared helpers of the rfm CUDA library (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "rfm.h"
+
+namespace rfm {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// Maps a CUDA launch-time error onto the library's return codes.
+inline int launch_status() {
+  const cudaError_t err = cudaGetLastError();
+  if (err == cudaSuccess) return RFM_OK;
+  if (err == cudaErrorNoDevice || err == cudaErrorInsufficientDriver) return RFM_ERR_NO_DEVICE;
+  return RFM_ERR_LAUNCH;
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace rfm

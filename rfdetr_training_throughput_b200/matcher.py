@@ -1,0 +1,432 @@
+"""B200 drop-in for RF-DETR's Hungarian matching step.
+
+``HungarianMatcher.forward(outputs, targets, group_detr)`` keeps rf-detr 1.10.1's
+contract (its call sites are the patched methods at patches.py:123-149 and
+patches.py:379-418): ``outputs["pred_logits"]`` ``[B, Q, C]`` and
+``outputs["pred_boxes"]`` ``[B, Q, 4]`` (cxcywh), ``targets[b]["labels"]`` ``[T_b]``
+and ``targets[b]["boxes"]`` ``[T_b, 4]``, ``group_detr`` query groups of
+``Q // group_detr`` queries each.  It returns one ``(query_idx, target_idx)`` pair
+of int64 device tensors per image, ``group_detr * min(Q // group_detr, T_b)``
+pairs long: groups in order, and within a group the pairs SciPy's
+``linear_sum_assignment`` returns for that group's ``[Q/G, T_b]`` block (ascending
+query index), with the group offset ``g * Q/G`` added to the query index
+(patches.py:398).
+
+Two launches do the whole step on the device, with no host synchronisation:
+``rfm_cost`` builds every layer's compact ``[Q, sum T]`` cost matrix and
+``rfm_lsap`` solves all ``layers x images x groups`` problems in place and
+writes the index pairs at their final position; the per-image tuples are views
+of one output buffer (``torch.split`` with host-known sizes).
+
+The sub-steps are exposed under the names of the functions the reference
+patches: ``compute_compact_detection_cost_matrix`` (patches.py:123-149),
+``assign_padded`` (patches.py:379-418) and ``batch_linear_assignment``
+(kernels_lap.py:332-355 behind patches.py:314-317).
+
+There is no CPU or Triton fallback: CPU tensors, segmentation outputs and
+problems wider than ``MAX_COLS`` raise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections import OrderedDict
+from dataclasses import dataclass
+from typing import Any, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+
+DEFAULT_WEIGHTS = {"cost_class": 2.0, "cost_bbox": 5.0, "cost_giou": 2.0, "focal_alpha": 0.25}
+
+
+def _stream_handle(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this matcher has no CPU path)")
+
+
+def _aligned16(t: torch.Tensor) -> torch.Tensor:
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+# --------------------------------------------------------------------------- plans
+
+
+@dataclass
+class StepPlan:
+    """Everything about one matcher step that depends only on host-known sizes."""
+
+    sizes: tuple[int, ...]
+    layers: int
+    queries: int
+    group_detr: int
+    ld: int
+    problems: np.ndarray  # PROBLEM_DTYPE, in launch order (largest tile first)
+    order: np.ndarray  # launch index -> (layer, image, group) problem index
+    plan: _lib.LsapPlan
+    total_pairs: int
+    per_image: list[int]  # pairs per (layer, image), layer-major
+    device_blob: torch.Tensor  # problems bytes followed by int32 offsets [B+1]
+    offsets_byte: int
+
+    @property
+    def problems_ptr(self) -> int:
+        return self.device_blob.data_ptr()
+
+    @property
+    def offsets_ptr(self) -> int:
+        return self.device_blob.data_ptr() + self.offsets_byte
+
+
+def build_problems(sizes: Sequence[int], layers: int, queries: int, group_detr: int, ld: int):
+    """Problem descriptors of a step, in (layer, image, group) order.
+
+    Problem ``(l, b, g)`` is the ``[Q/G, T_b]`` block of layer ``l``'s compact
+    matrix at rows ``g*Q/G ...`` and columns ``off[b] ...``; its pairs go to the
+    ``(l, b)`` image chunk at ``g * min(Q/G, T_b)``.  The layer-image-group order
+    and the group offset follow ``_stack_padded`` as patches.py:371,398 reads it.
+    Returns ``(problems, per_image_pairs, total_pairs, offsets)``; problems whose
+    image has no target are dropped.
+    """
+    if group_detr < 1 or queries % group_detr:
+        raise ValueError(f"num_queries {queries} is not a multiple of group_detr {group_detr}")
+    sz = np.asarray(sizes, dtype=np.int64).reshape(-1)
+    if (sz < 0).any():
+        raise ValueError("negative target count")
+    nimg = sz.shape[0]
+    qg = queries // group_detr
+    offsets = np.zeros(nimg + 1, dtype=np.int64)
+    offsets[1:] = np.cumsum(sz)
+    pairs = np.minimum(sz, qg)
+    per_image = np.tile(group_detr * pairs, layers)
+    image_base = np.zeros(layers * nimg + 1, dtype=np.int64)
+    image_base[1:] = np.cumsum(per_image)
+    lay = np.repeat(np.arange(layers, dtype=np.int64), nimg * group_detr)
+    img = np.tile(np.repeat(np.arange(nimg, dtype=np.int64), group_detr), layers)
+    grp = np.tile(np.arange(group_detr, dtype=np.int64), layers * nimg)
+    keep = sz[img] > 0
+    lay, img, grp = lay[keep], img[keep], grp[keep]
+    pr = np.zeros(lay.shape[0], dtype=_lib.PROBLEM_DTYPE)
+    pr["cost_offset"] = lay * queries * ld + grp * qg * ld + offsets[img]
+    pr["out_offset"] = image_base[lay * nimg + img] + grp * pairs[img]
+    pr["num_queries"] = qg
+    pr["num_targets"] = sz[img]
+    pr["query_base"] = grp * qg
+    return pr, [int(x) for x in per_image], int(image_base[-1]), offsets
+
+
+class _PlanCache:
+    def __init__(self, capacity: int = 64):
+        self.capacity = capacity
+        self._d: OrderedDict[tuple, StepPlan] = OrderedDict()
+
+    def get(self, key: tuple, make) -> StepPlan:
+        hit = self._d.get(key)
+        if hit is not None:
+            self._d.move_to_end(key)
+            return hit
+        value = make()
+        self._d[key] = value
+        if len(self._d) > self.capacity:
+            self._d.popitem(last=False)
+        return value
+
+
+_PLANS = _PlanCache()
+
+
+def plan_step(sizes: Sequence[int], layers: int, queries: int, group_detr: int, ld: int,
+              device: torch.device) -> StepPlan:
+    """Cached host planning plus ONE non-blocking pinned upload of descriptors and offsets."""
+    sizes = tuple(int(s) for s in sizes)
+    key = (sizes, layers, queries, group_detr, ld, str(device))
+
+    def make() -> StepPlan:
+        pr, per_image, total, offsets = build_problems(sizes, layers, queries, group_detr, ld)
+        need = pr["num_queries"].astype(np.int64) * (pr["num_targets"].astype(np.int64) | 1)
+        order = np.argsort(-need, kind="stable")
+        pr = np.ascontiguousarray(pr[order])
+        plan = _lib.make_plan(pr)
+        pbytes = pr.view(np.uint8).reshape(-1)
+        off32 = offsets.astype(np.int32)
+        offsets_byte = (pbytes.shape[0] + 15) // 16 * 16
+        blob = np.zeros(offsets_byte + off32.nbytes, dtype=np.uint8)
+        blob[: pbytes.shape[0]] = pbytes
+        blob[offsets_byte:] = off32.view(np.uint8)
+        host = torch.from_numpy(blob).pin_memory()
+        dev = host.to(device, non_blocking=True)
+        return StepPlan(sizes, layers, queries, group_detr, ld, pr, order, plan, total, per_image, dev,
+                        offsets_byte)
+
+    return _PLANS.get(key, make)
+
+
+# --------------------------------------------------------------------------- kernels
+
+
+def _gather_targets(targets: Sequence[dict], device: torch.device):
+    sizes = [int(t["labels"].shape[0]) for t in targets]
+    if any(int(t["boxes"].shape[0]) != s for t, s in zip(targets, sizes)):
+        raise ValueError("targets[i]['labels'] and ['boxes'] disagree in length")
+    labels = torch.cat([t["labels"].reshape(-1) for t in targets]).to(device=device, dtype=torch.int64)
+    boxes = torch.cat([t["boxes"].reshape(-1, 4) for t in targets]).to(device=device, dtype=torch.float32)
+    return sizes, labels.contiguous(), _aligned16(boxes.contiguous())
+
+
+def _stack_layer_outputs(outputs_list: Sequence[dict]) -> tuple[torch.Tensor, torch.Tensor]:
+    logits = [o["pred_logits"] for o in outputs_list]
+    boxes = [o["pred_boxes"] for o in outputs_list]
+    for i, (lg, bx) in enumerate(zip(logits, boxes)):
+        _require_cuda(lg, f"outputs[{i}]['pred_logits']")
+        _require_cuda(bx, f"outputs[{i}]['pred_boxes']")
+        if lg.dim() != 3 or bx.dim() != 3 or bx.shape[-1] != 4 or lg.shape[:2] != bx.shape[:2]:
+            raise ValueError("expected pred_logits [B, Q, C] and pred_boxes [B, Q, 4]")
+    if len(outputs_list) == 1:
+        lg = logits[0].unsqueeze(0)
+        bx = boxes[0].unsqueeze(0)
+    else:
+        lg = torch.stack(logits)
+        bx = torch.stack(boxes)
+    lg = lg.to(torch.float32).contiguous()
+    bx = _aligned16(bx.to(torch.float32).contiguous())
+    return lg, bx
+
+
+def launch_cost(logits: torch.Tensor, boxes: torch.Tensor, labels: torch.Tensor, tgt_boxes: torch.Tensor,
+                offsets_ptr: int, sum_t: int, ld: int, weights: dict, out: torch.Tensor) -> None:
+    """Enqueue ``rfm_cost`` for logits [L,B,Q,C] / boxes [L,B,Q,4] into ``out`` [L,Q,ld]."""
+    layers, nimg, queries, ncls = logits.shape
+    lib = _lib.load()
+    _lib.check("rfm_cost", lib.rfm_cost(
+        _ptr(logits), _ptr(boxes), _ptr(labels), _ptr(tgt_boxes), ctypes.c_void_p(offsets_ptr),
+        layers, nimg, queries, ncls, sum_t, ld,
+        float(weights["cost_class"]), float(weights["cost_bbox"]), float(weights["cost_giou"]),
+        float(weights["focal_alpha"]), _ptr(out), _stream_handle(out.device)))
+
+
+def launch_lsap(cost: torch.Tensor, ld: int, plan: StepPlan, pairs: torch.Tensor,
+                status: torch.Tensor | None) -> None:
+    """Enqueue ``rfm_lsap`` over a planned step; ``pairs`` is int64 [2, total_pairs]."""
+    lib = _lib.load()
+    ws = None
+    if plan.plan.workspace_bytes > 0:
+        ws = torch.empty(int(plan.plan.workspace_bytes), dtype=torch.uint8, device=cost.device)
+    q_out = pairs[0]
+    t_out = pairs[1]
+    _lib.check("rfm_lsap", lib.rfm_lsap(
+        _ptr(cost), ld, ctypes.c_void_p(plan.problems_ptr), ctypes.byref(plan.plan),
+        _ptr(q_out), _ptr(t_out), _ptr(status), _ptr(ws), _stream_handle(cost.device)))
+
+
+def raise_on_status(status: torch.Tensor) -> None:
+    """Host check of per-problem solver status (synchronises; SciPy's error messages)."""
+    st = status.cpu()
+    if bool((st == _lib.STATUS_INVALID).any()):
+        raise ValueError("matrix contains invalid numeric entries")
+    if bool((st == _lib.STATUS_INFEASIBLE).any()):
+        raise ValueError("cost matrix is infeasible")
+    if bool((st != _lib.STATUS_OK).any()):
+        raise RuntimeError("assignment solver reached its iteration bound")
+
+
+# --------------------------------------------------------------------------- matcher
+
+
+def _record(events: dict | None, name: str):
+    if events is None:
+        return None
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record()
+    events.setdefault(name, []).append(ev)
+    return ev
+
+
+def match_layers(outputs_list: Sequence[dict], targets: Sequence[dict], group_detr: int = 1, *,
+                 weights: dict | None = None, check_status: bool = False,
+                 return_cost: bool = False, extras: dict | None = None,
+                 events: dict | None = None) -> Any:
+    """Match every decoder layer of one step against the same targets, in two launches.
+
+    Returns one list of per-image ``(query_idx, target_idx)`` tuples per layer
+    (and the padded ``[L, Q, ld]`` cost buffer with ``return_cost``).  ``extras``,
+    when given, receives the packed ``[2, total]`` pair buffer the tuples view
+    (``"pairs"``), the cost buffer and the step plan.  ``events``, when given,
+    collects CUDA events recorded on the launching stream around each kernel
+    (``"cost"`` and ``"lsap"``: start/end pairs), for timing.
+    """
+    w = dict(DEFAULT_WEIGHTS if weights is None else weights)
+    if not outputs_list:
+        return []
+    logits, boxes = _stack_layer_outputs(outputs_list)
+    device = logits.device
+    layers, nimg, queries, _ = logits.shape
+    if len(targets) != nimg:
+        raise ValueError(f"{len(targets)} targets for a batch of {nimg} images")
+    sizes, labels, tgt_boxes = _gather_targets(targets, device)
+    sum_t = sum(sizes)
+    ld = (sum_t + 3) // 4 * 4
+    plan = plan_step(sizes, layers, queries, group_detr, ld, device)
+    cost = torch.empty((layers, queries, ld), dtype=torch.float32, device=device)
+    pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=device)
+    status = None
+    if check_status:
+        status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=device)
+    if ld > 0:
+        _record(events, "cost")
+        launch_cost(logits, boxes, labels, tgt_boxes, plan.offsets_ptr, sum_t, ld, w, cost)
+        _record(events, "cost")
+    if plan.problems.shape[0] > 0:
+        _record(events, "lsap")
+        launch_lsap(cost, ld, plan, pairs, status)
+        _record(events, "lsap")
+    if status is not None:
+        raise_on_status(status)
+    q_chunks = torch.split(pairs[0], plan.per_image)
+    t_chunks = torch.split(pairs[1], plan.per_image)
+    result = [[(q_chunks[l * nimg + b], t_chunks[l * nimg + b]) for b in range(nimg)] for l in range(layers)]
+    if extras is not None:
+        extras.update(pairs=pairs, cost=cost, plan=plan, ld=ld)
+    if return_cost:
+        return result, cost
+    return result
+
+
+def compute_compact_detection_cost_matrix(outputs: dict, targets: Sequence[dict], *,
+                                          weights: dict | None = None) -> torch.Tensor:
+    """Compact ``[Q, sum T]`` cost (``[L, Q, sum T]`` for 4-D logits), contiguous float32.
+
+    Same result as the triton_matcher patch's method (patches.py:123-149) without the
+    padded intermediate.  Labels are always clamped into ``[0, C-1]``
+    (kernels_matcher.py:133-134).
+    """
+    w = dict(DEFAULT_WEIGHTS if weights is None else weights)
+    lg, bx = outputs["pred_logits"], outputs["pred_boxes"]
+    _require_cuda(lg, "pred_logits")
+    _require_cuda(bx, "pred_boxes")
+    squeeze = lg.dim() == 3
+    if squeeze:
+        lg, bx = lg.unsqueeze(0), bx.unsqueeze(0)
+    lg = lg.to(torch.float32).contiguous()
+    bx = _aligned16(bx.to(torch.float32).contiguous())
+    layers, nimg, queries, _ = lg.shape
+    sizes, labels, tgt_boxes = _gather_targets(targets, lg.device)
+    sum_t = sum(sizes)
+    out = torch.empty((layers, queries, sum_t), dtype=torch.float32, device=lg.device)
+    if sum_t > 0:
+        offs = torch.tensor(np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)).pin_memory()
+        offs = offs.to(lg.device, non_blocking=True)
+        launch_cost(lg, bx, labels, tgt_boxes, offs.data_ptr(), sum_t, sum_t, w, out)
+    return out[0] if squeeze else out
+
+
+def assign_padded(cost_matrices: Sequence[torch.Tensor], sizes: Sequence[int], group_width: int,
+                  group_detr: int, *, check_status: bool = False) -> list[list[tuple[torch.Tensor, torch.Tensor]]]:
+    """``_assignment._assign_padded`` contract (patches.py:379-418), solved in place.
+
+    ``cost_matrices`` holds one compact ``[group_width * group_detr, sum T]``
+    matrix per layer.  No padding, stacking or sorting pass: the solver reads each
+    ``[group_width, T_b]`` block where it lies and writes the pairs at their final
+    position.  Returns, per layer, per image, ``(query_idx, target_idx)``.
+    """
+    results = []
+    for layer, cost in enumerate(cost_matrices):
+        _require_cuda(cost, f"cost_matrices[{layer}]")
+        if cost.dtype != torch.float32:
+            cost = cost.float()
+        if cost.dim() != 2 or cost.stride(1) != 1:
+            cost = cost.contiguous()
+        queries = group_width * group_detr
+        if cost.shape[0] != queries or cost.shape[1] != sum(sizes):
+            raise ValueError(f"cost matrix {tuple(cost.shape)} does not match {queries} queries x {sum(sizes)} targets")
+        ld = int(cost.stride(0))
+        plan = plan_step(sizes, 1, queries, group_detr, ld, cost.device)
+        pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=cost.device)
+        status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=cost.device) if check_status else None
+        if plan.problems.shape[0] > 0:
+            launch_lsap(cost, ld, plan, pairs, status)
+        if status is not None:
+            raise_on_status(status)
+        q_chunks = torch.split(pairs[0], plan.per_image)
+        t_chunks = torch.split(pairs[1], plan.per_image)
+        results.append(list(zip(q_chunks, t_chunks)))
+    return results
+
+
+def batch_linear_assignment(cost: torch.Tensor, *, check_status: bool = False) -> torch.Tensor:
+    """``torch_linear_assignment.batch_linear_assignment`` contract (kernels_lap.py:336-341).
+
+    ``cost`` ``[P, W, T]`` float32 CUDA -> ``[P, W]`` int64 task of each worker, -1
+    when unassigned, each problem solved as ``scipy.optimize.linear_sum_assignment``
+    solves it.
+    """
+    _require_cuda(cost, "cost")
+    if cost.dim() != 3:
+        raise ValueError("cost must be [problems, workers, tasks]")
+    cost = cost.to(torch.float32).contiguous()
+    nprob, workers, tasks = cost.shape
+    if max(workers, tasks) > _lib.MAX_COLS:
+        raise ValueError(f"problems wider than {_lib.MAX_COLS} columns are outside the supported envelope")
+    lib = _lib.load()
+    matching = torch.empty((nprob, workers), dtype=torch.int64, device=cost.device)
+    if nprob == 0 or workers == 0:
+        return matching
+    ws_bytes = int(lib.rfm_lsap_dense_workspace_bytes(nprob, workers, tasks))
+    if ws_bytes < 0:
+        raise _lib.RfmError("rfm_lsap_dense_workspace_bytes", -ws_bytes)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cost.device) if ws_bytes else None
+    status = torch.empty(nprob, dtype=torch.int32, device=cost.device) if check_status else None
+    _lib.check("rfm_lsap_dense", lib.rfm_lsap_dense(
+        _ptr(cost), nprob, workers, tasks, _ptr(matching), _ptr(status), _ptr(ws), _stream_handle(cost.device)))
+    if status is not None:
+        raise_on_status(status)
+    return matching
+
+
+class HungarianMatcher(torch.nn.Module):
+    """Drop-in for ``rfdetr.models.matcher.HungarianMatcher`` (detection path).
+
+    Constructor arguments mirror rf-detr's (``cost_class``, ``cost_bbox``,
+    ``cost_giou``, ``focal_alpha``; focal gamma is fixed at 2,
+    kernels_matcher.py:49-50).
+    """
+
+    def __init__(self, cost_class: float = 1.0, cost_bbox: float = 1.0, cost_giou: float = 1.0,
+                 focal_alpha: float = 0.25, **unused: Any):
+        super().__init__()
+        self.cost_class = float(cost_class)
+        self.cost_bbox = float(cost_bbox)
+        self.cost_giou = float(cost_giou)
+        self.focal_alpha = float(focal_alpha)
+        if self.cost_class == 0 and self.cost_bbox == 0 and self.cost_giou == 0:
+            raise ValueError("all costs can't be 0")
+
+    @property
+    def weights(self) -> dict:
+        return {"cost_class": self.cost_class, "cost_bbox": self.cost_bbox, "cost_giou": self.cost_giou,
+                "focal_alpha": self.focal_alpha}
+
+    @torch.no_grad()
+    def forward(self, outputs: dict, targets: Sequence[dict], group_detr: int = 1):
+        if "pred_masks" in outputs:
+            raise NotImplementedError("segmentation matching is outside this matcher (detection path only)")
+        return match_layers([outputs], targets, group_detr, weights=self.weights)[0]
+
+    @torch.no_grad()
+    def forward_layers(self, outputs_list: Sequence[dict], targets: Sequence[dict], group_detr: int = 1):
+        """All decoder layers of a step at once (the stacked_costs path, patches.py:235-249)."""
+        return match_layers(outputs_list, targets, group_detr, weights=self.weights)
+
+    @torch.no_grad()
+    def _compute_compact_detection_cost_matrix(self, outputs: dict, targets: Sequence[dict], *,
+                                               clamp_target_labels: bool = False) -> torch.Tensor:
+        return compute_compact_detection_cost_matrix(outputs, targets, weights=self.weights)

@@ -1,0 +1,91 @@
+"""rfm_cost on the GPU against the numpy oracle and the torch-operator golden fixtures."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import COST_RTOL
+from golden_io import matcher_case, names, to_targets
+from oracle import cost as ocost
+from rfdetr_training_throughput_b200 import matcher, workloads
+
+pytestmark = pytest.mark.gpu
+
+
+def _gpu_cost(logits, boxes, labels, tboxes, weights):
+    dev = torch.device("cuda")
+    outputs = {"pred_logits": torch.as_tensor(logits, device=dev), "pred_boxes": torch.as_tensor(boxes, device=dev)}
+    out = matcher.compute_compact_detection_cost_matrix(outputs, to_targets(labels, tboxes, dev), weights=weights)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def _assert_close(gpu, ref):
+    assert gpu.shape == ref.shape
+    assert np.isfinite(gpu).all()
+    bound = COST_RTOL * np.maximum(np.abs(ref), 1.0)
+    worst = float((np.abs(gpu - ref) / bound).max(initial=0.0))
+    assert worst <= 1.0, f"cost differs by {worst:.3f}x the tolerance"
+
+
+@pytest.mark.parametrize("name", names("matcher"))
+def test_cost_golden(name):
+    logits, boxes, labels, tboxes, _g, w, golden, _p = matcher_case(name)
+    gpu = _gpu_cost(logits, boxes, labels, tboxes, w)
+    _assert_close(gpu, ocost.compact_cost(logits, boxes, labels, tboxes, **w))
+    _assert_close(gpu, golden)
+
+
+@pytest.mark.parametrize("name", ["cpu1", "step", "crowd", "ties"])
+def test_cost_workloads(name):
+    wl = workloads.make(name, images=4) if name in ("crowd", "ties") else workloads.make(name)
+    labels = [t["labels"].numpy() for t in wl.targets]
+    tboxes = [t["boxes"].numpy() for t in wl.targets]
+    gpu = _gpu_cost(wl.pred_logits.numpy(), wl.pred_boxes.numpy(), labels, tboxes, wl.weights)
+    _assert_close(gpu, ocost.compact_cost(wl.pred_logits.numpy(), wl.pred_boxes.numpy(), labels, tboxes, **wl.weights))
+
+
+def test_box_terms_are_bit_exact():
+    """With cost_class = 0 only L1 and GIoU remain; their float32 op order is the reference chain's."""
+    wl = workloads.make("step", layers=2)
+    w = dict(wl.weights, cost_class=0.0)
+    labels = [t["labels"].numpy() for t in wl.targets]
+    tboxes = [t["boxes"].numpy() for t in wl.targets]
+    gpu = _gpu_cost(wl.pred_logits.numpy(), wl.pred_boxes.numpy(), labels, tboxes, w)
+    ref = ocost.compact_cost(wl.pred_logits.numpy(), wl.pred_boxes.numpy(), labels, tboxes, **w)
+    np.testing.assert_array_equal(gpu, ref)
+
+
+def test_labels_are_clamped_and_degenerate_boxes_finite():
+    wl = workloads.make("cpu1")
+    labels = [np.array([-3, 0, 1, 7, 1, 0, 2, 5, -1, 0, 1, 1], dtype=np.int64)]
+    tboxes = [wl.targets[0]["boxes"].numpy().copy()]
+    tboxes[0][:, 2:] = 0.0
+    boxes = wl.pred_boxes.numpy().copy()
+    boxes[..., 2:] = 0.0
+    gpu = _gpu_cost(wl.pred_logits.numpy(), boxes, labels, tboxes, wl.weights)
+    _assert_close(gpu, ocost.compact_cost(wl.pred_logits.numpy(), boxes, labels, tboxes, **wl.weights))
+
+
+def test_padded_stride_and_ragged_stride():
+    """The fused path pads rows to a multiple of 4 columns (pad written as 0); the drop-in is exact-width."""
+    wl = workloads.make("step", layers=1, images=3)
+    dev = torch.device("cuda")
+    res, padded = matcher.match_layers(wl.outputs_list(dev), wl.targets_on(dev), wl.group_detr,
+                                       weights=wl.weights, return_cost=True)
+    exact = matcher.compute_compact_detection_cost_matrix(wl.outputs_list(dev)[0], wl.targets_on(dev),
+                                                          weights=wl.weights)
+    s = sum(wl.sizes)
+    assert exact.shape == (wl.queries, s) and exact.is_contiguous()
+    assert torch.equal(padded[0, :, :s], exact)
+    assert padded.shape[-1] % 4 == 0
+    assert bool((padded[0, :, s:] == 0).all())
+
+
+def test_empty_targets():
+    wl = workloads.make("step", layers=1, images=2)
+    dev = torch.device("cuda")
+    targets = [{"labels": torch.zeros(0, dtype=torch.int64, device=dev),
+                "boxes": torch.zeros(0, 4, device=dev)} for _ in range(2)]
+    out = matcher.compute_compact_detection_cost_matrix(wl.outputs_list(dev)[0], targets, weights=wl.weights)
+    assert out.shape == (wl.queries, 0)

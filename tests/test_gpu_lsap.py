@@ -1,0 +1,104 @@
+"""The device solver against SciPy itself and the C oracle: identical indices, ties included."""
+
+import numpy as np
+import pytest
+import torch
+from scipy.optimize import linear_sum_assignment as scipy_lsa
+
+from golden_io import lsap_case, names
+from oracle.lsap import linear_sum_assignment as oracle_lsa
+from rfdetr_training_throughput_b200 import matcher
+
+pytestmark = pytest.mark.gpu
+
+
+def _dense_expected(cost: np.ndarray) -> np.ndarray:
+    """[P, W, T] -> [P, W] matching as torch_linear_assignment builds it from SciPy (patches.py:216-228)."""
+    out = np.full(cost.shape[:2], -1, dtype=np.int64)
+    for p in range(cost.shape[0]):
+        if cost.shape[2] == 0:
+            continue
+        r, c = scipy_lsa(cost[p])
+        out[p, r] = c
+    return out
+
+
+def _solve_dense(cost: np.ndarray, **kw) -> np.ndarray:
+    got = matcher.batch_linear_assignment(torch.as_tensor(cost, device="cuda"), **kw)
+    return got.cpu().numpy()
+
+
+@pytest.mark.parametrize("shape", [(520, 300, 1), (520, 300, 12), (520, 300, 37), (104, 300, 60),
+                                   (8, 300, 300), (1, 16, 16), (3, 64, 0), (6, 300, 333), (4, 64, 16),
+                                   (3, 600, 40), (5, 40, 1000)])
+def test_dense_random(shape):
+    rng = np.random.default_rng(sum(shape))
+    cost = (rng.random(shape, dtype=np.float32) * 10 - 5).astype(np.float32)
+    assert np.array_equal(_solve_dense(cost), _dense_expected(cost))
+
+
+@pytest.mark.parametrize("q", [4, 16])
+@pytest.mark.parametrize("shape", [(64, 300, 8), (32, 300, 40), (16, 300, 150), (8, 300, 260), (8, 300, 300),
+                                   (6, 40, 40), (6, 120, 200)])
+def test_dense_quantised_ties(shape, q):
+    rng = np.random.default_rng(shape[2] * q)
+    cost = (rng.integers(0, q, shape) / q).astype(np.float32)
+    assert np.array_equal(_solve_dense(cost), _dense_expected(cost))
+
+
+def test_dense_constant_matrix():
+    cost = np.full((4, 300, 8), 1.5, dtype=np.float32)
+    assert np.array_equal(_solve_dense(cost), _dense_expected(cost))
+
+
+@pytest.mark.parametrize("name", names("lsap"))
+def test_golden_lsap(name):
+    for m, res, r, c in lsap_case(name):
+        batch = m[None]
+        if res == "ok":
+            got = _solve_dense(batch)[0]
+            expect = np.full(m.shape[0], -1, dtype=np.int64)
+            expect[r] = c
+            assert np.array_equal(got, expect)
+        else:
+            msg = "infeasible" if res == "infeasible" else "invalid"
+            with pytest.raises(ValueError, match=msg):
+                _solve_dense(batch, check_status=True)
+            assert (_solve_dense(batch) == -1).all()
+
+
+def test_near_ties_need_float64():
+    """Costs 1e-6 apart only resolve as SciPy does with float64 path costs."""
+    rng = np.random.default_rng(5)
+    base = rng.integers(0, 4, (64, 300, 10)).astype(np.float32)
+    bump = rng.random(base.shape) < 0.05
+    base[bump] += np.float32(2.0 ** -20)
+    assert np.array_equal(_solve_dense(base), _dense_expected(base))
+
+
+def test_assign_padded_on_compact_matrix():
+    """The _assign_padded contract on a compact [G*300, sum T] matrix, against the C oracle."""
+    rng = np.random.default_rng(9)
+    sizes = [5, 0, 17, 1, 300, 9]
+    g = 3
+    cost = rng.integers(0, 8, (g * 300, sum(sizes))).astype(np.float32) / 8
+    res = matcher.assign_padded([torch.as_tensor(cost, device="cuda")], sizes, 300, g)[0]
+    col = 0
+    for b, t in enumerate(sizes):
+        q_exp, t_exp = [], []
+        for gi in range(g if t else 0):
+            r, c = oracle_lsa(cost[gi * 300:(gi + 1) * 300, col:col + t])
+            q_exp.append(r + gi * 300)
+            t_exp.append(c)
+        col += t
+        qs, ts = res[b]
+        assert np.array_equal(qs.cpu().numpy(), np.concatenate(q_exp) if q_exp else np.zeros(0))
+        assert np.array_equal(ts.cpu().numpy(), np.concatenate(t_exp) if t_exp else np.zeros(0))
+
+
+def test_repeat_calls_are_deterministic():
+    rng = np.random.default_rng(2)
+    cost = torch.as_tensor((rng.integers(0, 3, (200, 300, 24)) / 3).astype(np.float32), device="cuda")
+    a = matcher.batch_linear_assignment(cost)
+    b = matcher.batch_linear_assignment(cost)
+    assert torch.equal(a, b)

@@ -11,7 +11,7 @@ matches its own 1024-image shard (weak scaling, no collective on the data path)
 and ``value`` is all ranks' problems divided by the slowest rank's device time.
 
 Keys beyond the base contract:
-  e2e           the same metric through ``match_layers`` with pinned HOST inputs:
+  e2e           the same metric through ``match_packed`` with pinned HOST inputs:
                 the step's input copies and the D2H of its packed index pairs are
                 inside the timed region;
   roofline      the cost kernel, HBM-bound: algorithmic bytes per launch over its
@@ -50,7 +50,7 @@ L2_FLUSH_BYTES = 256 << 20
 def parse() -> argparse.Namespace:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["rfm", "reference"], default="rfm")
     ap.add_argument("--workload", default="sweep")
@@ -96,7 +96,7 @@ class ClockSampler:
             return
         uuid = str(torch.cuda.get_device_properties(device).uuid)
         gpu_id = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
-        self.cmd = [exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i", gpu_id]
+        self.cmd = [exe, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50", "-i", gpu_id]
 
     def start(self) -> None:
         if not hasattr(self, "cmd"):
@@ -148,11 +148,11 @@ def peak_hbm() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def cost_bytes(wl, ld: int) -> int:
-    """Algorithmic bytes of one rfm_cost launch: the compact output written once, each
-    prediction (box + logits row) and each target (box + int64 label) read once."""
+def cost_bytes(wl) -> int:
+    """Algorithmic bytes of one rfm_cost launch: every cost element written once (L x Q x sum T
+    float32), each prediction (box + logits row) and each target (box + int64 label) read once."""
     L, B, Q, C = wl.layers, wl.images, wl.queries, wl.classes
-    return 4 * L * Q * ld + 16 * L * B * Q + 4 * L * B * Q * C + 24 * sum(wl.sizes) + 4 * (B + 1)
+    return 4 * L * Q * sum(wl.sizes) + 16 * L * B * Q + 4 * L * B * Q * C + 24 * sum(wl.sizes) + 4 * (B + 1)
 
 
 def lsap_bytes(plan) -> int:
@@ -263,8 +263,9 @@ def run_rfm(args) -> None:
     from rfdetr_training_throughput_b200 import _lib, matcher, workloads
 
     wl = workloads.make(args.workload, shard=rank, images=args.images)
-    outputs = wl.outputs_list(device)
-    targets = wl.targets_on(device)
+    logits = wl.pred_logits.to(device)
+    boxes = wl.pred_boxes.to(device)
+    packed = matcher.PackedTargets.from_list(wl.targets_on(device), device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=device)
 
     def barrier():
@@ -272,23 +273,23 @@ def run_rfm(args) -> None:
             torch.distributed.barrier()
 
     def step(events=None, extras=None):
-        return matcher.match_layers(outputs, targets, wl.group_detr, weights=wl.weights, events=events,
+        return matcher.match_packed(logits, boxes, packed, wl.group_detr, weights=wl.weights, events=events,
                                     extras=extras)
 
+    sampler = ClockSampler(device)
+    sampler.start()
     extras: dict = {}
     for _ in range(max(args.warmup, 1)):
         step(extras=extras)
     plan = extras["plan"]
-    ld = extras["ld"]
+    ld = sum(wl.sizes)
     torch.cuda.synchronize(device)
 
-    sampler = ClockSampler(device)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     kernel_events: dict = {}
     barrier()
     torch.cuda.synchronize(device)
-    sampler.start()
     for k in range(args.steps):
         starts[k].record()
         step(events=kernel_events)
@@ -327,17 +328,15 @@ def run_rfm(args) -> None:
         h2d = sum(int(t.numel() * t.element_size()) for t in (h_logits, h_boxes, h_labels, h_tboxes))
         d2h = int(h_pairs.numel() * h_pairs.element_size())
 
+        sizes = tuple(sizes)
+
         def e2e_step():
             d_logits = h_logits.to(device, non_blocking=True)
             d_boxes = h_boxes.to(device, non_blocking=True)
-            d_labels = h_labels.to(device, non_blocking=True)
-            d_tboxes = h_tboxes.to(device, non_blocking=True)
-            outs = [{"pred_logits": d_logits[l], "pred_boxes": d_boxes[l]} for l in range(wl.layers)]
-            tg = [{"labels": lb, "boxes": bx} for lb, bx in zip(torch.split(d_labels, sizes),
-                                                               torch.split(d_tboxes, sizes))]
-            ex: dict = {}
-            matcher.match_layers(outs, tg, wl.group_detr, weights=wl.weights, extras=ex)
-            h_pairs.copy_(ex["pairs"], non_blocking=True)
+            tg = matcher.PackedTargets(h_labels.to(device, non_blocking=True),
+                                       h_tboxes.to(device, non_blocking=True), sizes)
+            res = matcher.match_packed(d_logits, d_boxes, tg, wl.group_detr, weights=wl.weights)
+            h_pairs.copy_(res.pairs, non_blocking=True)
 
         for _ in range(max(args.warmup, 1)):
             e2e_step()
@@ -363,7 +362,7 @@ def run_rfm(args) -> None:
 
     # ---- roofline of the cost kernel (HBM-bound) and the solver figures
     peak, peak_kind = peak_hbm()
-    cb = cost_bytes(wl, ld)
+    cb = cost_bytes(wl)
     cost_avg_s = statistics.mean(cost_ms) / 1e3 if cost_ms else float("nan")
     achieved = cb / cost_avg_s / 1e9
     traffic = traffic_per_launch()
@@ -376,8 +375,8 @@ def run_rfm(args) -> None:
     lsap = {"kernel": "rfm lsap_kernel", "avg_launch_us": lsap_avg_s * 1e6,
             "problems_per_s": problems / lsap_avg_s, "algorithmic_bytes_per_launch": lb,
             "achieved_gbs": lb / lsap_avg_s / 1e9, "share_of_step": (sum(lsap_ms) / total_ms) if total_ms else None,
-            "cols_per_lane": plan.plan.cols_per_lane, "tile_floats": plan.plan.tile_floats,
-            "workspace_bytes": int(plan.plan.workspace_bytes)}
+            "cols_per_lane": plan.plan.cols_per_lane, "ctas": plan.plan.num_ctas,
+            "cta_smem_bytes": plan.plan.cta_smem_bytes, "workspace_bytes": int(plan.plan.workspace_bytes)}
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:

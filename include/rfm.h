@@ -83,15 +83,24 @@ typedef struct rfm_problem {
 
 /*
  * Launch plan for one batch of problems, computed on the host from the
- * problem sizes (which the caller knows without reading the device).
+ * problem sizes (which the caller knows without reading the device) by
+ * rfm_lsap_make_plan.  Treat it as opaque.
  */
 typedef struct rfm_lsap_plan {
   int32_t cols_per_lane;    /* kernel instantiation: max(rows, cols) <= 32 * cols_per_lane */
-  int32_t tile_floats;      /* on-chip cost tile per CTA, in floats */
   int32_t max_rows;         /* largest min(num_queries, num_targets) in the batch */
   int32_t num_problems;
+  int32_t num_ctas;         /* entries of the CTA table */
+  int32_t cta_smem_bytes;   /* dynamic shared memory of one CTA */
+  int32_t tile_cap_floats;  /* largest cost tile staged on chip */
+  int64_t stride_q;         /* cost element (q, t) at cost_offset + q*stride_q + t*stride_t */
+  int64_t stride_t;
   int64_t workspace_bytes;  /* device scratch rfm_lsap needs for this batch */
 } rfm_lsap_plan;
+
+/* Layouts rfm_cost can write. */
+#define RFM_LAYOUT_QUERY_MAJOR 0  /* out[l][q][ld]: the compact [Q, sum T] matrix of patches.py:149 */
+#define RFM_LAYOUT_TARGET_MAJOR 1 /* out[l][col][ld]: its transpose, row = target, ld >= Q */
 
 /* Library identification string (static storage). */
 const char* rfm_version(void);
@@ -119,9 +128,14 @@ const char* rfm_error_string(int code);
  *                (kernels_matcher.py:133-134)
  *   tgt_boxes    [S, 4] float32 cxcywh, 16-byte aligned
  *   tgt_offsets  [B + 1] int32, off[0] = 0, off[B] = S = sum_targets
- *   out          [L, Q, ld] float32, ld >= S; columns S .. ld-1 are written
- *                with 0.  ld % 4 == 0 with a 16-byte aligned `out` selects
- *                128-bit stores (the fast path); any other ld is accepted.
+ *   layout       RFM_LAYOUT_QUERY_MAJOR: out [L, Q, ld], ld >= S, the compact
+ *                matrix itself; RFM_LAYOUT_TARGET_MAJOR: out [L, S, ld],
+ *                ld >= Q, ld % 4 == 0, its transpose (each target's row holds
+ *                its image's Q queries), the layout the solver reads fastest.
+ *   out          float32, 16-byte aligned for the target-major layout.  Pad
+ *                columns (S .. ld-1, resp. Q .. ld-1) are written with 0.
+ *                Query-major with ld % 4 == 0 and a 16-byte aligned `out`
+ *                uses 128-bit stores; any other ld is accepted.
  *
  * Focal cost with gamma 2 (kernels_matcher.py:49-50, 257-260):
  *   p = sigmoid(x)
@@ -130,15 +144,24 @@ const char* rfm_error_string(int code);
  */
 int rfm_cost(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
              const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
-             int num_queries, int num_classes, int sum_targets, int64_t ld, float cost_class,
-             float cost_bbox, float cost_giou, float focal_alpha, float* out, void* stream);
+             int num_queries, int num_classes, int sum_targets, int64_t ld, int layout,
+             float cost_class, float cost_bbox, float cost_giou, float focal_alpha, float* out,
+             void* stream);
 
 /*
- * Host-side planning for rfm_lsap.  Reads the sizes of host_problems[0..n),
- * writes each problem's scratch_offset (floats into the workspace, or -1)
- * and fills *plan.  Pure host code: no CUDA call.
+ * Host-side planning for rfm_lsap.  Reads the sizes of host_problems[0..n)
+ * and the cost strides (element (q, t) of a problem at
+ * cost_offset + q*stride_q + t*stride_t), writes each problem's
+ * scratch_offset (floats into the workspace, or -1), fills the CTA table
+ * host_ctas (4 int32 per CTA, room for num_problems entries; plan->num_ctas
+ * are used) and *plan.  Problems are packed into CTAs in the order given, so
+ * callers sort them by decreasing num_queries * num_targets for balance.
+ * tile_cap_floats bounds the cost tile a problem may stage on chip (-1: the
+ * library default, 0: never stage).  Pure host code: no CUDA call.
  */
-int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, rfm_lsap_plan* plan);
+int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, int64_t stride_q,
+                       int64_t stride_t, int64_t tile_cap_floats, int32_t* host_ctas,
+                       rfm_lsap_plan* plan);
 
 /*
  * Batched exact rectangular assignment with SciPy's semantics
@@ -148,8 +171,10 @@ int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, rfm_lsap_pl
  * the float32 costs, and ties between equal path costs are broken exactly as
  * SciPy's sequential scan breaks them.
  *
- *   cost        float32 matrix addressed by each problem's cost_offset and ld
+ *   cost        float32 matrix addressed by each problem's cost_offset and the
+ *               plan's strides
  *   problems    [num_problems] DEVICE copy of the planned rfm_problem array
+ *   ctas        [plan->num_ctas * 4] DEVICE copy of the planned CTA table
  *   plan        host pointer to the plan rfm_lsap_make_plan returned
  *   query_out,
  *   target_out  int64 outputs addressed by out_offset
@@ -159,7 +184,7 @@ int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, rfm_lsap_pl
  * Problems whose smaller side is 0 write nothing.  When a problem's status
  * is not RFM_STATUS_OK its output slots are filled with -1.
  */
-int rfm_lsap(const float* cost, int64_t ld, const rfm_problem* problems,
+int rfm_lsap(const float* cost, const rfm_problem* problems, const int32_t* ctas,
              const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out, int32_t* status,
              void* workspace, void* stream);
 

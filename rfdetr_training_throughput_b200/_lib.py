@@ -54,14 +54,22 @@ PROBLEM_DTYPE = np.dtype(
 assert PROBLEM_DTYPE.itemsize == 40
 
 
+LAYOUT_QUERY_MAJOR = 0
+LAYOUT_TARGET_MAJOR = 1
+
+
 class LsapPlan(ctypes.Structure):
     """Mirror of ``struct rfm_lsap_plan``."""
 
     _fields_ = [
         ("cols_per_lane", ctypes.c_int32),
-        ("tile_floats", ctypes.c_int32),
         ("max_rows", ctypes.c_int32),
         ("num_problems", ctypes.c_int32),
+        ("num_ctas", ctypes.c_int32),
+        ("cta_smem_bytes", ctypes.c_int32),
+        ("tile_cap_floats", ctypes.c_int32),
+        ("stride_q", ctypes.c_int64),
+        ("stride_t", ctypes.c_int64),
         ("workspace_bytes", ctypes.c_int64),
     ]
 
@@ -101,12 +109,12 @@ def load() -> ctypes.CDLL:
     lib.rfm_error_string.restype = ctypes.c_char_p
     lib.rfm_error_string.argtypes = [_i32]
     lib.rfm_cost.restype = _i32
-    lib.rfm_cost.argtypes = [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i64,
+    lib.rfm_cost.argtypes = [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i64, _i32,
                              _f32, _f32, _f32, _f32, _p, _p]
     lib.rfm_lsap_make_plan.restype = _i32
-    lib.rfm_lsap_make_plan.argtypes = [_p, _i32, ctypes.POINTER(LsapPlan)]
+    lib.rfm_lsap_make_plan.argtypes = [_p, _i32, _i64, _i64, _i64, _p, ctypes.POINTER(LsapPlan)]
     lib.rfm_lsap.restype = _i32
-    lib.rfm_lsap.argtypes = [_p, _i64, _p, ctypes.POINTER(LsapPlan), _p, _p, _p, _p, _p]
+    lib.rfm_lsap.argtypes = [_p, _p, _p, ctypes.POINTER(LsapPlan), _p, _p, _p, _p, _p]
     lib.rfm_lsap_dense_workspace_bytes.restype = _i64
     lib.rfm_lsap_dense_workspace_bytes.argtypes = [_i32, _i32, _i32]
     lib.rfm_lsap_dense.restype = _i32
@@ -128,12 +136,24 @@ def check(func: str, code: int) -> None:
         raise RfmError(func, code)
 
 
-def make_plan(problems: np.ndarray) -> LsapPlan:
-    """Run the host-side planner over a ``PROBLEM_DTYPE`` array (fills scratch offsets in place)."""
+def default_tile_cap() -> int:
+    """On-chip tile cap for the solver (floats); ``RFM_LSAP_TILE_CAP`` overrides the library default."""
+    return int(os.environ.get("RFM_LSAP_TILE_CAP", "-1"))
+
+
+def make_plan(problems: np.ndarray, stride_q: int, stride_t: int,
+              tile_cap: int | None = None) -> tuple[LsapPlan, np.ndarray]:
+    """Run the host-side planner over a ``PROBLEM_DTYPE`` array.
+
+    Fills the problems' scratch offsets in place; returns the plan and the CTA
+    table (int32 ``[num_ctas, 4]``) to upload next to the problems.
+    """
     if problems.dtype != PROBLEM_DTYPE or not problems.flags.c_contiguous:
         raise ValueError("problems must be a contiguous PROBLEM_DTYPE array")
     plan = LsapPlan()
+    ctas = np.zeros((max(problems.shape[0], 1), 4), dtype=np.int32)
+    cap = default_tile_cap() if tile_cap is None else int(tile_cap)
     check("rfm_lsap_make_plan",
           load().rfm_lsap_make_plan(problems.ctypes.data if problems.size else None, problems.shape[0],
-                                    ctypes.byref(plan)))
-    return plan
+                                    int(stride_q), int(stride_t), cap, ctas.ctypes.data, ctypes.byref(plan)))
+    return plan, np.ascontiguousarray(ctas[: plan.num_ctas])

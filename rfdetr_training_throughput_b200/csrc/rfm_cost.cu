@@ -5,7 +5,16 @@
 // (patches.py:137-149): the compact [Q, sum T] matrix of every decoder layer is
 // written directly, so there is no padded intermediate and no copy.
 //
-// Work mapping.  Each thread owns four consecutive columns of the output (one
+// Two output layouts.  TARGET-MAJOR (the transpose, out[l][col][q]) is the one
+// the fused matcher step uses: one CTA covers one image and a 512-query tile;
+// each thread owns four consecutive queries (one 16-byte vector of every output
+// row), loads their boxes and logits once, evaluates the focal cost once per
+// class when there are at most four classes, and then walks the image's
+// targets (staged in shared memory, read as broadcasts), so every store is a
+// fully coalesced 128-bit write along the row and every input is read once.
+//
+// QUERY-MAJOR (the compact matrix itself, out[l][q][col]) serves the drop-in
+// cost-matrix call.  Each thread owns four consecutive columns of the output (one
 // 16-byte vector) and walks a strip of rows.  The target data of its columns
 // (box, xyxy corners, area, clamped label, owning image) is loaded once into
 // registers and reused for every row; the per-(image, query) prediction data
@@ -15,10 +24,12 @@
 // row then starts 16-byte aligned; the caller pads ld and the pad columns are
 // written with 0); any other ld takes a scalar-store variant.
 //
-// Arithmetic.  The box terms use explicitly rounded float32 intrinsics in the
-// reference chain's order of operations (no FMA contraction), so they are
-// bit-identical to a float32 evaluation of kernels_matcher.py:98-127 and :264;
-// the focal term uses CUDA's expf/log1pf.
+// Arithmetic.  Every add, subtract and multiply of the box terms is an explicitly
+// rounded float32 operation (scalar, or the packed f32x2 pair with the same
+// per-lane rounding) in the reference chain's order (kernels_matcher.py:98-127);
+// the two GIoU quotients are a * rcp(b), the focal term uses fast exp/log, and
+// the weighted sum is two explicit FMAs (all well inside the 1e-5 relative bar).
+// Both layouts evaluate the same operations and produce bit-identical matrices.
 #include "rfm_common.cuh"
 
 namespace rfm {
@@ -59,22 +70,40 @@ __device__ __forceinline__ Corners corners(const float4 b) {
   return c;
 }
 
+// a / b as a * rcp(b): PTX rcp.approx (max error about 1 ulp) and one rounded
+// multiply.  b is never below the 1e-7 clamp, so flushing subnormals is moot.
+__device__ __forceinline__ float quot(float a, float b) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(b));
+  return __fmul_rn(a, r);
+}
+
 // alpha (1-p)^2 (-logsigmoid(x)) - (1-alpha) p^2 (-logsigmoid(-x)), p = sigmoid(x)
-// (kernels_matcher.py:257-260; logsigmoid(x) = min(x, 0) - log1p(exp(-|x|))).
+// (kernels_matcher.py:257-260), with logsigmoid(x) = min(x, 0) - log1p(exp(-|x|)).
+// Fast exponent and logarithm: e = exp(-|x|), log1p(e) = log(1 + e),
+// sigmoid(x) = (x >= 0 ? 1 : e) / (1 + e); within ~1e-6 of the exact chain.  Every
+// rounding step is explicit so all call sites produce identical bits.
 __device__ __forceinline__ float focal_cost(float x, float alpha, float one_minus_alpha) {
-  const float p = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
-  const float l = log1pf(expf(-fabsf(x)));
+  const float e = __expf(-fabsf(x));
+  const float onep = __fadd_rn(1.0f, e);
+  const float l = __logf(onep);
+  const float p = quot(x >= 0.0f ? 1.0f : e, onep);
+  const float q = __fsub_rn(1.0f, p);
   const float ls_pos = __fsub_rn(fminf(x, 0.0f), l);
   const float ls_neg = __fsub_rn(fminf(-x, 0.0f), l);
-  const float q = __fsub_rn(1.0f, p);
   const float neg = __fmul_rn(__fmul_rn(one_minus_alpha, __fmul_rn(p, p)), -ls_neg);
   const float pos = __fmul_rn(__fmul_rn(alpha, __fmul_rn(q, q)), -ls_pos);
   return __fsub_rn(pos, neg);
 }
 
+// cost_bbox * l1 + w_class_cost + cost_giou * (-giou), evaluated as
+// fma(-cost_giou, giou, fma(cost_bbox, l1, w_class_cost)) in every kernel.
+__device__ __forceinline__ float combine(float l1, float giou, float wcls, const CostArgs& a) {
+  return __fmaf_rn(-a.w_giou, giou, __fmaf_rn(a.w_bbox, l1, wcls));
+}
+
 __device__ __forceinline__ float pair_cost(const float4 pb, const Corners& pc, const float4 tb,
-                                           const Corners& tc, float class_cost,
-                                           const CostArgs& a) {
+                                           const Corners& tc, float wcls, const CostArgs& a) {
   // torch.cdist(p=1) over the four cxcywh coordinates (kernels_matcher.py:98-103)
   const float l1 = __fadd_rn(
       __fadd_rn(__fadd_rn(fabsf(__fsub_rn(pb.x, tb.x)), fabsf(__fsub_rn(pb.y, tb.y))),
@@ -85,14 +114,12 @@ __device__ __forceinline__ float pair_cost(const float4 pb, const Corners& pc, c
   const float ih = __fsub_rn(fminf(pc.y1, tc.y1), fmaxf(pc.y0, tc.y0));
   const float inter = __fmul_rn(fmaxf(iw, 0.0f), fmaxf(ih, 0.0f));
   const float uni = __fsub_rn(__fadd_rn(pc.area, tc.area), inter);
-  const float iou = __fdiv_rn(inter, fmaxf(uni, kBoxEps));
+  const float iou = quot(inter, fmaxf(uni, kBoxEps));
   const float ew = __fsub_rn(fmaxf(pc.x1, tc.x1), fminf(pc.x0, tc.x0));
   const float eh = __fsub_rn(fmaxf(pc.y1, tc.y1), fminf(pc.y0, tc.y0));
   const float hull = __fmul_rn(fmaxf(ew, 0.0f), fmaxf(eh, 0.0f));
-  const float giou = __fsub_rn(iou, __fdiv_rn(__fsub_rn(hull, uni), fmaxf(hull, kBoxEps)));
-  // cost_bbox * l1 + cost_class * class + cost_giou * (-giou)  (kernels_matcher.py:264)
-  return __fadd_rn(__fadd_rn(__fmul_rn(a.w_bbox, l1), __fmul_rn(a.w_class, class_cost)),
-                   __fmul_rn(a.w_giou, -giou));
+  const float giou = __fsub_rn(iou, quot(__fsub_rn(hull, uni), fmaxf(hull, kBoxEps)));
+  return combine(l1, giou, wcls, a);
 }
 
 // Largest image b with offsets[b] <= col (images with no targets are skipped).
@@ -110,7 +137,7 @@ __device__ __forceinline__ int image_of(const int32_t* offsets, int B, int col) 
 }
 
 template <bool kVec>
-__global__ void __launch_bounds__(kThreads) cost_kernel(const CostArgs a) {
+__global__ void __launch_bounds__(kThreads) cost_qmajor_kernel(const CostArgs a) {
   const int64_t col0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   if (col0 >= a.ld) return;
   const int layer = blockIdx.z;
@@ -149,8 +176,8 @@ __global__ void __launch_bounds__(kThreads) cost_kernel(const CostArgs a) {
         const int64_t pq = (layer_base + image[c]) * a.Q + q;
         const float4 pb = __ldg(a.pboxes + pq);
         const float x = __ldg(a.logits + pq * a.C + label[c]);
-        r[c] = pair_cost(pb, corners(pb), tb[c], tc[c], focal_cost(x, a.alpha, a.one_minus_alpha),
-                         a);
+        r[c] = pair_cost(pb, corners(pb), tb[c], tc[c],
+                         __fmul_rn(a.w_class, focal_cost(x, a.alpha, a.one_minus_alpha)), a);
       }
     }
     float* dst = a.out + (static_cast<int64_t>(layer) * a.Q + q) * a.ld + col0;
@@ -165,21 +192,274 @@ __global__ void __launch_bounds__(kThreads) cost_kernel(const CostArgs a) {
   }
 }
 
+
+constexpr int kTmThreads = 128;  // 4 queries each: 512 queries per CTA
+constexpr int kTmCols = 32;      // target rows per CTA (may span several images)
+constexpr int kSmallClasses = 4;
+
+// Packed float32 pairs: two queries per instruction (sm_100 f32x2 pipe), each
+// half rounded exactly as the scalar instruction would round it.
+__device__ __forceinline__ unsigned long long pk(float2 a) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a.x), "f"(a.y));
+  return r;
+}
+__device__ __forceinline__ float2 upk(unsigned long long r) {
+  float2 a;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a.x), "=f"(a.y) : "l"(r));
+  return a;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)));
+  return upk(r);
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)));
+  return upk(r);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)));
+  return upk(r);
+}
+__device__ __forceinline__ float2 dup2(float x) { return make_float2(x, x); }
+
+// Shared per-target data (48 bytes; read as broadcasts).
+struct TargetRow {
+  float4 box;  // cx, cy, w, h
+  float4 xy;   // x0, y0, x1, y1
+  float area;
+  int label;
+  int image;
+  int plain;   // w >= 0, h >= 0 and area >= 2e-7: the clamps are no-ops
+};
+
+// Prediction data of one pair of queries of one image.
+struct PredPair {
+  float2 cx, cy, w, h, x0, y0, x1, y1, area;
+};
+
+__device__ __forceinline__ PredPair pred_pair(const float4 a, const float4 b) {
+  PredPair p;
+  p.cx = make_float2(a.x, b.x);
+  p.cy = make_float2(a.y, b.y);
+  p.w = make_float2(a.z, b.z);
+  p.h = make_float2(a.w, b.w);
+  const float2 hw = mul2(dup2(0.5f), p.w);
+  const float2 hh = mul2(dup2(0.5f), p.h);
+  p.x0 = sub2(p.cx, hw);
+  p.y0 = sub2(p.cy, hh);
+  p.x1 = add2(p.cx, hw);
+  p.y1 = add2(p.cy, hh);
+  p.area = mul2(sub2(p.x1, p.x0), sub2(p.y1, p.y0));
+  return p;
+}
+
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk(a)), "l"(pk(b)), "l"(pk(c)));
+  return upk(r);
+}
+
+// Cost of one target against a pair of queries (two packed lanes).  With
+// kUnclamped the hull and 1e-7 clamps are skipped: the caller guarantees they
+// are no-ops (both boxes have non-negative width and height, so the hull
+// extents are >= 0, and the target's area is >= 2e-7, so union and hull exceed
+// 1e-7), which leaves every result bit-identical to the clamped formula.
+template <bool kUnclamped>
+__device__ __forceinline__ float2 pair_cost2(const PredPair& p, const TargetRow& t, float2 wcls,
+                                             const CostArgs& a) {
+  const float2 dcx = sub2(p.cx, dup2(t.box.x));
+  const float2 dcy = sub2(p.cy, dup2(t.box.y));
+  const float2 dw = sub2(p.w, dup2(t.box.z));
+  const float2 dh = sub2(p.h, dup2(t.box.w));
+  const float2 l1 = make_float2(((fabsf(dcx.x) + fabsf(dcy.x)) + fabsf(dw.x)) + fabsf(dh.x),
+                                ((fabsf(dcx.y) + fabsf(dcy.y)) + fabsf(dw.y)) + fabsf(dh.y));
+  const float2 iw = sub2(make_float2(fminf(p.x1.x, t.xy.z), fminf(p.x1.y, t.xy.z)),
+                         make_float2(fmaxf(p.x0.x, t.xy.x), fmaxf(p.x0.y, t.xy.x)));
+  const float2 ih = sub2(make_float2(fminf(p.y1.x, t.xy.w), fminf(p.y1.y, t.xy.w)),
+                         make_float2(fmaxf(p.y0.x, t.xy.y), fmaxf(p.y0.y, t.xy.y)));
+  const float2 inter = mul2(make_float2(fmaxf(iw.x, 0.f), fmaxf(iw.y, 0.f)),
+                            make_float2(fmaxf(ih.x, 0.f), fmaxf(ih.y, 0.f)));
+  const float2 uni = sub2(add2(p.area, dup2(t.area)), inter);
+  const float2 ew = sub2(make_float2(fmaxf(p.x1.x, t.xy.z), fmaxf(p.x1.y, t.xy.z)),
+                         make_float2(fminf(p.x0.x, t.xy.x), fminf(p.x0.y, t.xy.x)));
+  const float2 eh = sub2(make_float2(fmaxf(p.y1.x, t.xy.w), fmaxf(p.y1.y, t.xy.w)),
+                         make_float2(fminf(p.y0.x, t.xy.y), fminf(p.y0.y, t.xy.y)));
+  float2 hull, uc, hc;
+  if (kUnclamped) {
+    hull = mul2(ew, eh);
+    uc = uni;
+    hc = hull;
+  } else {
+    hull = mul2(make_float2(fmaxf(ew.x, 0.f), fmaxf(ew.y, 0.f)),
+                make_float2(fmaxf(eh.x, 0.f), fmaxf(eh.y, 0.f)));
+    uc = make_float2(fmaxf(uni.x, kBoxEps), fmaxf(uni.y, kBoxEps));
+    hc = make_float2(fmaxf(hull.x, kBoxEps), fmaxf(hull.y, kBoxEps));
+  }
+  const float2 iou = make_float2(quot(inter.x, uc.x), quot(inter.y, uc.y));
+  const float2 gap = sub2(hull, uni);
+  const float2 giou = sub2(iou, make_float2(quot(gap.x, hc.x), quot(gap.y, hc.y)));
+  return fma2(dup2(-a.w_giou), giou, fma2(dup2(a.w_bbox), l1, wcls));
+}
+
+// Loads of the next image's predictions, issued before they are needed.
+template <int NCLS>
+struct PredRaw {
+  float4 box[4];
+  float lg[4][NCLS > 0 ? NCLS : 1];
+};
+
+template <int NCLS>
+__device__ __forceinline__ void load_raw(PredRaw<NCLS>& r, const CostArgs& a, int64_t pbase, int q0) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int q = q0 + k < a.Q ? q0 + k : a.Q - 1;  // pad queries reuse a valid row
+    r.box[k] = __ldg(a.pboxes + pbase + q);
+    if (NCLS > 0) {
+#pragma unroll
+      for (int c = 0; c < NCLS; ++c) r.lg[k][c] = __ldg(a.logits + (pbase + q) * NCLS + c);
+    }
+  }
+}
+
+template <int NCLS>
+__global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs a) {
+  __shared__ TargetRow s_t[kTmCols];
+  __shared__ int s_seg[kTmCols + 1];
+  __shared__ int s_nseg;
+  const int layer = blockIdx.z;
+  const int c_begin = blockIdx.x * kTmCols;
+  const int n = min(kTmCols, a.S - c_begin);
+  const int tid = threadIdx.x;
+
+  // stage this CTA's targets and split them into runs of one image
+  if (tid < 32) {
+    int img = -1;
+    if (tid < n) {
+      const int col = c_begin + tid;
+      img = image_of(a.offsets, a.B, col);
+      TargetRow t;
+      t.box = __ldg(a.tboxes + col);
+      const Corners c = corners(t.box);
+      t.xy = make_float4(c.x0, c.y0, c.x1, c.y1);
+      t.area = c.area;
+      const int64_t raw = __ldg(a.labels + col);
+      t.label = static_cast<int>(raw < 0 ? 0 : (raw >= a.C ? a.C - 1 : raw));
+      t.image = img;
+      t.plain = (t.box.z >= 0.0f && t.box.w >= 0.0f && c.area >= 2e-7f) ? 1 : 0;
+      s_t[tid] = t;
+    }
+    const int prev = __shfl_up_sync(kFullMask, img, 1);
+    const bool start = tid < n && (tid == 0 || prev != img);
+    const unsigned starts = __ballot_sync(kFullMask, start);
+    if (start) s_seg[__popc(starts & ((1u << tid) - 1u))] = tid;
+    if (tid == 0) {
+      s_nseg = __popc(starts);
+      s_seg[__popc(starts)] = n;
+    }
+  }
+  __syncthreads();
+  const int q0 = (blockIdx.y * kTmThreads + tid) * 4;
+  if (q0 >= a.ld) return;
+  const int nseg = s_nseg;
+  const int64_t layer_base = static_cast<int64_t>(layer) * a.B;
+
+  PredRaw<NCLS> raw;
+  load_raw<NCLS>(raw, a, (layer_base + s_t[0].image) * a.Q, q0);
+  float* out_row = a.out + (static_cast<int64_t>(layer) * a.S + c_begin) * a.ld + q0;
+  for (int sg = 0; sg < nseg; ++sg) {
+    const int img = s_t[s_seg[sg]].image;
+    const int64_t pbase = (layer_base + img) * a.Q;
+    const PredPair p01 = pred_pair(raw.box[0], raw.box[1]);
+    const PredPair p23 = pred_pair(raw.box[2], raw.box[3]);
+    bool preds_plain = true;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) preds_plain = preds_plain && raw.box[k].z >= 0.0f && raw.box[k].w >= 0.0f;
+    float2 wcls01[kSmallClasses], wcls23[kSmallClasses];
+    if (NCLS > 0) {
+#pragma unroll
+      for (int c = 0; c < NCLS; ++c) {
+        float f[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          f[k] = __fmul_rn(a.w_class, focal_cost(raw.lg[k][c], a.alpha, a.one_minus_alpha));
+        }
+        wcls01[c] = make_float2(f[0], f[1]);
+        wcls23[c] = make_float2(f[2], f[3]);
+      }
+    }
+    if (sg + 1 < nseg) {
+      load_raw<NCLS>(raw, a, (layer_base + s_t[s_seg[sg + 1]].image) * a.Q, q0);
+    }
+    const int c_end = s_seg[sg + 1];
+    for (int c = s_seg[sg]; c < c_end; ++c) {
+      const TargetRow t = s_t[c];
+      float2 w01, w23;
+      if (NCLS > 0) {
+        w01 = wcls01[0];
+        w23 = wcls23[0];
+#pragma unroll
+        for (int cl = 1; cl < NCLS; ++cl) {
+          w01 = t.label == cl ? wcls01[cl] : w01;
+          w23 = t.label == cl ? wcls23[cl] : w23;
+        }
+      } else {
+        float f[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int q = q0 + k < a.Q ? q0 + k : a.Q - 1;
+          f[k] = __fmul_rn(a.w_class, focal_cost(__ldg(a.logits + (pbase + q) * a.C + t.label),
+                                                 a.alpha, a.one_minus_alpha));
+        }
+        w01 = make_float2(f[0], f[1]);
+        w23 = make_float2(f[2], f[3]);
+      }
+      float2 r01, r23;
+      if (preds_plain && t.plain) {
+        r01 = pair_cost2<true>(p01, t, w01, a);
+        r23 = pair_cost2<true>(p23, t, w23, a);
+      } else {
+        r01 = pair_cost2<false>(p01, t, w01, a);
+        r23 = pair_cost2<false>(p23, t, w23, a);
+      }
+      if (q0 + 4 > a.Q) {  // zero the pad queries of the last tile
+        if (q0 + 1 >= a.Q) r01.y = 0.f;
+        if (q0 + 2 >= a.Q) r23.x = 0.f;
+        if (q0 + 3 >= a.Q) r23.y = 0.f;
+      }
+      *reinterpret_cast<float4*>(out_row + static_cast<int64_t>(c) * a.ld) =
+          make_float4(r01.x, r01.y, r23.x, r23.y);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace rfm
 
 extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
                         const int64_t* tgt_labels, const float* tgt_boxes,
                         const int32_t* tgt_offsets, int num_layers, int num_images,
-                        int num_queries, int num_classes, int sum_targets, int64_t ld,
+                        int num_queries, int num_classes, int sum_targets, int64_t ld, int layout,
                         float cost_class, float cost_bbox, float cost_giou, float focal_alpha,
                         float* out, void* stream) {
   using namespace rfm;
   if (num_layers < 1 || num_layers > 65535 || num_images < 1 || num_queries < 1 ||
-      num_classes < 1 || sum_targets < 0 || ld < sum_targets) {
+      num_classes < 1 || sum_targets < 0) {
     return RFM_ERR_INVALID_ARGUMENT;
   }
-  if (ld == 0) return RFM_OK;
+  if (layout == RFM_LAYOUT_QUERY_MAJOR) {
+    if (ld < sum_targets) return RFM_ERR_INVALID_ARGUMENT;
+    if (ld == 0) return RFM_OK;
+  } else if (layout == RFM_LAYOUT_TARGET_MAJOR) {
+    if (ld < num_queries || (ld & 3) != 0) return RFM_ERR_INVALID_ARGUMENT;
+    if (sum_targets == 0) return RFM_OK;
+    if (out != nullptr && !aligned16(out)) return RFM_ERR_INVALID_ARGUMENT;
+  } else {
+    return RFM_ERR_INVALID_ARGUMENT;
+  }
   if (out == nullptr) return RFM_ERR_INVALID_ARGUMENT;
   if (sum_targets > 0 &&
       (pred_logits == nullptr || pred_boxes == nullptr || tgt_labels == nullptr ||
@@ -210,6 +490,22 @@ extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
   a.one_minus_alpha = static_cast<float>(1.0 - static_cast<double>(focal_alpha));
   a.out = out;
 
+  if (layout == RFM_LAYOUT_TARGET_MAJOR) {
+    const int64_t gy = (ld / 4 + kTmThreads - 1) / kTmThreads;
+    const int64_t gx = (static_cast<int64_t>(sum_targets) + kTmCols - 1) / kTmCols;
+    if (gy > 65535 || gx > 0x7fffffff) return RFM_ERR_UNSUPPORTED;
+    const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy),
+                    static_cast<unsigned>(num_layers));
+    switch (num_classes) {
+      case 1: cost_tmajor_kernel<1><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
+      case 2: cost_tmajor_kernel<2><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
+      case 3: cost_tmajor_kernel<3><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
+      case 4: cost_tmajor_kernel<4><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
+      default: cost_tmajor_kernel<0><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
+    }
+    return launch_status();
+  }
+
   const int64_t chunks = (ld + 3) / 4;
   int tx = 1;
   while (tx < chunks && tx < 64) tx <<= 1;
@@ -222,9 +518,9 @@ extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
                   static_cast<unsigned>(num_layers));
   const dim3 block(tx, ty, 1);
   if ((ld & 3) == 0 && aligned16(out)) {
-    cost_kernel<true><<<grid, block, 0, as_stream(stream)>>>(a);
+    cost_qmajor_kernel<true><<<grid, block, 0, as_stream(stream)>>>(a);
   } else {
-    cost_kernel<false><<<grid, block, 0, as_stream(stream)>>>(a);
+    cost_qmajor_kernel<false><<<grid, block, 0, as_stream(stream)>>>(a);
   }
   return launch_status();
 }

@@ -1,5 +1,5 @@
-// Batched exact rectangular linear assignment, SciPy semantics, one CTA (one
-// warp) per problem.
+// Batched exact rectangular linear assignment with SciPy's semantics; one warp
+// solves one problem (a CTA holds one to four such warps).
 //
 // Replaces lsap_kernel / batch_lap_cuda (kernels_lap.py:88-305) and the device
 // unpack of the device_indices patch (patches.py:379-418).
@@ -16,29 +16,35 @@
 //     a strictly smaller path cost, or an equal one whose column is free.  Over
 //     a whole scan that selects, among the columns at the minimum, the LAST
 //     free one in scan order if any is free, else the FIRST one.  The warp
-//     reproduces it as an argmin over the key (cost, free ? -(pos+1) : pos),
-//     where pos is the column's position in `remaining`, which is maintained
-//     with SciPy's reverse fill and swap-with-last removal.
+//     reproduces it as a lexicographic argmin over (cost, key) with
+//     key = free ? B-1-pos : B+pos, where pos is the column's position in
+//     `remaining`, maintained with SciPy's reverse fill and swap-with-last
+//     removal.
 //
-// Layout.  Lane l owns columns l, l+32, ..., l+32(K-1).  Its columns' duals
-// v, path costs, positions in `remaining`, "still remaining" and "free" bits
-// live in registers, so the scan is register work plus one cost load per
-// column; the argmin is a 5-step shuffle butterfly.  The row duals, the
-// matching and `remaining` (position -> column) live in shared memory.  The
-// dual update needs no cross-lane traffic: every visited non-sink column j
-// owns exactly one tree row, row4col[j], so its lane applies
+// Layout.  Lane l owns solver columns l, l+32, ..., l+32(K-1).  Its columns'
+// duals v, path costs, tie keys, "still remaining" and "free" bits live in
+// registers, so the scan is register work plus one cost load per column; the
+// warp argmin is three redux.sync minimum steps over an order-preserving
+// integer image of the float64 cost and the key.  Row duals (float64), the
+// matching, the path and `remaining` (position -> column) live in shared
+// memory as int16.  The dual update needs no cross-lane traffic: every visited
+// non-sink column j owns exactly one tree row, row4col[j], so its lane applies
 // u[row4col[j]] += minv - spc[j] and v[j] -= minv - spc[j] itself.
 //
-// Cost tile.  The problem's cost is staged once: into shared memory when it
-// fits the launch's tile budget (row stride num_targets|1 keeps both access
-// orientations bank-conflict free); otherwise a tall problem is transposed
-// into the caller's workspace so that each solver row is one coalesced read
-// from L2, and a wide or square one is read in place (its solver rows are the
-// matrix rows).
+// Cost source.  Element (q, t) of a problem is read at
+// cost[cost_offset + q * stride_q + t * stride_t], so the solver reads either
+// the query-major compact matrix or its target-major transpose in place.  The
+// problem is used in the solver's orientation (rows = targets when
+// transposed): staged into shared memory with cp.async when the tile is
+// within the cap (SHARED); otherwise read straight from L2/HBM when solver
+// rows are contiguous in the source (DIRECT), or first transposed into the
+// caller's workspace (SCRATCH).  The host packs problems, sorted by tile
+// size, into CTAs of up to four warps under a shared-memory budget, so small
+// problems share a CTA and the SM holds as many warps as registers allow.
 //
 // Termination: every inner step removes one column from `remaining`, so each
 // augmentation is bounded by num_cols steps (kernels_lap.py:78-84,147-148);
-// the path flip is bounded by num_rows + 1 steps.
+// the path flip is bounded by num_rows + 1 steps.  There are no spin-waits.
 #include <math_constants.h>
 
 #include <climits>
@@ -48,14 +54,29 @@
 namespace rfm {
 namespace {
 
-constexpr int kSmemLimitDefault = 227 * 1024;
+constexpr int kSmemPerSm = 228 * 1024;
+constexpr int kSmemPerCtaReserved = 1024;
+constexpr int kSmemPerBlockMax = 227 * 1024;
+constexpr int64_t kTileCapDefault = 16384;  // floats: 64 KB of staged cost per warp
+constexpr int kMaxWarpsPerCta = 4;
+// Shared-memory budget of one CTA: four CTAs of four warps fill an SM.
+constexpr int kCtaBudget = kSmemPerSm / 4 - kSmemPerCtaReserved;
+// Tie keys: a free column at position pos gets kKeyBase - 1 - pos, a matched one
+// kKeyBase + pos, so the smallest key is SciPy's pick among equal path costs.
+constexpr unsigned kKeyBase = 1024u;
+constexpr unsigned kNoKey = 0xffffffffu;
+
+enum Mode : int { kModeShared = 0, kModeDirect = 1, kModeScratch = 2 };
 
 struct LsapArgs {
   const float* cost;
-  int64_t ld;
+  int64_t stride_q, stride_t;
   const rfm_problem* problems;  // pair mode
-  int dense_w, dense_t;         // dense mode: uniform [P, W, T] problems
-  int tile_floats;
+  const int4* ctas;             // pair mode: {first problem, warps, slot bytes, 0} per CTA
+  int num_problems;
+  int dense_w, dense_t;  // dense mode: uniform [P, W, T] problems
+  int dense_warps, dense_slot;
+  int tile_cap;
   int max_rows;
   float* workspace;
   int64_t* q_out;  // pair mode: query indices; dense mode: matching [P, W]
@@ -63,141 +84,249 @@ struct LsapArgs {
   int32_t* status;
 };
 
-struct Problem {
-  int64_t cost_off, out_off, scratch_off;
-  int nq, nt, qbase;
+// The problem in the solver's orientation: nr rows, nc columns, and the
+// source strides of one row step (rs) and one column step (cs).
+struct Shape {
+  bool transposed;
+  int nr, nc;
+  int64_t rs, cs;
 };
 
-enum class Mode { kShared, kDirect, kScratch };
-
-__host__ __device__ inline int64_t tile_need(int nq, int nt) {
-  return static_cast<int64_t>(nq) * (nt | 1);
+__host__ __device__ inline Shape solver_shape(int nq, int nt, int64_t sq, int64_t st) {
+  Shape s;
+  s.transposed = nt < nq;
+  if (s.transposed) {
+    s.nr = nt;
+    s.nc = nq;
+    s.rs = st;
+    s.cs = sq;
+  } else {
+    s.nr = nq;
+    s.nc = nt;
+    s.rs = sq;
+    s.cs = st;
+  }
+  return s;
 }
 
-__host__ __device__ inline int64_t fixed_smem_bytes(int cols_cap, int max_rows) {
-  // u (double) + col4row (int) per row; row4col, path, remaining (int) per column
-  const int64_t b = static_cast<int64_t>(max_rows) * 12 + static_cast<int64_t>(cols_cap) * 12;
+// SHARED when the tile is within the cap and the warp's slot holds it.
+__host__ __device__ inline int choose_mode(const Shape& s, int64_t tile_cap, int64_t slot_floats) {
+  const int64_t t = static_cast<int64_t>(s.nr) * s.nc;
+  if (t <= tile_cap && t <= slot_floats) return kModeShared;
+  if (s.cs == 1) return kModeDirect;
+  return kModeScratch;
+}
+
+__host__ __device__ inline int64_t fixed_warp_bytes(int cols_cap, int max_rows) {
+  // u (float64) and col4row (int16) per row; row4col, path, remaining (int16) per column
+  const int64_t b = static_cast<int64_t>(max_rows) * 10 + static_cast<int64_t>(cols_cap) * 6;
   return (b + 15) & ~int64_t(15);
 }
 
+__host__ __device__ inline int64_t warp_bytes_for(int cols_cap, int max_rows, int64_t tile_floats) {
+  return fixed_warp_bytes(cols_cap, max_rows) + ((tile_floats * 4 + 15) & ~int64_t(15));
+}
+
+// Order-preserving map of a float64 (NaN excluded) onto uint64; -0 and +0 map
+// to the same value (x + 0.0 is +0.0 for either zero), as they compare equal.
+__device__ __forceinline__ unsigned long long ordered_bits(double x) {
+  const long long b = __double_as_longlong(x + 0.0);
+  return b >= 0 ? (static_cast<unsigned long long>(b) | 0x8000000000000000ull)
+                : ~static_cast<unsigned long long>(b);
+}
+
+__device__ __forceinline__ double from_ordered(unsigned long long o) {
+  const unsigned long long b = (o & 0x8000000000000000ull) ? (o & 0x7fffffffffffffffull) : ~o;
+  return __longlong_as_double(static_cast<long long>(b));
+}
+
+// Lexicographic (value, key) minimum over the warp with three redux.sync steps;
+// every lane receives the winner.
+__device__ __forceinline__ void warp_argmin(double& v, unsigned& key) {
+  const unsigned long long o = ordered_bits(v);
+  const unsigned hi = static_cast<unsigned>(o >> 32);
+  const unsigned lo = static_cast<unsigned>(o);
+  const unsigned mhi = __reduce_min_sync(kFullMask, hi);
+  const unsigned mlo = __reduce_min_sync(kFullMask, hi == mhi ? lo : 0xffffffffu);
+  key = __reduce_min_sync(kFullMask, (hi == mhi && lo == mlo) ? key : kNoKey);
+  v = from_ordered((static_cast<unsigned long long>(mhi) << 32) | mlo);
+}
+
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
+__device__ __forceinline__ bool invalid_cost(float x) { return (x != x) || (x == -CUDART_INF_F); }
+
 template <int K>
-__device__ __forceinline__ void set_pos(int (&pos)[K], int k_sel, int value) {
+__device__ __forceinline__ void set_key(unsigned (&key)[K], int k_sel, unsigned value) {
 #pragma unroll
   for (int k = 0; k < K; ++k) {
-    if (k == k_sel) pos[k] = value;
+    if (k == k_sel) key[k] = value;
   }
 }
 
+// Load policies of the scan: shared tile, read-only global, L2-only global.
+enum Load : int { kLoadShared = 0, kLoadGlobal = 1, kLoadScratch = 2 };
+
+template <int L>
+__device__ __forceinline__ float load_cost(const float* p) {
+  if (L == kLoadShared) return *p;
+  if (L == kLoadGlobal) return __ldg(p);
+  return __ldcg(p);
+}
+
 // One scan step of the augmenting-path search over the lane's columns.
-template <int K, bool kShared>
-__device__ __forceinline__ void scan_row(const float* row, int col_stride, int lane, int i,
-                                         double minv, double ui, const double (&v)[K],
-                                         double (&spc)[K], const int (&pos)[K], unsigned rem,
-                                         unsigned freem, int* path_s, double& bv, int& bk) {
+template <int K, int L>
+__device__ __forceinline__ void scan_row(const float* row, int lane, int i, double minv, double ui,
+                                         const double (&v)[K], double (&spc)[K],
+                                         const unsigned (&key)[K], unsigned rem, int16_t* path_s,
+                                         double& bv, unsigned& bk) {
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     if (rem & (1u << k)) {
       const int j = lane + 32 * k;
-      float cf;
-      if (kShared) {
-        cf = row[j * col_stride];
-      } else {
-        cf = __ldcg(row + static_cast<int64_t>(j) * col_stride);
-      }
+      const float cf = load_cost<L>(row + j);
       const double r = ((minv + static_cast<double>(cf)) - ui) - v[k];
       if (r < spc[k]) {
         spc[k] = r;
-        path_s[j] = i;
+        path_s[j] = static_cast<int16_t>(i);
       }
-      const int key = (freem & (1u << k)) ? -(pos[k] + 1) : pos[k];
-      if (spc[k] < bv || (spc[k] == bv && key < bk)) {
+      if (spc[k] < bv || (spc[k] == bv && key[k] < bk)) {
         bv = spc[k];
-        bk = key;
+        bk = key[k];
       }
     }
   }
 }
 
 template <int K, bool kDense>
-__global__ void __launch_bounds__(32) lsap_kernel(const LsapArgs a) {
+__global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int kCols = 32 * K;
-  const int lane = threadIdx.x;
-  const int p = blockIdx.x;
-
-  Problem pr;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int p, slot;
   if (kDense) {
-    pr.nq = a.dense_w;
-    pr.nt = a.dense_t;
-    pr.cost_off = static_cast<int64_t>(p) * a.dense_w * a.dense_t;
-    pr.out_off = static_cast<int64_t>(p) * a.dense_w;
-    pr.scratch_off = pr.cost_off;
-    pr.qbase = 0;
+    p = blockIdx.x * a.dense_warps + warp;
+    slot = a.dense_slot;
+    if (p >= a.num_problems) return;
+  } else {
+    const int4 cta = a.ctas[blockIdx.x];
+    if (warp >= cta.y) return;
+    p = cta.x + warp;
+    slot = cta.z;
+  }
+
+  int64_t cost_off, out_off, scratch_off;
+  int nq, nt, qbase;
+  if (kDense) {
+    nq = a.dense_w;
+    nt = a.dense_t;
+    cost_off = static_cast<int64_t>(p) * a.dense_w * a.dense_t;
+    out_off = static_cast<int64_t>(p) * a.dense_w;
+    scratch_off = cost_off;
+    qbase = 0;
   } else {
     const rfm_problem d = a.problems[p];
-    pr.cost_off = d.cost_offset;
-    pr.out_off = d.out_offset;
-    pr.scratch_off = d.scratch_offset;
-    pr.nq = d.num_queries;
-    pr.nt = d.num_targets;
-    pr.qbase = d.query_base;
+    cost_off = d.cost_offset;
+    out_off = d.out_offset;
+    scratch_off = d.scratch_offset;
+    nq = d.num_queries;
+    nt = d.num_targets;
+    qbase = d.query_base;
   }
-  const int64_t ld = kDense ? a.dense_t : a.ld;
-  const bool transposed = pr.nt < pr.nq;
-  const int nr = transposed ? pr.nt : pr.nq;
-  const int nc = transposed ? pr.nq : pr.nt;
-  int64_t* q_out = a.q_out + pr.out_off;
-  int64_t* t_out = kDense ? nullptr : a.t_out + pr.out_off;
+  const Shape s = solver_shape(nq, nt, a.stride_q, a.stride_t);
+  const int nr = s.nr;
+  const int nc = s.nc;
+  int64_t* q_out = a.q_out + out_off;
+  int64_t* t_out = kDense ? nullptr : a.t_out + out_off;
 
   if (nr == 0) {
     if (kDense) {
-      for (int w = lane; w < pr.nq; w += 32) q_out[w] = -1;
+      for (int w = lane; w < nq; w += 32) q_out[w] = -1;
     }
     if (a.status != nullptr && lane == 0) a.status[p] = RFM_STATUS_OK;
     return;
   }
 
-  double* u_s = reinterpret_cast<double*>(smem_raw);
-  int* col4row_s = reinterpret_cast<int*>(u_s + a.max_rows);
-  int* row4col_s = col4row_s + a.max_rows;
-  int* path_s = row4col_s + kCols;
-  int* rem_s = path_s + kCols;
-  float* tile = reinterpret_cast<float*>(smem_raw + fixed_smem_bytes(kCols, a.max_rows));
-
-  // ---- stage the cost and validate it (SciPy rejects NaN and -inf) --------
-  const float* src = a.cost + pr.cost_off;
-  const int tp = pr.nt | 1;
-  Mode mode;
+  unsigned char* base = smem_raw + static_cast<int64_t>(warp) * slot;
+  double* u_s = reinterpret_cast<double*>(base);
+  int16_t* col4row_s = reinterpret_cast<int16_t*>(u_s + a.max_rows);
+  int16_t* row4col_s = col4row_s + a.max_rows;
+  int16_t* path_s = row4col_s + kCols;
+  int16_t* rem_s = path_s + kCols;
+  // ---- stage / validate the cost (SciPy rejects NaN and -inf) -------------
+  const float* src = a.cost + cost_off;
+  const int64_t fixed = fixed_warp_bytes(kCols, a.max_rows);
+  float* tile = reinterpret_cast<float*>(base + fixed);
+  const int mode = choose_mode(s, a.tile_cap, (slot - fixed) / 4);
   bool bad = false;
-  float* scratch = nullptr;
-  if (tile_need(pr.nq, pr.nt) <= a.tile_floats) {
-    mode = Mode::kShared;
-    const int total = pr.nq * pr.nt;
-    for (int e = lane; e < total; e += 32) {
-      const int q = e / pr.nt;
-      const int t = e - q * pr.nt;
-      const float x = __ldg(src + q * ld + t);
-      bad |= (x != x) || (x == -CUDART_INF_F);
-      tile[q * tp + t] = x;
-    }
-  } else if (transposed) {
-    mode = Mode::kScratch;
-    scratch = a.workspace + pr.scratch_off;
-    for (int t = 0; t < pr.nt; ++t) {
-      for (int q = lane; q < pr.nq; q += 32) {
-        const float x = __ldg(src + q * ld + t);
-        bad |= (x != x) || (x == -CUDART_INF_F);
-        scratch[static_cast<int64_t>(t) * pr.nq + q] = x;
+  const float* rows = src;  // solver row i starts at rows + i * row_pitch
+  int64_t row_pitch = s.rs;
+  if (mode == kModeShared) {
+    if (s.cs == 1) {
+      const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (s.rs & 3) == 0 && (nc & 3) == 0;
+      if (vec) {
+        const int chunks = nc >> 2;
+        for (int i = 0; i < nr; ++i) {
+          for (int c = lane; c < chunks; c += 32) cp_async16(tile + i * nc + 4 * c, src + i * s.rs + 4 * c);
+        }
+      } else {
+        for (int i = 0; i < nr; ++i) {
+          for (int j = lane; j < nc; j += 32) cp_async4(tile + i * nc + j, src + i * s.rs + j);
+        }
       }
+    } else {
+      // the source runs along solver rows: consecutive lanes take consecutive rows
+      const int total = nr * nc;
+      for (int e = lane; e < total; e += 32) {
+        const int j = e / nr;
+        const int i = e - j * nr;
+        cp_async4(tile + i * nc + j, src + i * s.rs + j * s.cs);
+      }
+    }
+    cp_async_wait_all();
+    __syncwarp();
+    const int total = nr * nc;
+    if ((total & 3) == 0) {
+      const float4* t4 = reinterpret_cast<const float4*>(tile);
+      for (int e = lane; e < (total >> 2); e += 32) {
+        const float4 x = t4[e];
+        bad |= invalid_cost(x.x) || invalid_cost(x.y) || invalid_cost(x.z) || invalid_cost(x.w);
+      }
+    } else {
+      for (int e = lane; e < total; e += 32) bad |= invalid_cost(tile[e]);
+    }
+    rows = tile;
+    row_pitch = nc;
+  } else if (mode == kModeDirect) {
+    for (int i = 0; i < nr; ++i) {
+#pragma unroll 4
+      for (int j = lane; j < nc; j += 32) bad |= invalid_cost(__ldg(src + i * s.rs + j));
     }
   } else {
-    mode = Mode::kDirect;
-    for (int q = 0; q < pr.nq; ++q) {
-      for (int t = lane; t < pr.nt; t += 32) {
-        const float x = __ldg(src + q * ld + t);
-        bad |= (x != x) || (x == -CUDART_INF_F);
-      }
+    float* scratch = a.workspace + scratch_off;
+    const int total = nr * nc;
+    for (int e = lane; e < total; e += 32) {
+      const int j = e / nr;
+      const int i = e - j * nr;
+      const float x = __ldg(src + i * s.rs + j * s.cs);
+      bad |= invalid_cost(x);
+      scratch[static_cast<int64_t>(i) * nc + j] = x;
     }
+    rows = scratch;
+    row_pitch = nc;
   }
   bad = __any_sync(kFullMask, bad);
   for (int i = lane; i < nr; i += 32) {
@@ -220,13 +349,14 @@ __global__ void __launch_bounds__(32) lsap_kernel(const LsapArgs a) {
   int code = bad ? RFM_STATUS_INVALID : RFM_STATUS_OK;
   for (int cur = 0; cur < nr && code == RFM_STATUS_OK; ++cur) {
     double spc[K];
-    int pos[K];
+    unsigned key[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const int j = lane + 32 * k;
+      const unsigned pos = static_cast<unsigned>(nc - 1 - j);  // remaining[it] = nc-1-it (reverse fill)
       spc[k] = CUDART_INF;
-      pos[k] = nc - 1 - j;  // remaining[it] = nc - 1 - it  (reverse fill)
-      if (j < nc) rem_s[nc - 1 - j] = j;
+      key[k] = (freem & (1u << k)) ? kKeyBase - 1u - pos : kKeyBase + pos;
+      if (j < nc) rem_s[nc - 1 - j] = static_cast<int16_t>(j);
     }
     unsigned rem = valid;
     int i = cur;
@@ -238,43 +368,31 @@ __global__ void __launch_bounds__(32) lsap_kernel(const LsapArgs a) {
     for (int it = 0; it < nc; ++it) {
       const double ui = u_s[i];
       double bv = CUDART_INF;
-      int bk = INT_MAX;
-      if (mode == Mode::kShared) {
-        if (transposed) {
-          scan_row<K, true>(tile + i, tp, lane, i, minv, ui, v, spc, pos, rem, freem, path_s, bv,
-                            bk);
-        } else {
-          scan_row<K, true>(tile + i * tp, 1, lane, i, minv, ui, v, spc, pos, rem, freem, path_s,
-                            bv, bk);
-        }
-      } else if (mode == Mode::kScratch) {
-        scan_row<K, false>(scratch + static_cast<int64_t>(i) * pr.nq, 1, lane, i, minv, ui, v, spc,
-                           pos, rem, freem, path_s, bv, bk);
+      unsigned bk = kNoKey;
+      const float* row = rows + i * row_pitch;
+      if (mode == kModeShared) {
+        scan_row<K, kLoadShared>(row, lane, i, minv, ui, v, spc, key, rem, path_s, bv, bk);
+      } else if (mode == kModeDirect) {
+        scan_row<K, kLoadGlobal>(row, lane, i, minv, ui, v, spc, key, rem, path_s, bv, bk);
       } else {
-        scan_row<K, false>(src + i * ld, 1, lane, i, minv, ui, v, spc, pos, rem, freem, path_s, bv,
-                           bk);
+        scan_row<K, kLoadScratch>(row, lane, i, minv, ui, v, spc, key, rem, path_s, bv, bk);
       }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const double ov = __shfl_xor_sync(kFullMask, bv, off);
-        const int ok = __shfl_xor_sync(kFullMask, bk, off);
-        if (ov < bv || (ov == bv && ok < bk)) {
-          bv = ov;
-          bk = ok;
-        }
-      }
+      warp_argmin(bv, bk);
       if (bv == CUDART_INF) {
         code = RFM_STATUS_INFEASIBLE;
         break;
       }
-      const int ps = bk < 0 ? -bk - 1 : bk;
+      const int ps = static_cast<int>(bk < kKeyBase ? kKeyBase - 1u - bk : bk - kKeyBase);
       const int last = nrem - 1;
       const int js = rem_s[ps];
       const int jl = rem_s[last];
       const int rj = row4col_s[js];
       __syncwarp();
-      if (lane == 0) rem_s[ps] = jl;  // swap-with-last removal
-      if ((jl & 31) == lane) set_pos<K>(pos, jl >> 5, ps);
+      if (lane == 0) rem_s[ps] = static_cast<int16_t>(jl);  // swap-with-last removal
+      if ((jl & 31) == lane) {
+        const int kl = jl >> 5;
+        set_key<K>(key, kl, ((freem >> kl) & 1u) ? kKeyBase - 1u - ps : kKeyBase + ps);
+      }
       if ((js & 31) == lane) rem &= ~(1u << (js >> 5));
       nrem = last;
       minv = bv;
@@ -298,10 +416,7 @@ __global__ void __launch_bounds__(32) lsap_kernel(const LsapArgs a) {
       if (visited & (1u << k)) {
         const int j = lane + 32 * k;
         const double d = minv - spc[k];
-        if (j != sink) {
-          const int r = row4col_s[j];
-          u_s[r] += d;
-        }
+        if (j != sink) u_s[row4col_s[j]] += d;
         v[k] -= d;
       }
     }
@@ -313,11 +428,11 @@ __global__ void __launch_bounds__(32) lsap_kernel(const LsapArgs a) {
     if (lane == 0) {
       flipped = 0;
       int j = sink;
-      for (int s = 0; s <= nr; ++s) {
+      for (int step = 0; step <= nr; ++step) {
         const int ii = path_s[j];
-        row4col_s[j] = ii;
+        row4col_s[j] = static_cast<int16_t>(ii);
         const int prev = col4row_s[ii];
-        col4row_s[ii] = j;
+        col4row_s[ii] = static_cast<int16_t>(j);
         j = prev;
         if (ii == cur) {
           flipped = 1;
@@ -334,8 +449,8 @@ __global__ void __launch_bounds__(32) lsap_kernel(const LsapArgs a) {
   if (kDense) {
     // matching[w] = task of worker w, -1 if none (kernels_lap.py:336-341)
     if (code != RFM_STATUS_OK) {
-      for (int w = lane; w < pr.nq; w += 32) q_out[w] = -1;
-    } else if (transposed) {
+      for (int w = lane; w < nq; w += 32) q_out[w] = -1;
+    } else if (s.transposed) {
       for (int w = lane; w < nc; w += 32) q_out[w] = row4col_s[w];
     } else {
       for (int w = lane; w < nr; w += 32) q_out[w] = col4row_s[w];
@@ -345,9 +460,9 @@ __global__ void __launch_bounds__(32) lsap_kernel(const LsapArgs a) {
       q_out[k] = -1;
       t_out[k] = -1;
     }
-  } else if (transposed) {
+  } else if (s.transposed) {
     // rows are targets: emit matched queries (solver columns) in ascending order
-    int base = 0;
+    int slot0 = 0;
     const unsigned lt_mask = (1u << lane) - 1u;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -355,30 +470,19 @@ __global__ void __launch_bounds__(32) lsap_kernel(const LsapArgs a) {
       const unsigned ballot = __ballot_sync(kFullMask, matched);
       if (matched) {
         const int j = lane + 32 * k;
-        const int slot = base + __popc(ballot & lt_mask);
-        q_out[slot] = j + pr.qbase;
+        const int slot = slot0 + __popc(ballot & lt_mask);
+        q_out[slot] = j + qbase;
         t_out[slot] = row4col_s[j];
       }
-      base += __popc(ballot);
+      slot0 += __popc(ballot);
     }
   } else {
     for (int r = lane; r < nr; r += 32) {
-      q_out[r] = r + pr.qbase;
+      q_out[r] = r + qbase;
       t_out[r] = col4row_s[r];
     }
   }
   if (a.status != nullptr && lane == 0) a.status[p] = code;
-}
-
-int smem_limit() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return kSmemLimitDefault;
-  int v = 0;
-  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-      v <= 0) {
-    return kSmemLimitDefault;
-  }
-  return v;
 }
 
 int cols_per_lane_for(int max_cols) {
@@ -388,23 +492,16 @@ int cols_per_lane_for(int max_cols) {
   return -1;
 }
 
-// Largest on-chip tile (floats) a CTA may stage: the hardware limit, and a
-// soft cap that keeps several CTAs resident per SM.
-constexpr int64_t kTileSoftCapFloats = 16384;
-
-int64_t tile_budget(int cols_cap, int max_rows, int64_t max_need) {
-  const int64_t hard = (static_cast<int64_t>(kSmemLimitDefault) -
-                        fixed_smem_bytes(cols_cap, max_rows)) / 4;
-  int64_t t = max_need < kTileSoftCapFloats ? max_need : kTileSoftCapFloats;
-  if (t > hard) t = hard;
-  return t < 0 ? 0 : t;
+// Shared-memory slot of one problem: the fixed arrays plus its tile when staged.
+int64_t slot_bytes(const Shape& s, int cols_cap, int max_rows, int64_t tile_cap) {
+  const int64_t t = static_cast<int64_t>(s.nr) * s.nc;
+  return warp_bytes_for(cols_cap, max_rows, (s.nr > 0 && t <= tile_cap) ? t : 0);
 }
 
 template <bool kDense>
-int launch(const LsapArgs& a, int cols_per_lane, int num_problems, void* stream) {
-  const int cols_cap = 32 * cols_per_lane;
-  const int64_t smem = fixed_smem_bytes(cols_cap, a.max_rows) + static_cast<int64_t>(a.tile_floats) * 4;
-  if (smem > smem_limit()) return RFM_ERR_UNSUPPORTED;
+int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta, int64_t smem,
+           void* stream) {
+  if (smem > kSmemPerBlockMax) return RFM_ERR_UNSUPPORTED;
   const void* fn = nullptr;
   switch (cols_per_lane) {
     case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense>); break;
@@ -412,14 +509,13 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_problems, void* stream)
     case 32: fn = reinterpret_cast<const void*>(&lsap_kernel<32, kDense>); break;
     default: return RFM_ERR_INVALID_ARGUMENT;
   }
-  if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess) {
-      return launch_status();
-    }
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess) {
+    return launch_status();
   }
-  const dim3 grid(static_cast<unsigned>(num_problems));
-  const dim3 block(32);
+  const dim3 grid(static_cast<unsigned>(num_ctas));
+  const dim3 block(32 * warps_per_cta);
   switch (cols_per_lane) {
     case 4: lsap_kernel<4, kDense><<<grid, block, smem, as_stream(stream)>>>(a); break;
     case 10: lsap_kernel<10, kDense><<<grid, block, smem, as_stream(stream)>>>(a); break;
@@ -431,98 +527,152 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_problems, void* stream)
 }  // namespace
 }  // namespace rfm
 
-extern "C" int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems,
+extern "C" int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, int64_t stride_q,
+                                  int64_t stride_t, int64_t tile_cap_floats, int32_t* host_ctas,
                                   rfm_lsap_plan* plan) {
   using namespace rfm;
-  if (plan == nullptr || num_problems < 0 || (num_problems > 0 && host_problems == nullptr)) {
+  if (plan == nullptr || num_problems < 0 ||
+      (num_problems > 0 && (host_problems == nullptr || host_ctas == nullptr)) || stride_q < 0 ||
+      stride_t < 0) {
     return RFM_ERR_INVALID_ARGUMENT;
   }
+  int64_t cap = tile_cap_floats < 0 ? kTileCapDefault : tile_cap_floats;
   int max_cols = 1, max_rows = 1;
-  int64_t max_need = 0;
   for (int p = 0; p < num_problems; ++p) {
     const rfm_problem& d = host_problems[p];
     if (d.num_queries < 0 || d.num_targets < 0 || d.cost_offset < 0 || d.out_offset < 0 ||
         d.reserved != 0) {
       return RFM_ERR_INVALID_ARGUMENT;
     }
-    const int lo = d.num_queries < d.num_targets ? d.num_queries : d.num_targets;
-    const int hi = d.num_queries < d.num_targets ? d.num_targets : d.num_queries;
-    if (lo == 0) continue;
-    if (hi > max_cols) max_cols = hi;
-    if (lo > max_rows) max_rows = lo;
-    const int64_t need = tile_need(d.num_queries, d.num_targets);
-    if (need > max_need) max_need = need;
+    const Shape s = solver_shape(d.num_queries, d.num_targets, stride_q, stride_t);
+    if (s.nr == 0) continue;
+    if (s.nc > max_cols) max_cols = s.nc;
+    if (s.nr > max_rows) max_rows = s.nr;
   }
   const int cpl = cols_per_lane_for(max_cols);
   if (cpl < 0) return RFM_ERR_UNSUPPORTED;
-  const int64_t tile = tile_budget(32 * cpl, max_rows, max_need);
+  const int cols_cap = 32 * cpl;
+  const int64_t fixed = fixed_warp_bytes(cols_cap, max_rows);
+  const int64_t hard_cap = (kSmemPerBlockMax - fixed) / 4;
+  if (cap > hard_cap) cap = hard_cap;
+
+  // scratch for tiles that are neither staged nor row-contiguous in the source
   int64_t scratch = 0;
   for (int p = 0; p < num_problems; ++p) {
     rfm_problem& d = host_problems[p];
     d.scratch_offset = -1;
-    const int lo = d.num_queries < d.num_targets ? d.num_queries : d.num_targets;
-    if (lo == 0) continue;
-    if (tile_need(d.num_queries, d.num_targets) > tile && d.num_targets < d.num_queries) {
+    const Shape s = solver_shape(d.num_queries, d.num_targets, stride_q, stride_t);
+    if (s.nr == 0) continue;
+    const int64_t slot = slot_bytes(s, cols_cap, max_rows, cap);
+    if (choose_mode(s, cap, (slot - fixed) / 4) == kModeScratch) {
       d.scratch_offset = scratch;
-      scratch += (static_cast<int64_t>(d.num_queries) * d.num_targets + 3) & ~int64_t(3);
+      scratch += (static_cast<int64_t>(s.nr) * s.nc + 3) & ~int64_t(3);
     }
   }
+
+  // pack consecutive problems into CTAs of up to four warps under the budget;
+  // every warp of a CTA gets the CTA's largest slot
+  int64_t budget = kCtaBudget;
+  for (int p = 0; p < num_problems; ++p) {
+    const rfm_problem& d = host_problems[p];
+    const int64_t sl = slot_bytes(solver_shape(d.num_queries, d.num_targets, stride_q, stride_t),
+                                  cols_cap, max_rows, cap);
+    if (sl > budget) budget = sl;
+  }
+  int num_ctas = 0;
+  int64_t cta_smem = 0;
+  for (int p = 0; p < num_problems;) {
+    const rfm_problem& d0 = host_problems[p];
+    int64_t slot = slot_bytes(solver_shape(d0.num_queries, d0.num_targets, stride_q, stride_t),
+                              cols_cap, max_rows, cap);
+    int count = 1;
+    while (count < kMaxWarpsPerCta && p + count < num_problems) {
+      const rfm_problem& d = host_problems[p + count];
+      const int64_t sl = slot_bytes(solver_shape(d.num_queries, d.num_targets, stride_q, stride_t),
+                                    cols_cap, max_rows, cap);
+      const int64_t next = sl > slot ? sl : slot;
+      if ((count + 1) * next > budget) break;
+      slot = next;
+      ++count;
+    }
+    host_ctas[4 * num_ctas + 0] = p;
+    host_ctas[4 * num_ctas + 1] = count;
+    host_ctas[4 * num_ctas + 2] = static_cast<int32_t>(slot);
+    host_ctas[4 * num_ctas + 3] = 0;
+    if (count * slot > cta_smem) cta_smem = count * slot;
+    ++num_ctas;
+    p += count;
+  }
   plan->cols_per_lane = cpl;
-  plan->tile_floats = static_cast<int32_t>(tile);
   plan->max_rows = max_rows;
   plan->num_problems = num_problems;
+  plan->num_ctas = num_ctas;
+  plan->cta_smem_bytes = static_cast<int32_t>(cta_smem);
+  plan->tile_cap_floats = static_cast<int32_t>(cap);
+  plan->stride_q = stride_q;
+  plan->stride_t = stride_t;
   plan->workspace_bytes = scratch * 4;
   return RFM_OK;
 }
 
-extern "C" int rfm_lsap(const float* cost, int64_t ld, const rfm_problem* problems,
+extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const int32_t* ctas,
                         const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out,
                         int32_t* status, void* workspace, void* stream) {
   using namespace rfm;
-  if (plan == nullptr || plan->num_problems < 0 || plan->tile_floats < 0 || plan->max_rows < 1 ||
-      plan->workspace_bytes < 0 || ld < 0) {
+  if (plan == nullptr || plan->num_problems < 0 || plan->num_ctas < 0 || plan->max_rows < 1 ||
+      plan->workspace_bytes < 0 || plan->stride_q < 0 || plan->stride_t < 0 ||
+      plan->tile_cap_floats < 0 || plan->cta_smem_bytes < 0 || plan->cta_smem_bytes > kSmemPerBlockMax ||
+      cols_per_lane_for(32 * plan->cols_per_lane) != plan->cols_per_lane) {
     return RFM_ERR_INVALID_ARGUMENT;
   }
-  if (plan->num_problems == 0) return RFM_OK;
-  if (cost == nullptr || problems == nullptr || query_out == nullptr || target_out == nullptr ||
-      (plan->workspace_bytes > 0 && workspace == nullptr)) {
+  if (plan->num_problems == 0 || plan->num_ctas == 0) return RFM_OK;
+  if (cost == nullptr || problems == nullptr || ctas == nullptr || query_out == nullptr ||
+      target_out == nullptr || (plan->workspace_bytes > 0 && workspace == nullptr)) {
     return RFM_ERR_INVALID_ARGUMENT;
   }
   LsapArgs a;
   a.cost = cost;
-  a.ld = ld;
+  a.stride_q = plan->stride_q;
+  a.stride_t = plan->stride_t;
   a.problems = problems;
+  a.ctas = reinterpret_cast<const int4*>(ctas);
+  a.num_problems = plan->num_problems;
   a.dense_w = 0;
   a.dense_t = 0;
-  a.tile_floats = plan->tile_floats;
+  a.dense_warps = 0;
+  a.dense_slot = 0;
+  a.tile_cap = plan->tile_cap_floats;
   a.max_rows = plan->max_rows;
   a.workspace = static_cast<float*>(workspace);
   a.q_out = query_out;
   a.t_out = target_out;
   a.status = status;
-  return launch<false>(a, plan->cols_per_lane, plan->num_problems, stream);
+  return launch<false>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta, plan->cta_smem_bytes,
+                       stream);
 }
 
 namespace {
 struct DensePlan {
-  int cpl;
-  int64_t tile;
-  int max_rows;
-  int64_t scratch_bytes;
+  int cpl, max_rows, warps;
+  int64_t slot, tile_cap, scratch_bytes;
 };
 
 int dense_plan(int num_problems, int num_workers, int num_tasks, DensePlan* out) {
   using namespace rfm;
   if (num_problems < 0 || num_workers < 0 || num_tasks < 0) return RFM_ERR_INVALID_ARGUMENT;
-  const int lo = num_workers < num_tasks ? num_workers : num_tasks;
-  const int hi = num_workers < num_tasks ? num_tasks : num_workers;
-  out->cpl = cols_per_lane_for(hi < 1 ? 1 : hi);
+  const Shape s = solver_shape(num_workers, num_tasks, num_tasks, 1);
+  out->cpl = cols_per_lane_for(s.nc < 1 ? 1 : s.nc);
   if (out->cpl < 0) return RFM_ERR_UNSUPPORTED;
-  out->max_rows = lo < 1 ? 1 : lo;
-  const int64_t need = lo == 0 ? 0 : tile_need(num_workers, num_tasks);
-  out->tile = tile_budget(32 * out->cpl, out->max_rows, need);
+  out->max_rows = s.nr < 1 ? 1 : s.nr;
+  const int64_t fixed = fixed_warp_bytes(32 * out->cpl, out->max_rows);
+  out->tile_cap = kTileCapDefault;
+  if (out->tile_cap > (kSmemPerBlockMax - fixed) / 4) out->tile_cap = (kSmemPerBlockMax - fixed) / 4;
+  out->slot = slot_bytes(s, 32 * out->cpl, out->max_rows, out->tile_cap);
+  int w = kMaxWarpsPerCta;
+  while (w > 1 && w * out->slot > kCtaBudget) --w;
+  out->warps = w;
   out->scratch_bytes = 0;
-  if (lo > 0 && need > out->tile && num_tasks < num_workers) {
+  if (s.nr > 0 && choose_mode(s, out->tile_cap, (out->slot - fixed) / 4) == kModeScratch) {
     out->scratch_bytes = static_cast<int64_t>(num_problems) * num_workers * num_tasks * 4;
   }
   return RFM_OK;
@@ -550,15 +700,21 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   }
   LsapArgs a;
   a.cost = cost;
-  a.ld = num_tasks;
+  a.stride_q = num_tasks;
+  a.stride_t = 1;
   a.problems = nullptr;
+  a.ctas = nullptr;
+  a.num_problems = num_problems;
   a.dense_w = num_workers;
   a.dense_t = num_tasks;
-  a.tile_floats = static_cast<int>(dp.tile);
+  a.dense_warps = dp.warps;
+  a.dense_slot = static_cast<int>(dp.slot);
+  a.tile_cap = static_cast<int>(dp.tile_cap);
   a.max_rows = dp.max_rows;
   a.workspace = static_cast<float*>(workspace);
   a.q_out = matching;
   a.t_out = nullptr;
   a.status = status;
-  return launch<true>(a, dp.cpl, num_problems, stream);
+  const int ctas = (num_problems + dp.warps - 1) / dp.warps;
+  return launch<true>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);
 }

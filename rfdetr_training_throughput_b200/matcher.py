@@ -13,10 +13,12 @@ query index), with the group offset ``g * Q/G`` added to the query index
 (patches.py:398).
 
 Two launches do the whole step on the device, with no host synchronisation:
-``rfm_cost`` builds every layer's compact ``[Q, sum T]`` cost matrix and
-``rfm_lsap`` solves all ``layers x images x groups`` problems in place and
-writes the index pairs at their final position; the per-image tuples are views
-of one output buffer (``torch.split`` with host-known sizes).
+``rfm_cost`` writes every layer's cost matrix (target-major: the transpose of the
+compact ``[Q, sum T]`` matrix, so that both kernels move whole coalesced rows)
+and ``rfm_lsap`` solves all ``layers x images x groups`` problems in place and
+writes the index pairs at their final position.  ``match_packed`` is the
+allocation-light core (packed targets in, one packed pair buffer out);
+``match_layers`` and ``HungarianMatcher`` wrap it in rf-detr's list interface.
 
 The sub-steps are exposed under the names of the functions the reference
 patches: ``compute_compact_detection_cost_matrix`` (patches.py:123-149),
@@ -59,6 +61,80 @@ def _aligned16(t: torch.Tensor) -> torch.Tensor:
     return t if t.data_ptr() % 16 == 0 else t.clone()
 
 
+def _round4(x: int) -> int:
+    return (x + 3) // 4 * 4
+
+
+# --------------------------------------------------------------------------- inputs / outputs
+
+
+@dataclass
+class PackedTargets:
+    """All images' targets of a batch in two device tensors plus host-known sizes.
+
+    ``labels`` ``[S]`` int64 and ``boxes`` ``[S, 4]`` float32 cxcywh hold image
+    ``b``'s targets at rows ``offsets[b]:offsets[b+1]`` (``sizes`` is known on the
+    host, as ``len(target["boxes"])`` is in rf-detr).
+    """
+
+    labels: torch.Tensor
+    boxes: torch.Tensor
+    sizes: tuple[int, ...]
+
+    @staticmethod
+    def from_list(targets: Sequence[dict], device: torch.device | None = None) -> "PackedTargets":
+        sizes = tuple(int(t["labels"].shape[0]) for t in targets)
+        if any(int(t["boxes"].shape[0]) != s for t, s in zip(targets, sizes)):
+            raise ValueError("targets[i]['labels'] and ['boxes'] disagree in length")
+        if device is None:
+            device = targets[0]["labels"].device if targets else torch.device("cuda")
+        if not targets:
+            return PackedTargets(torch.zeros(0, dtype=torch.int64, device=device),
+                                 torch.zeros((0, 4), dtype=torch.float32, device=device), sizes)
+        labels = torch.cat([t["labels"].reshape(-1) for t in targets]).to(device=device, dtype=torch.int64)
+        boxes = torch.cat([t["boxes"].reshape(-1, 4) for t in targets]).to(device=device, dtype=torch.float32)
+        return PackedTargets(labels.contiguous(), _aligned16(boxes.contiguous()), sizes)
+
+    def checked(self) -> "PackedTargets":
+        _require_cuda(self.labels, "labels")
+        _require_cuda(self.boxes, "boxes")
+        total = sum(self.sizes)
+        if self.labels.shape != (total,) or self.boxes.shape != (total, 4):
+            raise ValueError("packed targets do not match their sizes")
+        labels = self.labels if self.labels.dtype == torch.int64 else self.labels.long()
+        boxes = self.boxes if self.boxes.dtype == torch.float32 else self.boxes.float()
+        return PackedTargets(labels.contiguous(), _aligned16(boxes.contiguous()), self.sizes)
+
+
+class MatchResult:
+    """Packed result of one matcher step: ``pairs`` ``[2, total]`` int64 on the device.
+
+    Layer ``l``, image ``b`` owns ``pairs[:, start:start+count]`` with the host-known
+    ``count = group_detr * min(Q/G, T_b)``; ``layer(l)`` builds rf-detr's list of
+    per-image ``(query_idx, target_idx)`` views (no copy).
+    """
+
+    def __init__(self, pairs: torch.Tensor, per_image: list[int], layers: int, images: int):
+        self.pairs = pairs
+        self.per_image = per_image
+        self.layers = layers
+        self.images = images
+        self._views = None
+
+    def _split(self):
+        if self._views is None:
+            self._views = (torch.split(self.pairs[0], self.per_image), torch.split(self.pairs[1], self.per_image))
+        return self._views
+
+    def layer(self, l: int) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        q, t = self._split()
+        base = l * self.images
+        return [(q[base + b], t[base + b]) for b in range(self.images)]
+
+    def as_lists(self) -> list[list[tuple[torch.Tensor, torch.Tensor]]]:
+        return [self.layer(l) for l in range(self.layers)]
+
+
 # --------------------------------------------------------------------------- plans
 
 
@@ -70,13 +146,15 @@ class StepPlan:
     layers: int
     queries: int
     group_detr: int
+    layout: int
     ld: int
     problems: np.ndarray  # PROBLEM_DTYPE, in launch order (largest tile first)
     order: np.ndarray  # launch index -> (layer, image, group) problem index
     plan: _lib.LsapPlan
     total_pairs: int
     per_image: list[int]  # pairs per (layer, image), layer-major
-    device_blob: torch.Tensor  # problems bytes followed by int32 offsets [B+1]
+    device_blob: torch.Tensor  # problems, then the int32 CTA table, then int32 offsets [B+1]
+    ctas_byte: int
     offsets_byte: int
 
     @property
@@ -84,19 +162,30 @@ class StepPlan:
         return self.device_blob.data_ptr()
 
     @property
+    def ctas_ptr(self) -> int:
+        return self.device_blob.data_ptr() + self.ctas_byte
+
+    @property
     def offsets_ptr(self) -> int:
         return self.device_blob.data_ptr() + self.offsets_byte
 
 
-def build_problems(sizes: Sequence[int], layers: int, queries: int, group_detr: int, ld: int):
+def strides(layout: int, ld: int) -> tuple[int, int]:
+    """(stride_q, stride_t) of a cost layout with row stride ``ld``."""
+    return (ld, 1) if layout == _lib.LAYOUT_QUERY_MAJOR else (1, ld)
+
+
+def build_problems(sizes: Sequence[int], layers: int, queries: int, group_detr: int, ld: int,
+                   layout: int = _lib.LAYOUT_QUERY_MAJOR):
     """Problem descriptors of a step, in (layer, image, group) order.
 
     Problem ``(l, b, g)`` is the ``[Q/G, T_b]`` block of layer ``l``'s compact
-    matrix at rows ``g*Q/G ...`` and columns ``off[b] ...``; its pairs go to the
-    ``(l, b)`` image chunk at ``g * min(Q/G, T_b)``.  The layer-image-group order
-    and the group offset follow ``_stack_padded`` as patches.py:371,398 reads it.
-    Returns ``(problems, per_image_pairs, total_pairs, offsets)``; problems whose
-    image has no target are dropped.
+    matrix at rows ``g*Q/G ...`` and columns ``off[b] ...`` (or the same block of
+    its target-major transpose); its pairs go to the ``(l, b)`` image chunk at
+    ``g * min(Q/G, T_b)``.  The layer-image-group order and the group offset follow
+    ``_stack_padded`` as patches.py:371,398 reads it.  Returns
+    ``(problems, per_image_pairs, total_pairs, offsets)``; problems whose image has
+    no target are dropped.
     """
     if group_detr < 1 or queries % group_detr:
         raise ValueError(f"num_queries {queries} is not a multiple of group_detr {group_detr}")
@@ -104,6 +193,7 @@ def build_problems(sizes: Sequence[int], layers: int, queries: int, group_detr: 
     if (sz < 0).any():
         raise ValueError("negative target count")
     nimg = sz.shape[0]
+    total_t = int(sz.sum())
     qg = queries // group_detr
     offsets = np.zeros(nimg + 1, dtype=np.int64)
     offsets[1:] = np.cumsum(sz)
@@ -117,7 +207,10 @@ def build_problems(sizes: Sequence[int], layers: int, queries: int, group_detr: 
     keep = sz[img] > 0
     lay, img, grp = lay[keep], img[keep], grp[keep]
     pr = np.zeros(lay.shape[0], dtype=_lib.PROBLEM_DTYPE)
-    pr["cost_offset"] = lay * queries * ld + grp * qg * ld + offsets[img]
+    if layout == _lib.LAYOUT_QUERY_MAJOR:
+        pr["cost_offset"] = lay * queries * ld + grp * qg * ld + offsets[img]
+    else:
+        pr["cost_offset"] = lay * total_t * ld + offsets[img] * ld + grp * qg
     pr["out_offset"] = image_base[lay * nimg + img] + grp * pairs[img]
     pr["num_queries"] = qg
     pr["num_targets"] = sz[img]
@@ -141,46 +234,46 @@ class _PlanCache:
             self._d.popitem(last=False)
         return value
 
+    def clear(self) -> None:
+        self._d.clear()
+
 
 _PLANS = _PlanCache()
 
 
 def plan_step(sizes: Sequence[int], layers: int, queries: int, group_detr: int, ld: int,
-              device: torch.device) -> StepPlan:
+              device: torch.device, layout: int = _lib.LAYOUT_QUERY_MAJOR,
+              tile_cap: int | None = None) -> StepPlan:
     """Cached host planning plus ONE non-blocking pinned upload of descriptors and offsets."""
     sizes = tuple(int(s) for s in sizes)
-    key = (sizes, layers, queries, group_detr, ld, str(device))
+    cap = _lib.default_tile_cap() if tile_cap is None else int(tile_cap)
+    key = (sizes, layers, queries, group_detr, ld, layout, cap, str(device))
 
     def make() -> StepPlan:
-        pr, per_image, total, offsets = build_problems(sizes, layers, queries, group_detr, ld)
-        need = pr["num_queries"].astype(np.int64) * (pr["num_targets"].astype(np.int64) | 1)
+        pr, per_image, total, offsets = build_problems(sizes, layers, queries, group_detr, ld, layout)
+        need = pr["num_queries"].astype(np.int64) * pr["num_targets"].astype(np.int64)
         order = np.argsort(-need, kind="stable")
         pr = np.ascontiguousarray(pr[order])
-        plan = _lib.make_plan(pr)
+        sq, st = strides(layout, ld)
+        plan, ctas = _lib.make_plan(pr, sq, st, cap)
         pbytes = pr.view(np.uint8).reshape(-1)
+        cbytes = ctas.view(np.uint8).reshape(-1)
         off32 = offsets.astype(np.int32)
-        offsets_byte = (pbytes.shape[0] + 15) // 16 * 16
+        ctas_byte = (pbytes.shape[0] + 15) // 16 * 16
+        offsets_byte = (ctas_byte + cbytes.shape[0] + 15) // 16 * 16
         blob = np.zeros(offsets_byte + off32.nbytes, dtype=np.uint8)
         blob[: pbytes.shape[0]] = pbytes
+        blob[ctas_byte: ctas_byte + cbytes.shape[0]] = cbytes
         blob[offsets_byte:] = off32.view(np.uint8)
         host = torch.from_numpy(blob).pin_memory()
         dev = host.to(device, non_blocking=True)
-        return StepPlan(sizes, layers, queries, group_detr, ld, pr, order, plan, total, per_image, dev,
-                        offsets_byte)
+        return StepPlan(sizes, layers, queries, group_detr, layout, ld, pr, order, plan, total, per_image, dev,
+                        ctas_byte, offsets_byte)
 
     return _PLANS.get(key, make)
 
 
 # --------------------------------------------------------------------------- kernels
-
-
-def _gather_targets(targets: Sequence[dict], device: torch.device):
-    sizes = [int(t["labels"].shape[0]) for t in targets]
-    if any(int(t["boxes"].shape[0]) != s for t, s in zip(targets, sizes)):
-        raise ValueError("targets[i]['labels'] and ['boxes'] disagree in length")
-    labels = torch.cat([t["labels"].reshape(-1) for t in targets]).to(device=device, dtype=torch.int64)
-    boxes = torch.cat([t["boxes"].reshape(-1, 4) for t in targets]).to(device=device, dtype=torch.float32)
-    return sizes, labels.contiguous(), _aligned16(boxes.contiguous())
 
 
 def _stack_layer_outputs(outputs_list: Sequence[dict]) -> tuple[torch.Tensor, torch.Tensor]:
@@ -192,40 +285,41 @@ def _stack_layer_outputs(outputs_list: Sequence[dict]) -> tuple[torch.Tensor, to
         if lg.dim() != 3 or bx.dim() != 3 or bx.shape[-1] != 4 or lg.shape[:2] != bx.shape[:2]:
             raise ValueError("expected pred_logits [B, Q, C] and pred_boxes [B, Q, 4]")
     if len(outputs_list) == 1:
-        lg = logits[0].unsqueeze(0)
-        bx = boxes[0].unsqueeze(0)
-    else:
-        lg = torch.stack(logits)
-        bx = torch.stack(boxes)
-    lg = lg.to(torch.float32).contiguous()
-    bx = _aligned16(bx.to(torch.float32).contiguous())
-    return lg, bx
+        return logits[0].unsqueeze(0), boxes[0].unsqueeze(0)
+    return torch.stack(logits), torch.stack(boxes)
+
+
+def _prepare_predictions(logits: torch.Tensor, boxes: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    _require_cuda(logits, "pred_logits")
+    _require_cuda(boxes, "pred_boxes")
+    if logits.dim() != 4 or boxes.dim() != 4 or boxes.shape[-1] != 4 or logits.shape[:3] != boxes.shape[:3]:
+        raise ValueError("expected pred_logits [L, B, Q, C] and pred_boxes [L, B, Q, 4]")
+    logits = logits.to(torch.float32).contiguous()
+    boxes = _aligned16(boxes.to(torch.float32).contiguous())
+    return logits, boxes
 
 
 def launch_cost(logits: torch.Tensor, boxes: torch.Tensor, labels: torch.Tensor, tgt_boxes: torch.Tensor,
-                offsets_ptr: int, sum_t: int, ld: int, weights: dict, out: torch.Tensor) -> None:
-    """Enqueue ``rfm_cost`` for logits [L,B,Q,C] / boxes [L,B,Q,4] into ``out`` [L,Q,ld]."""
+                offsets_ptr: int, sum_t: int, ld: int, layout: int, weights: dict, out: torch.Tensor) -> None:
+    """Enqueue ``rfm_cost`` for logits [L,B,Q,C] / boxes [L,B,Q,4] into ``out``."""
     layers, nimg, queries, ncls = logits.shape
     lib = _lib.load()
     _lib.check("rfm_cost", lib.rfm_cost(
         _ptr(logits), _ptr(boxes), _ptr(labels), _ptr(tgt_boxes), ctypes.c_void_p(offsets_ptr),
-        layers, nimg, queries, ncls, sum_t, ld,
+        layers, nimg, queries, ncls, sum_t, ld, layout,
         float(weights["cost_class"]), float(weights["cost_bbox"]), float(weights["cost_giou"]),
         float(weights["focal_alpha"]), _ptr(out), _stream_handle(out.device)))
 
 
-def launch_lsap(cost: torch.Tensor, ld: int, plan: StepPlan, pairs: torch.Tensor,
-                status: torch.Tensor | None) -> None:
+def launch_lsap(cost: torch.Tensor, plan: StepPlan, pairs: torch.Tensor, status: torch.Tensor | None) -> None:
     """Enqueue ``rfm_lsap`` over a planned step; ``pairs`` is int64 [2, total_pairs]."""
     lib = _lib.load()
     ws = None
     if plan.plan.workspace_bytes > 0:
         ws = torch.empty(int(plan.plan.workspace_bytes), dtype=torch.uint8, device=cost.device)
-    q_out = pairs[0]
-    t_out = pairs[1]
     _lib.check("rfm_lsap", lib.rfm_lsap(
-        _ptr(cost), ld, ctypes.c_void_p(plan.problems_ptr), ctypes.byref(plan.plan),
-        _ptr(q_out), _ptr(t_out), _ptr(status), _ptr(ws), _stream_handle(cost.device)))
+        _ptr(cost), ctypes.c_void_p(plan.problems_ptr), ctypes.c_void_p(plan.ctas_ptr), ctypes.byref(plan.plan),
+        _ptr(pairs[0]), _ptr(pairs[1]), _ptr(status), _ptr(ws), _stream_handle(cost.device)))
 
 
 def raise_on_status(status: torch.Tensor) -> None:
@@ -242,66 +336,77 @@ def raise_on_status(status: torch.Tensor) -> None:
 # --------------------------------------------------------------------------- matcher
 
 
-def _record(events: dict | None, name: str):
-    if events is None:
-        return None
-    ev = torch.cuda.Event(enable_timing=True)
-    ev.record()
-    events.setdefault(name, []).append(ev)
-    return ev
+def _record(events: dict | None, name: str) -> None:
+    if events is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        events.setdefault(name, []).append(ev)
 
 
-def match_layers(outputs_list: Sequence[dict], targets: Sequence[dict], group_detr: int = 1, *,
-                 weights: dict | None = None, check_status: bool = False,
-                 return_cost: bool = False, extras: dict | None = None,
-                 events: dict | None = None) -> Any:
-    """Match every decoder layer of one step against the same targets, in two launches.
+def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: PackedTargets,
+                 group_detr: int = 1, *, weights: dict | None = None, check_status: bool = False,
+                 extras: dict | None = None, events: dict | None = None) -> MatchResult:
+    """One matcher step over logits ``[L, B, Q, C]`` and boxes ``[L, B, Q, 4]``, two launches.
 
-    Returns one list of per-image ``(query_idx, target_idx)`` tuples per layer
-    (and the padded ``[L, Q, ld]`` cost buffer with ``return_cost``).  ``extras``,
-    when given, receives the packed ``[2, total]`` pair buffer the tuples view
-    (``"pairs"``), the cost buffer and the step plan.  ``events``, when given,
+    ``extras``, when given, receives the target-major cost buffer ``[L, S, ld]``
+    (``"cost"``), its row stride and the step plan.  ``events``, when given,
     collects CUDA events recorded on the launching stream around each kernel
-    (``"cost"`` and ``"lsap"``: start/end pairs), for timing.
+    (``"cost"`` and ``"lsap"``: start/end pairs).
     """
-    w = dict(DEFAULT_WEIGHTS if weights is None else weights)
-    if not outputs_list:
-        return []
-    logits, boxes = _stack_layer_outputs(outputs_list)
+    w = DEFAULT_WEIGHTS if weights is None else weights
+    logits, boxes = _prepare_predictions(pred_logits, pred_boxes)
+    tg = targets.checked()
     device = logits.device
     layers, nimg, queries, _ = logits.shape
-    if len(targets) != nimg:
-        raise ValueError(f"{len(targets)} targets for a batch of {nimg} images")
-    sizes, labels, tgt_boxes = _gather_targets(targets, device)
-    sum_t = sum(sizes)
-    ld = (sum_t + 3) // 4 * 4
-    plan = plan_step(sizes, layers, queries, group_detr, ld, device)
-    cost = torch.empty((layers, queries, ld), dtype=torch.float32, device=device)
+    if len(tg.sizes) != nimg:
+        raise ValueError(f"{len(tg.sizes)} targets for a batch of {nimg} images")
+    sum_t = sum(tg.sizes)
+    ld = _round4(queries)
+    layout = _lib.LAYOUT_TARGET_MAJOR
+    plan = plan_step(tg.sizes, layers, queries, group_detr, ld, device, layout)
+    cost = torch.empty((layers, sum_t, ld), dtype=torch.float32, device=device)
     pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=device)
-    status = None
-    if check_status:
-        status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=device)
-    if ld > 0:
+    status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=device) if check_status else None
+    if sum_t > 0:
         _record(events, "cost")
-        launch_cost(logits, boxes, labels, tgt_boxes, plan.offsets_ptr, sum_t, ld, w, cost)
+        launch_cost(logits, boxes, tg.labels, tg.boxes, plan.offsets_ptr, sum_t, ld, layout, w, cost)
         _record(events, "cost")
     if plan.problems.shape[0] > 0:
         _record(events, "lsap")
-        launch_lsap(cost, ld, plan, pairs, status)
+        launch_lsap(cost, plan, pairs, status)
         _record(events, "lsap")
     if status is not None:
         raise_on_status(status)
-    q_chunks = torch.split(pairs[0], plan.per_image)
-    t_chunks = torch.split(pairs[1], plan.per_image)
-    result = [[(q_chunks[l * nimg + b], t_chunks[l * nimg + b]) for b in range(nimg)] for l in range(layers)]
     if extras is not None:
-        extras.update(pairs=pairs, cost=cost, plan=plan, ld=ld)
+        extras.update(cost=cost, ld=ld, plan=plan, layout=layout)
+    return MatchResult(pairs, plan.per_image, layers, nimg)
+
+
+def match_layers(outputs_list: Sequence[dict], targets: Sequence[dict] | PackedTargets, group_detr: int = 1, *,
+                 weights: dict | None = None, check_status: bool = False, return_cost: bool = False,
+                 extras: dict | None = None, events: dict | None = None) -> Any:
+    """Match every decoder layer of one step against the same targets (the stacked
+    single-pass path of patches.py:235-249), in two launches.
+
+    Returns one list of per-image ``(query_idx, target_idx)`` tuples per layer; with
+    ``return_cost`` also the compact ``[L, Q, sum T]`` cost matrix the solver used
+    (a transposed view of the target-major buffer).
+    """
+    if not outputs_list:
+        return []
+    logits, boxes = _stack_layer_outputs(outputs_list)
+    packed = targets if isinstance(targets, PackedTargets) else PackedTargets.from_list(targets, logits.device)
+    ex = {} if (extras is None and return_cost) else extras
+    res = match_packed(logits, boxes, packed, group_detr, weights=weights, check_status=check_status,
+                       extras=ex, events=events)
+    lists = res.as_lists()
     if return_cost:
-        return result, cost
-    return result
+        q = logits.shape[2]
+        return lists, ex["cost"][:, :, :q].transpose(1, 2)
+    return lists
 
 
-def compute_compact_detection_cost_matrix(outputs: dict, targets: Sequence[dict], *,
+def compute_compact_detection_cost_matrix(outputs: dict, targets: Sequence[dict] | PackedTargets, *,
                                           weights: dict | None = None) -> torch.Tensor:
     """Compact ``[Q, sum T]`` cost (``[L, Q, sum T]`` for 4-D logits), contiguous float32.
 
@@ -309,23 +414,22 @@ def compute_compact_detection_cost_matrix(outputs: dict, targets: Sequence[dict]
     padded intermediate.  Labels are always clamped into ``[0, C-1]``
     (kernels_matcher.py:133-134).
     """
-    w = dict(DEFAULT_WEIGHTS if weights is None else weights)
+    w = DEFAULT_WEIGHTS if weights is None else weights
     lg, bx = outputs["pred_logits"], outputs["pred_boxes"]
     _require_cuda(lg, "pred_logits")
-    _require_cuda(bx, "pred_boxes")
     squeeze = lg.dim() == 3
     if squeeze:
         lg, bx = lg.unsqueeze(0), bx.unsqueeze(0)
-    lg = lg.to(torch.float32).contiguous()
-    bx = _aligned16(bx.to(torch.float32).contiguous())
+    lg, bx = _prepare_predictions(lg, bx)
     layers, nimg, queries, _ = lg.shape
-    sizes, labels, tgt_boxes = _gather_targets(targets, lg.device)
-    sum_t = sum(sizes)
+    packed = targets if isinstance(targets, PackedTargets) else PackedTargets.from_list(targets, lg.device)
+    tg = packed.checked()
+    sum_t = sum(tg.sizes)
     out = torch.empty((layers, queries, sum_t), dtype=torch.float32, device=lg.device)
     if sum_t > 0:
-        offs = torch.tensor(np.concatenate([[0], np.cumsum(sizes)]).astype(np.int32)).pin_memory()
+        offs = torch.from_numpy(np.concatenate([[0], np.cumsum(tg.sizes)]).astype(np.int32)).pin_memory()
         offs = offs.to(lg.device, non_blocking=True)
-        launch_cost(lg, bx, labels, tgt_boxes, offs.data_ptr(), sum_t, sum_t, w, out)
+        launch_cost(lg, bx, tg.labels, tg.boxes, offs.data_ptr(), sum_t, sum_t, _lib.LAYOUT_QUERY_MAJOR, w, out)
     return out[0] if squeeze else out
 
 
@@ -349,16 +453,14 @@ def assign_padded(cost_matrices: Sequence[torch.Tensor], sizes: Sequence[int], g
         if cost.shape[0] != queries or cost.shape[1] != sum(sizes):
             raise ValueError(f"cost matrix {tuple(cost.shape)} does not match {queries} queries x {sum(sizes)} targets")
         ld = int(cost.stride(0))
-        plan = plan_step(sizes, 1, queries, group_detr, ld, cost.device)
+        plan = plan_step(sizes, 1, queries, group_detr, ld, cost.device, _lib.LAYOUT_QUERY_MAJOR)
         pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=cost.device)
         status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=cost.device) if check_status else None
         if plan.problems.shape[0] > 0:
-            launch_lsap(cost, ld, plan, pairs, status)
+            launch_lsap(cost, plan, pairs, status)
         if status is not None:
             raise_on_status(status)
-        q_chunks = torch.split(pairs[0], plan.per_image)
-        t_chunks = torch.split(pairs[1], plan.per_image)
-        results.append(list(zip(q_chunks, t_chunks)))
+        results.append(MatchResult(pairs, plan.per_image, 1, len(sizes)).layer(0))
     return results
 
 

@@ -46,51 +46,80 @@ def test_problem_struct_layout_matches_header():
     assert [f[1] for f in fields] == list(_lib.PROBLEM_DTYPE.names)
     sizes = {"int64_t": 8, "int32_t": 4}
     assert [sizes[f[0]] for f in fields] == [_lib.PROBLEM_DTYPE[n].itemsize for n in _lib.PROBLEM_DTYPE.names]
-    assert ctypes.sizeof(_lib.LsapPlan) == 24
+    assert ctypes.sizeof(_lib.LsapPlan) == 48
 
 
 def test_invalid_arguments_are_rejected_before_any_cuda_call():
     lib = _lib.load()
     # negative sizes, ld < sum_targets
-    assert lib.rfm_cost(None, None, None, None, None, 0, 1, 1, 1, 0, 0, 1.0, 1.0, 1.0, 0.25, None, None) == 1
-    assert lib.rfm_cost(None, None, None, None, None, 1, 1, 1, 1, 8, 4, 1.0, 1.0, 1.0, 0.25, None, None) == 1
+    qm, tm = _lib.LAYOUT_QUERY_MAJOR, _lib.LAYOUT_TARGET_MAJOR
+    assert lib.rfm_cost(None, None, None, None, None, 0, 1, 1, 1, 0, 0, qm, 1.0, 1.0, 1.0, 0.25, None, None) == 1
+    assert lib.rfm_cost(None, None, None, None, None, 1, 1, 1, 1, 8, 4, qm, 1.0, 1.0, 1.0, 0.25, None, None) == 1
+    # target-major rows must hold every query and keep 16-byte alignment
+    assert lib.rfm_cost(None, None, None, None, None, 1, 1, 8, 1, 3, 6, tm, 1.0, 1.0, 1.0, 0.25, None, None) == 1
+    assert lib.rfm_cost(None, None, None, None, None, 1, 1, 8, 1, 3, 10, tm, 1.0, 1.0, 1.0, 0.25, None, None) == 1
+    assert lib.rfm_cost(None, None, None, None, None, 1, 1, 8, 1, 3, 8, 7, 1.0, 1.0, 1.0, 0.25, None, None) == 1
     # zero-sized output: nothing to do
-    assert lib.rfm_cost(None, None, None, None, None, 1, 1, 1, 1, 0, 0, 1.0, 1.0, 1.0, 0.25, None, None) == 0
-    plan = _lib.LsapPlan(cols_per_lane=10, tile_floats=0, max_rows=1, num_problems=3, workspace_bytes=0)
-    assert lib.rfm_lsap(None, 8, None, ctypes.byref(plan), None, None, None, None, None) == 1
-    assert lib.rfm_lsap(None, 8, None, None, None, None, None, None, None) == 1
+    assert lib.rfm_cost(None, None, None, None, None, 1, 1, 1, 1, 0, 0, qm, 1.0, 1.0, 1.0, 0.25, None, None) == 0
+    plan = _lib.LsapPlan(cols_per_lane=10, max_rows=1, num_problems=3, num_ctas=1, cta_smem_bytes=4096,
+                         tile_cap_floats=0, stride_q=1, stride_t=8, workspace_bytes=0)
+    assert lib.rfm_lsap(None, None, None, ctypes.byref(plan), None, None, None, None, None) == 1
+    assert lib.rfm_lsap(None, None, None, None, None, None, None, None, None) == 1
+    plan.cols_per_lane = 7
+    assert lib.rfm_lsap(None, None, None, ctypes.byref(plan), None, None, None, None, None) == 1
     assert lib.rfm_lsap_dense(None, -1, 3, 3, None, None, None, None) == 1
     assert lib.rfm_lsap_dense(None, 4, 2000, 3, None, None, None, None) == 2
     assert lib.rfm_lsap_dense_workspace_bytes(-1, 3, 3) < 0
 
 
+def _cta_cover(ctas, n):
+    """The CTA table covers problems 0..n-1 once, in order, with 1-4 warps each."""
+    nxt = 0
+    for first, count, slot, zero in ctas.tolist():
+        assert first == nxt and 1 <= count <= 4 and slot % 16 == 0 and zero == 0
+        nxt += count
+    assert nxt == n
+
+
 def test_planner_modes_and_workspace():
-    pr = np.zeros(5, dtype=_lib.PROBLEM_DTYPE)
+    sizes = [250, 300, 60, 8, 0]
+    pr = np.zeros(len(sizes), dtype=_lib.PROBLEM_DTYPE)
     pr["num_queries"] = 300
-    pr["num_targets"] = [8, 250, 300, 0, 60]
-    plan = _lib.make_plan(pr)
-    assert plan.cols_per_lane == 10
-    assert plan.max_rows == 300
-    assert plan.num_problems == 5
-    # tall tiles above the on-chip budget (64 KB) are staged in scratch; square/wide ones are
-    # read in place; 300 x (60|1) floats = 73 KB is above the budget as well
-    assert pr["scratch_offset"].tolist() == [-1, 0, -1, -1, 300 * 250]
+    pr["num_targets"] = sizes
+    # query-major source (strides q: 1000, t: 1): tall tiles above the on-chip cap (64 KB) are
+    # transposed into scratch, the square one is read in place, the small one is staged
+    plan, ctas = _lib.make_plan(pr, 1000, 1)
+    assert plan.cols_per_lane == 10 and plan.max_rows == 300 and plan.num_problems == 5
+    assert pr["scratch_offset"].tolist() == [0, -1, 300 * 250, -1, -1]
     assert plan.workspace_bytes == (300 * 250 + 300 * 60) * 4
-    assert plan.tile_floats == 16384
-    pr2 = np.zeros(2, dtype=_lib.PROBLEM_DTYPE)
-    pr2["num_queries"] = 300
-    pr2["num_targets"] = [8, 12]
-    plan2 = _lib.make_plan(pr2)
-    assert plan2.workspace_bytes == 0 and plan2.tile_floats == 300 * 13
+    assert plan.stride_q == 1000 and plan.stride_t == 1 and plan.tile_cap_floats == 16384
+    _cta_cover(ctas, 5)
+    assert plan.cta_smem_bytes == max(c * s for _, c, s, _ in ctas.tolist())
+    # target-major source (q: 1, t: 4000): tall problems' solver rows are contiguous and are read
+    # in place; only the square one (solver rows = queries, strided here) needs scratch
+    pr2 = pr.copy()
+    plan2, _ = _lib.make_plan(pr2, 1, 4000)
+    assert pr2["scratch_offset"].tolist() == [-1, 0, -1, -1, -1] and plan2.workspace_bytes == 300 * 300 * 4
+    # a zero cap stages nothing; rows are then read straight from L2/HBM, four warps per CTA
+    pr3 = pr.copy()
+    plan3, ctas3 = _lib.make_plan(pr3, 1, 4000, tile_cap=0)
+    assert plan3.workspace_bytes == 300 * 300 * 4 and ctas3.tolist()[0][1] == 4
+    # small staged tiles share CTAs
+    small = np.zeros(9, dtype=_lib.PROBLEM_DTYPE)
+    small["num_queries"] = 300
+    small["num_targets"] = [12, 12, 10, 9, 8, 8, 8, 8, 3]
+    plan4, ctas4 = _lib.make_plan(small, 1, 4000)
+    _cta_cover(ctas4, 9)
+    assert plan4.workspace_bytes == 0 and plan4.num_ctas < 9
     wide = np.zeros(1, dtype=_lib.PROBLEM_DTYPE)
     wide["num_queries"] = 64
     wide["num_targets"] = 1025
     with pytest.raises(_lib.RfmError):
-        _lib.make_plan(wide)
+        _lib.make_plan(wide, 1025, 1)
     bad = np.zeros(1, dtype=_lib.PROBLEM_DTYPE)
     bad["num_queries"] = -1
     with pytest.raises(_lib.RfmError):
-        _lib.make_plan(bad)
+        _lib.make_plan(bad, 1, 1)
 
 
 def test_dense_workspace_bytes():

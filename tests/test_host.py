@@ -28,6 +28,18 @@ def test_build_problems_layout_brute_force():
     assert per_image == [g * min(qg, t) for _ in range(layers) for t in sizes]
 
 
+def test_build_problems_target_major_offsets():
+    sizes = [3, 0, 5]
+    layers, queries, g, ld = 2, 12, 3, 12
+    pr, _, _, offsets = matcher.build_problems(sizes, layers, queries, g, ld, layout=1)
+    qg = queries // g
+    s = sum(sizes)
+    expect = [l * s * ld + offsets[b] * ld + gi * qg for l in range(layers) for b, t in enumerate(sizes)
+              for gi in range(g) if t]
+    assert [int(x) for x in pr["cost_offset"]] == expect
+    assert matcher.strides(0, 7) == (7, 1) and matcher.strides(1, 7) == (1, 7)
+
+
 def test_build_problems_rejects_bad_groups():
     with pytest.raises(ValueError):
         matcher.build_problems([3], 1, 10, 3, 4)

@@ -1,0 +1,101 @@
+"""Install the B200 matcher into an importable rf-detr, by the reference's patch names.
+
+Mirrors the reference's plugin interface for this path (patches.py:704-735): a
+``PATCHES`` registry of named, opt-in monkeypatches and ``apply_patches("a,b")``,
+which applies them in order, returns one description per patch and raises
+``KeyError`` on an unknown name.  The hot-path names keep their meaning:
+
+``triton_matcher``  ``HungarianMatcher._compute_compact_detection_cost_matrix``
+                    -> ``rfm_cost`` (patches.py:100-152)
+``cuda_lap``        ``torch_linear_assignment.batch_linear_assignment``
+                    -> ``rfm_lsap_dense`` (patches.py:291-327)
+``device_indices``  ``rfdetr.models._assignment._assign_padded``
+                    -> ``rfm_lsap`` on the compact matrices in place (patches.py:330-421)
+``stacked_costs``   raise rf-detr's stacked-cost budget so all layers share one pass
+                    (patches.py:235-249)
+``matcher``         ``HungarianMatcher.forward`` -> the two-launch device step (new: the
+                    whole matcher in one call, detection outputs only)
+
+Unlike the reference there is no fallback to the original implementation for
+CPU tensors or out-of-envelope inputs: the patched functions raise instead.
+"""
+
+from __future__ import annotations
+
+import importlib
+from typing import Callable
+
+from . import matcher as _m
+
+
+def _module(name: str):
+    try:
+        return importlib.import_module(name)
+    except ImportError as e:  # pragma: no cover - exercised with a stub in tests
+        raise ImportError(f"{name} is not importable; install rf-detr to patch it") from e
+
+
+def _apply_triton_matcher() -> str:
+    cls = _module("rfdetr.models.matcher").HungarianMatcher
+
+    def compute_compact_detection_cost_matrix(self, outputs, targets, *, clamp_target_labels=False):
+        if "pred_masks" in outputs:
+            raise NotImplementedError("segmentation costs are outside this matcher")
+        weights = {"cost_class": self.cost_class, "cost_bbox": self.cost_bbox, "cost_giou": self.cost_giou,
+                   "focal_alpha": self.focal_alpha}
+        return _m.compute_compact_detection_cost_matrix(outputs, targets, weights=weights)
+
+    cls._compute_compact_detection_cost_matrix = compute_compact_detection_cost_matrix
+    return "triton_matcher: compact cost matrix built by the sm_100a rfm_cost kernel"
+
+
+def _apply_cuda_lap() -> str:
+    module = _module("torch_linear_assignment.assignment")
+    module.batch_linear_assignment = _m.batch_linear_assignment
+    package = _module("torch_linear_assignment")
+    package.batch_linear_assignment = _m.batch_linear_assignment
+    return "cuda_lap: batch_linear_assignment solved by the SciPy-exact sm_100a solver"
+
+
+def _apply_device_indices() -> str:
+    module = _module("rfdetr.models._assignment")
+
+    def assign_padded(cost_matrices, sizes, group_width, group_detr):
+        return _m.assign_padded(cost_matrices, sizes, group_width, group_detr)
+
+    module._assign_padded = assign_padded
+    return "device_indices: assignment solved in place and unpacked on the device"
+
+
+def _apply_stacked_costs() -> str:
+    module = _module("rfdetr.models.matcher")
+    module._STACKED_COST_ELEMENT_LIMIT = 1 << 40
+    return "stacked_costs: matcher folds all layers into one cost-construction pass"
+
+
+def _apply_matcher() -> str:
+    cls = _module("rfdetr.models.matcher").HungarianMatcher
+    cls.forward = _m.HungarianMatcher.forward
+    cls.forward_layers = _m.HungarianMatcher.forward_layers
+    if not hasattr(cls, "weights"):
+        cls.weights = _m.HungarianMatcher.weights
+    return "matcher: HungarianMatcher.forward runs the two-launch device step"
+
+
+PATCHES: dict[str, Callable[[], str]] = {
+    "triton_matcher": _apply_triton_matcher,
+    "cuda_lap": _apply_cuda_lap,
+    "device_indices": _apply_device_indices,
+    "stacked_costs": _apply_stacked_costs,
+    "matcher": _apply_matcher,
+}
+
+
+def apply_patches(names: str) -> list[str]:
+    """Apply a comma-separated patch list; returns one description per patch."""
+    applied: list[str] = []
+    for name in [item.strip() for item in names.split(",") if item.strip()]:
+        if name not in PATCHES:
+            raise KeyError(f"unknown patch {name!r}; available: {sorted(PATCHES)}")
+        applied.append(PATCHES[name]())
+    return applied

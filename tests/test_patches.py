@@ -1,0 +1,63 @@
+"""The rf-detr patch registry, exercised against stub modules (rf-detr is not installed here)."""
+
+import sys
+import types
+
+import pytest
+import torch
+
+from rfdetr_training_throughput_b200 import matcher, patches
+
+
+@pytest.fixture()
+def fake_rfdetr(monkeypatch):
+    class HungarianMatcher:
+        def __init__(self):
+            self.cost_class, self.cost_bbox, self.cost_giou, self.focal_alpha = 2.0, 5.0, 2.0, 0.25
+
+        def _compute_compact_detection_cost_matrix(self, outputs, targets, *, clamp_target_labels=False):
+            return "upstream"
+
+        def forward(self, outputs, targets, group_detr=1):
+            return "upstream"
+
+    mods = {
+        "rfdetr": types.ModuleType("rfdetr"),
+        "rfdetr.models": types.ModuleType("rfdetr.models"),
+        "rfdetr.models.matcher": types.ModuleType("rfdetr.models.matcher"),
+        "rfdetr.models._assignment": types.ModuleType("rfdetr.models._assignment"),
+        "torch_linear_assignment": types.ModuleType("torch_linear_assignment"),
+        "torch_linear_assignment.assignment": types.ModuleType("torch_linear_assignment.assignment"),
+    }
+    mods["rfdetr.models.matcher"].HungarianMatcher = HungarianMatcher
+    mods["rfdetr.models.matcher"]._STACKED_COST_ELEMENT_LIMIT = 350_000
+    mods["rfdetr.models._assignment"]._assign_padded = lambda *a: "upstream"
+    mods["torch_linear_assignment.assignment"].batch_linear_assignment = lambda c: "upstream"
+    mods["torch_linear_assignment"].batch_linear_assignment = lambda c: "upstream"
+    for name, mod in mods.items():
+        monkeypatch.setitem(sys.modules, name, mod)
+    return mods
+
+
+def test_apply_patches_rebinds_the_reference_names(fake_rfdetr):
+    done = patches.apply_patches("triton_matcher, cuda_lap,device_indices,stacked_costs,matcher")
+    assert len(done) == 5 and all(":" in d for d in done)
+    cls = fake_rfdetr["rfdetr.models.matcher"].HungarianMatcher
+    assert fake_rfdetr["torch_linear_assignment.assignment"].batch_linear_assignment is matcher.batch_linear_assignment
+    assert fake_rfdetr["torch_linear_assignment"].batch_linear_assignment is matcher.batch_linear_assignment
+    assert fake_rfdetr["rfdetr.models.matcher"]._STACKED_COST_ELEMENT_LIMIT == 1 << 40
+    assert cls.forward is matcher.HungarianMatcher.forward
+    m = cls()
+    # patched paths have no CPU fallback: host tensors raise instead of returning "upstream"
+    outputs = {"pred_logits": torch.zeros(1, 3, 2), "pred_boxes": torch.zeros(1, 3, 4)}
+    targets = [{"labels": torch.zeros(1, dtype=torch.int64), "boxes": torch.zeros(1, 4)}]
+    with pytest.raises(ValueError, match="CUDA"):
+        m._compute_compact_detection_cost_matrix(outputs, targets)
+    with pytest.raises(ValueError, match="CUDA"):
+        fake_rfdetr["rfdetr.models._assignment"]._assign_padded([torch.zeros(3, 1)], [1], 3, 1)
+
+
+def test_unknown_patch_name_raises_keyerror():
+    with pytest.raises(KeyError, match="unknown patch"):
+        patches.apply_patches("not_a_patch")
+    assert patches.apply_patches("") == []

@@ -199,6 +199,27 @@ int64_t rfm_lsap_dense_workspace_bytes(int num_problems, int num_workers, int nu
 int rfm_lsap_dense(const float* cost, int num_problems, int num_workers, int num_tasks,
                    int64_t* matching, int32_t* status, void* workspace, void* stream);
 
+/*
+ * rfm_lsap_dense without a caller-provided workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory where
+ * they call the solver (a C FFI host without a device allocator, or a training
+ * step that must not add a cudaMalloc/cudaFree or compete with the
+ * framework's caching allocator).  The scratch is a built-in device array of
+ * RFM_NOALLOC_SCRATCH_BYTES held by every GPU that loads the library.
+ *
+ *   - Same inputs, outputs and results as rfm_lsap_dense; allocates nothing.
+ *   - Returns RFM_ERR_UNSUPPORTED, without launching, when the batch needs more
+ *     scratch than the built-in array (rfm_lsap_dense_workspace_bytes() >
+ *     RFM_NOALLOC_SCRATCH_BYTES); use rfm_lsap_dense with a workspace then.
+ *   - The first call on a device looks up the array's device address (once
+ *     per device); make that first call before any stream capture.
+ *   - All calls share the array: calls whose GPU work overlaps (e.g. on two
+ *     streams at once) race on it.  Nothing in it needs clearing between calls.
+ */
+#define RFM_NOALLOC_SCRATCH_BYTES (16u << 20)
+int rfm_lsap_dense_noalloc(const float* cost, int num_problems, int num_workers, int num_tasks,
+                           int64_t* matching, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

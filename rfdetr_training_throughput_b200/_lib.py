@@ -37,7 +37,11 @@ EXPORTS = (
     "rfm_lsap",
     "rfm_lsap_dense_workspace_bytes",
     "rfm_lsap_dense",
+    "rfm_lsap_dense_noalloc",
 )
+
+#: Size of the built-in scratch of rfm_lsap_dense_noalloc (RFM_NOALLOC_SCRATCH_BYTES).
+NOALLOC_SCRATCH_BYTES = 16 << 20
 
 #: numpy mirror of ``struct rfm_problem`` (40 bytes).
 PROBLEM_DTYPE = np.dtype(
@@ -119,6 +123,8 @@ def load() -> ctypes.CDLL:
     lib.rfm_lsap_dense_workspace_bytes.argtypes = [_i32, _i32, _i32]
     lib.rfm_lsap_dense.restype = _i32
     lib.rfm_lsap_dense.argtypes = [_p, _i32, _i32, _i32, _p, _p, _p, _p]
+    lib.rfm_lsap_dense_noalloc.restype = _i32
+    lib.rfm_lsap_dense_noalloc.argtypes = [_p, _i32, _i32, _i32, _p, _p, _p]
     _lib = lib
     return lib
 

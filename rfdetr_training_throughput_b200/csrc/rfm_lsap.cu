@@ -718,3 +718,67 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   const int ctas = (num_problems + dp.warps - 1) / dp.warps;
   return launch<true>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);
 }
+
+// ---------------------------------------------------------------------------
+// rfm_lsap_dense_noalloc: rfm_lsap_dense with a built-in scratch buffer.
+//
+// Some callers cannot hand the solver a workspace: hosts that reach the
+// library through a C FFI with no device allocator of their own, and training
+// loops that run the matcher between kernels where a cudaMalloc/cudaFree
+// (which may synchronise the whole device) or a second allocator competing
+// with the framework's caching pool is not acceptable.  For them the scratch
+// lives in a file-scope __device__ array of RFM_NOALLOC_SCRATCH_BYTES that is
+// part of this module, so every GPU that loads the library holds it until the
+// process exits.  Host code only ever uses its device address, fetched once
+// per device with cudaGetSymbolAddress on the first call made on that device.
+//
+// The solver writes every scratch element before reading it, so nothing has to
+// be cleared between calls.  All calls share this one buffer: calls whose work
+// overlaps on the GPU (for instance on two streams at once) race on it.
+static __device__ __align__(256) float g_noalloc_scratch[RFM_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+#include <mutex>
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_address[kNoAllocMaxDevices] = {};
+
+// Device address of the built-in scratch on the current device (set up once).
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  const cudaError_t e0 = cudaGetDevice(&dev);
+  if (e0 != cudaSuccess) {
+    cudaGetLastError();
+    return RFM_ERR_NO_DEVICE;
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return RFM_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_address[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) ? RFM_ERR_NO_DEVICE
+                                                                          : RFM_ERR_LAUNCH;
+    }
+    g_noalloc_address[dev] = p;
+  }
+  *out = g_noalloc_address[dev];
+  return RFM_OK;
+}
+}  // namespace
+
+extern "C" int rfm_lsap_dense_noalloc(const float* cost, int num_problems, int num_workers,
+                                      int num_tasks, int64_t* matching, int32_t* status,
+                                      void* stream) {
+  const int64_t need = rfm_lsap_dense_workspace_bytes(num_problems, num_workers, num_tasks);
+  if (need < 0) return static_cast<int>(-need);
+  if (need > static_cast<int64_t>(RFM_NOALLOC_SCRATCH_BYTES)) return RFM_ERR_UNSUPPORTED;
+  void* scratch = nullptr;
+  if (need > 0 && num_problems > 0 && num_workers > 0) {
+    const int rc = noalloc_scratch_address(&scratch);
+    if (rc != RFM_OK) return rc;
+  }
+  return rfm_lsap_dense(cost, num_problems, num_workers, num_tasks, matching, status, scratch, stream);
+}

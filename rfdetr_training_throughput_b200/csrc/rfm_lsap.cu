@@ -118,8 +118,9 @@ __host__ __device__ inline int choose_mode(const Shape& s, int64_t tile_cap, int
 }
 
 __host__ __device__ inline int64_t fixed_warp_bytes(int cols_cap, int max_rows) {
-  // u (float64) and col4row (int16) per row; row4col, path, remaining (int16) per column
-  const int64_t b = static_cast<int64_t>(max_rows) * 10 + static_cast<int64_t>(cols_cap) * 6;
+  // u and first-pick cost (float64), col4row and first-pick column (int16) per row;
+  // the 32 lanes' visited masks; row4col, path, remaining (int16) per column
+  const int64_t b = static_cast<int64_t>(max_rows) * 20 + 128 + static_cast<int64_t>(cols_cap) * 6;
   return (b + 15) & ~int64_t(15);
 }
 
@@ -210,6 +211,44 @@ __device__ __forceinline__ void scan_row(const float* row, int lane, int i, doub
   }
 }
 
+
+// Order-preserving map of a float (NaN excluded) onto uint32.
+__device__ __forceinline__ unsigned ordered32(float x) {
+  const unsigned b = __float_as_uint(x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ float from_ordered32(unsigned o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
+// First pick of one row when every column is free and v = 0: the smallest
+// cost, ties to the smallest column; lane 0 records it (column -1 when the
+// row's minimum is +inf, which leaves the row to the full search).
+template <int K>
+__device__ __forceinline__ void record_first_pick(const float (&x)[K], unsigned valid, int lane,
+                                                  int nc, int row, double* pick_m_s,
+                                                  int16_t* pick_w_s) {
+  float bvf = CUDART_INF_F;
+  int bj = 0xffff;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float c = x[k] + 0.0f;  // -0 and +0 tie, as the doubles (0 + c) do
+    if (((valid >> k) & 1u) && c < bvf) {
+      bvf = c;
+      bj = lane + 32 * k;
+    }
+  }
+  const unsigned o = ordered32(bvf);
+  const unsigned mo = __reduce_min_sync(kFullMask, o);
+  const unsigned mj = __reduce_min_sync(kFullMask, o == mo ? static_cast<unsigned>(bj) : 0xffffu);
+  if (lane == 0) {
+    const float m = from_ordered32(mo);
+    pick_m_s[row] = static_cast<double>(m);
+    pick_w_s[row] = static_cast<int16_t>(m == CUDART_INF_F || mj >= static_cast<unsigned>(nc) ? -1 : mj);
+  }
+}
+
 template <int K, bool kDense>
 __global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -262,11 +301,39 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapAr
 
   unsigned char* base = smem_raw + static_cast<int64_t>(warp) * slot;
   double* u_s = reinterpret_cast<double*>(base);
-  int16_t* col4row_s = reinterpret_cast<int16_t*>(u_s + a.max_rows);
-  int16_t* row4col_s = col4row_s + a.max_rows;
+  double* pick_m_s = u_s + a.max_rows;
+  unsigned* vis_s = reinterpret_cast<unsigned*>(pick_m_s + a.max_rows);
+  int16_t* col4row_s = reinterpret_cast<int16_t*>(vis_s + 32);
+  int16_t* pick_w_s = col4row_s + a.max_rows;
+  int16_t* row4col_s = pick_w_s + a.max_rows;
   int16_t* path_s = row4col_s + kCols;
   int16_t* rem_s = path_s + kCols;
-  // ---- stage / validate the cost (SciPy rejects NaN and -inf) -------------
+  unsigned valid = 0;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if (lane + 32 * k < nc) valid |= 1u << k;
+  }
+  for (int i = lane; i < nr; i += 32) {
+    u_s[i] = 0.0;
+    col4row_s[i] = -1;
+  }
+  for (int j = lane; j < nc; j += 32) row4col_s[j] = -1;
+
+  // ---- load the cost once: validate it (SciPy rejects NaN and -inf), keep
+  // it on chip when it fits, and find every row's first pick ---------------
+  // First picks (exact shortcut).  At its turn a row's first scan evaluates
+  // ((0 + c) - u) - v[j] with u = 0 over all columns in reverse-fill order.
+  // When the pick is a free column the search ends there: u[row] becomes the
+  // minimum, v is unchanged (the sink's slack is exactly 0) and only the sink
+  // turns matched.  The picks of all rows are therefore computed once, against
+  // v = 0 with every column free (SciPy's tie rule then takes the smallest
+  // column index; float order equals the order of the exactly promoted
+  // doubles), and a row commits its pick in O(1) while it is still valid.  A
+  // pick stays the exact argmin until its column is taken or visited by a full
+  // search: full searches only lower v on the columns they visit (by
+  // minv - spc >= 0), which raises those columns' reduced costs, and columns
+  // only ever turn from free to matched, which raises their tie keys.  Should
+  // rounding ever make a dual step negative, every pending pick is dropped.
   const float* src = a.cost + cost_off;
   const int64_t fixed = fixed_warp_bytes(kCols, a.max_rows);
   float* tile = reinterpret_cast<float*>(base + fixed);
@@ -274,80 +341,96 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapAr
   bool bad = false;
   const float* rows = src;  // solver row i starts at rows + i * row_pitch
   int64_t row_pitch = s.rs;
-  if (mode == kModeShared) {
-    if (s.cs == 1) {
-      const bool vec = (reinterpret_cast<uintptr_t>(src) & 15) == 0 && (s.rs & 3) == 0 && (nc & 3) == 0;
-      if (vec) {
-        const int chunks = nc >> 2;
-        for (int i = 0; i < nr; ++i) {
-          for (int c = lane; c < chunks; c += 32) cp_async16(tile + i * nc + 4 * c, src + i * s.rs + 4 * c);
-        }
-      } else {
-        for (int i = 0; i < nr; ++i) {
-          for (int j = lane; j < nc; j += 32) cp_async4(tile + i * nc + j, src + i * s.rs + j);
+  if (s.cs == 1) {
+    // solver rows are contiguous in the source: one coalesced pass over them
+    for (int i = 0; i < nr; i += 2) {
+      const bool two = i + 1 < nr;
+      float x0[K], x1[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int j = lane + 32 * k;
+        const bool ok = (valid >> k) & 1u;
+        x0[k] = ok ? __ldg(src + i * s.rs + j) : CUDART_INF_F;
+        x1[k] = (ok && two) ? __ldg(src + (i + 1) * s.rs + j) : CUDART_INF_F;
+      }
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        if ((valid >> k) & 1u) {
+          const int j = lane + 32 * k;
+          bad |= invalid_cost(x0[k]) || (two && invalid_cost(x1[k]));
+          if (mode == kModeShared) {
+            tile[i * nc + j] = x0[k];
+            if (two) tile[(i + 1) * nc + j] = x1[k];
+          }
         }
       }
-    } else {
-      // the source runs along solver rows: consecutive lanes take consecutive rows
-      const int total = nr * nc;
+      record_first_pick<K>(x0, valid, lane, nc, i, pick_m_s, pick_w_s);
+      if (two) record_first_pick<K>(x1, valid, lane, nc, i + 1, pick_m_s, pick_w_s);
+    }
+    if (mode == kModeShared) {
+      rows = tile;
+      row_pitch = nc;
+    }
+  } else {
+    // the source runs along solver rows: stage a transposed copy first
+    const int total = nr * nc;
+    if (mode == kModeShared) {
       for (int e = lane; e < total; e += 32) {
         const int j = e / nr;
         const int i = e - j * nr;
         cp_async4(tile + i * nc + j, src + i * s.rs + j * s.cs);
       }
-    }
-    cp_async_wait_all();
-    __syncwarp();
-    const int total = nr * nc;
-    if ((total & 3) == 0) {
-      const float4* t4 = reinterpret_cast<const float4*>(tile);
-      for (int e = lane; e < (total >> 2); e += 32) {
-        const float4 x = t4[e];
-        bad |= invalid_cost(x.x) || invalid_cost(x.y) || invalid_cost(x.z) || invalid_cost(x.w);
-      }
+      cp_async_wait_all();
+      __syncwarp();
+      rows = tile;
     } else {
-      for (int e = lane; e < total; e += 32) bad |= invalid_cost(tile[e]);
+      float* scratch = a.workspace + scratch_off;
+      for (int e = lane; e < total; e += 32) {
+        const int j = e / nr;
+        const int i = e - j * nr;
+        scratch[static_cast<int64_t>(i) * nc + j] = __ldg(src + i * s.rs + j * s.cs);
+      }
+      __syncwarp();
+      rows = scratch;
     }
-    rows = tile;
     row_pitch = nc;
-  } else if (mode == kModeDirect) {
     for (int i = 0; i < nr; ++i) {
-#pragma unroll 4
-      for (int j = lane; j < nc; j += 32) bad |= invalid_cost(__ldg(src + i * s.rs + j));
+      float x[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int j = lane + 32 * k;
+        const bool ok = (valid >> k) & 1u;
+        x[k] = !ok ? CUDART_INF_F : (mode == kModeShared ? rows[i * nc + j] : __ldcg(rows + i * nc + j));
+        bad |= ok && invalid_cost(x[k]);
+      }
+      record_first_pick<K>(x, valid, lane, nc, i, pick_m_s, pick_w_s);
     }
-  } else {
-    float* scratch = a.workspace + scratch_off;
-    const int total = nr * nc;
-    for (int e = lane; e < total; e += 32) {
-      const int j = e / nr;
-      const int i = e - j * nr;
-      const float x = __ldg(src + i * s.rs + j * s.cs);
-      bad |= invalid_cost(x);
-      scratch[static_cast<int64_t>(i) * nc + j] = x;
-    }
-    rows = scratch;
-    row_pitch = nc;
   }
   bad = __any_sync(kFullMask, bad);
-  for (int i = lane; i < nr; i += 32) {
-    u_s[i] = 0.0;
-    col4row_s[i] = -1;
-  }
-  for (int j = lane; j < nc; j += 32) row4col_s[j] = -1;
 
-  unsigned valid = 0;
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    if (lane + 32 * k < nc) valid |= 1u << k;
-  }
   unsigned freem = valid;
   double v[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) v[k] = 0.0;
   __syncwarp();
-
   int code = bad ? RFM_STATUS_INVALID : RFM_STATUS_OK;
+
   for (int cur = 0; cur < nr && code == RFM_STATUS_OK; ++cur) {
+    const int w = pick_w_s[cur];
+    if (w >= 0 && row4col_s[w] < 0) {  // still valid: commit the trivial augmentation
+      const double m = pick_m_s[cur];
+      __syncwarp();
+      if (lane == 0) {
+        u_s[cur] += m;
+        row4col_s[w] = static_cast<int16_t>(cur);
+        col4row_s[cur] = static_cast<int16_t>(w);
+      }
+      if ((w & 31) == lane) freem &= ~(1u << (w >> 5));
+      __syncwarp();
+      continue;
+    }
+
+    // ---- full shortest-augmenting-path search for row `cur` ---------------
     double spc[K];
     unsigned key[K];
 #pragma unroll
@@ -411,15 +494,18 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapAr
 
     // ---- dual update over the tree (lane-local, see header comment) -------
     const unsigned visited = valid & ~rem;
+    bool raised = false;  // a visited column's v went up: rounding broke minv >= spc
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       if (visited & (1u << k)) {
         const int j = lane + 32 * k;
         const double d = minv - spc[k];
+        raised |= d < 0.0;
         if (j != sink) u_s[row4col_s[j]] += d;
         v[k] -= d;
       }
     }
+    raised = __any_sync(kFullMask, raised);
     if (lane == 0) u_s[cur] += minv;
     __syncwarp();
 
@@ -442,6 +528,15 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapAr
     }
     if ((sink & 31) == lane) freem &= ~(1u << (sink >> 5));
     if (!__shfl_sync(kFullMask, flipped, 0)) code = RFM_STATUS_NO_SINK;
+
+    // ---- drop the pending picks this search visited (all of them if some
+    // column's reduced costs went down) ------------------------------------
+    vis_s[lane] = raised ? 0xffffffffu : visited;
+    __syncwarp();
+    for (int r = cur + 1 + lane; r < nr; r += 32) {
+      const int pw = pick_w_s[r];
+      if (pw >= 0 && ((vis_s[pw & 31] >> (pw >> 5)) & 1u)) pick_w_s[r] = -1;
+    }
     __syncwarp();
   }
 

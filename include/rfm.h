@@ -93,10 +93,16 @@ typedef struct rfm_lsap_plan {
   int32_t num_ctas;         /* entries of the CTA table */
   int32_t cta_smem_bytes;   /* dynamic shared memory of one CTA */
   int32_t tile_cap_floats;  /* largest cost tile staged on chip */
+  int32_t flags;            /* RFM_PLAN_* */
+  int32_t reserved;
   int64_t stride_q;         /* cost element (q, t) at cost_offset + q*stride_q + t*stride_t */
   int64_t stride_t;
   int64_t workspace_bytes;  /* device scratch rfm_lsap needs for this batch */
 } rfm_lsap_plan;
+
+/* rfm_lsap_plan.flags: the batch runs on persistent warps that pull problems
+ * in order from a counter kept at the start of the workspace. */
+#define RFM_PLAN_PERSISTENT 1
 
 /* Layouts rfm_cost can write. */
 #define RFM_LAYOUT_QUERY_MAJOR 0  /* out[l][q][ld]: the compact [Q, sum T] matrix of patches.py:149 */

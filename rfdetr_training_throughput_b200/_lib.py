@@ -58,6 +58,8 @@ PROBLEM_DTYPE = np.dtype(
 assert PROBLEM_DTYPE.itemsize == 40
 
 
+PLAN_PERSISTENT = 1
+
 LAYOUT_QUERY_MAJOR = 0
 LAYOUT_TARGET_MAJOR = 1
 
@@ -72,6 +74,8 @@ class LsapPlan(ctypes.Structure):
         ("num_ctas", ctypes.c_int32),
         ("cta_smem_bytes", ctypes.c_int32),
         ("tile_cap_floats", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
         ("stride_q", ctypes.c_int64),
         ("stride_t", ctypes.c_int64),
         ("workspace_bytes", ctypes.c_int64),

@@ -65,6 +65,8 @@ constexpr int kCtaBudget = kSmemPerSm / 4 - kSmemPerCtaReserved;
 // kKeyBase + pos, so the smallest key is SciPy's pick among equal path costs.
 constexpr unsigned kKeyBase = 1024u;
 constexpr unsigned kNoKey = 0xffffffffu;
+// Persistent launches keep their problem counter at the start of the workspace.
+constexpr int64_t kQueueBytes = 256;
 
 enum Mode : int { kModeShared = 0, kModeDirect = 1, kModeScratch = 2 };
 
@@ -75,7 +77,9 @@ struct LsapArgs {
   const int4* ctas;             // pair mode: {first problem, warps, slot bytes, 0} per CTA
   int num_problems;
   int dense_w, dense_t;  // dense mode: uniform [P, W, T] problems
-  int dense_warps, dense_slot;
+  int dense_warps;
+  int slot;              // dense and persistent modes: uniform shared-memory slot per warp
+  int* queue;            // persistent mode: next-problem counter (zeroed before the launch)
   int tile_cap;
   int max_rows;
   float* workspace;
@@ -156,11 +160,6 @@ __device__ __forceinline__ void warp_argmin(double& v, unsigned& key) {
 __device__ __forceinline__ void cp_async4(float* dst, const float* src) {
   const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
-  const unsigned d = static_cast<unsigned>(__cvta_generic_to_shared(dst));
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_wait_all() {
@@ -245,28 +244,15 @@ __device__ __forceinline__ void record_first_pick(const float (&x)[K], unsigned 
   if (lane == 0) {
     const float m = from_ordered32(mo);
     pick_m_s[row] = static_cast<double>(m);
-    pick_w_s[row] = static_cast<int16_t>(m == CUDART_INF_F || mj >= static_cast<unsigned>(nc) ? -1 : mj);
+    pick_w_s[row] = static_cast<int16_t>(m == CUDART_INF_F || mj >= static_cast<unsigned>(nc) ? -1 : static_cast<int>(mj));
   }
 }
 
+// Solves problem p with the warp's shared-memory slot at `base` (`slot` bytes).
 template <int K, bool kDense>
-__global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapArgs a) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+__device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned char* base, int slot,
+                                              int lane) {
   constexpr int kCols = 32 * K;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  int p, slot;
-  if (kDense) {
-    p = blockIdx.x * a.dense_warps + warp;
-    slot = a.dense_slot;
-    if (p >= a.num_problems) return;
-  } else {
-    const int4 cta = a.ctas[blockIdx.x];
-    if (warp >= cta.y) return;
-    p = cta.x + warp;
-    slot = cta.z;
-  }
-
   int64_t cost_off, out_off, scratch_off;
   int nq, nt, qbase;
   if (kDense) {
@@ -299,7 +285,6 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapAr
     return;
   }
 
-  unsigned char* base = smem_raw + static_cast<int64_t>(warp) * slot;
   double* u_s = reinterpret_cast<double*>(base);
   double* pick_m_s = u_s + a.max_rows;
   unsigned* vis_s = reinterpret_cast<unsigned*>(pick_m_s + a.max_rows);
@@ -580,6 +565,36 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapAr
   if (a.status != nullptr && lane == 0) a.status[p] = code;
 }
 
+template <int K, bool kDense>
+__global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  if (kDense) {
+    const int p = blockIdx.x * a.dense_warps + warp;
+    if (p < a.num_problems) {
+      solve_problem<K, kDense>(a, p, smem_raw + static_cast<int64_t>(warp) * a.slot, a.slot, lane);
+    }
+  } else if (a.queue != nullptr) {
+    // persistent warps: pull problems (sorted largest first) until none is left
+    unsigned char* base = smem_raw + static_cast<int64_t>(warp) * a.slot;
+    for (;;) {
+      int p = 0;
+      if (lane == 0) p = atomicAdd(a.queue, 1);
+      p = __shfl_sync(kFullMask, p, 0);
+      if (p >= a.num_problems) break;
+      solve_problem<K, kDense>(a, p, base, a.slot, lane);
+      __syncwarp();
+    }
+  } else {
+    const int4 cta = a.ctas[blockIdx.x];
+    if (warp < cta.y) {
+      solve_problem<K, kDense>(a, cta.x + warp, smem_raw + static_cast<int64_t>(warp) * cta.z, cta.z,
+                               lane);
+    }
+  }
+}
+
 int cols_per_lane_for(int max_cols) {
   if (max_cols <= 128) return 4;
   if (max_cols <= 320) return 10;
@@ -591,6 +606,39 @@ int cols_per_lane_for(int max_cols) {
 int64_t slot_bytes(const Shape& s, int cols_cap, int max_rows, int64_t tile_cap) {
   const int64_t t = static_cast<int64_t>(s.nr) * s.nc;
   return warp_bytes_for(cols_cap, max_rows, (s.nr > 0 && t <= tile_cap) ? t : 0);
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    return 1;
+  }
+  return n;
+}
+
+// CTAs of the pair-mode kernel that fit on one SM at this shared-memory size.
+int resident_ctas(int cols_per_lane, int64_t smem) {
+  const void* fn = nullptr;
+  switch (cols_per_lane) {
+    case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, false>); break;
+    case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, false>); break;
+    default: fn = reinterpret_cast<const void*>(&lsap_kernel<32, false>); break;
+  }
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, 32 * kMaxWarpsPerCta,
+                                                    static_cast<size_t>(smem)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
 }
 
 template <bool kDense>
@@ -651,6 +699,30 @@ extern "C" int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, 
   const int64_t hard_cap = (kSmemPerBlockMax - fixed) / 4;
   if (cap > hard_cap) cap = hard_cap;
 
+  // When every problem's solver rows are contiguous in the source, nothing is
+  // staged: persistent warps with a uniform slot pull the problems in order.
+  bool contiguous = true;
+  for (int p = 0; p < num_problems && contiguous; ++p) {
+    const rfm_problem& d = host_problems[p];
+    const Shape s = solver_shape(d.num_queries, d.num_targets, stride_q, stride_t);
+    if (s.nr > 0 && s.cs != 1) contiguous = false;
+  }
+  if (contiguous) {
+    for (int p = 0; p < num_problems; ++p) host_problems[p].scratch_offset = -1;
+    plan->cols_per_lane = cpl;
+    plan->max_rows = max_rows;
+    plan->num_problems = num_problems;
+    plan->num_ctas = 0;  // sized at launch from the device's occupancy
+    plan->cta_smem_bytes = static_cast<int32_t>(kMaxWarpsPerCta * fixed);
+    plan->tile_cap_floats = 0;
+    plan->flags = RFM_PLAN_PERSISTENT;
+    plan->reserved = 0;
+    plan->stride_q = stride_q;
+    plan->stride_t = stride_t;
+    plan->workspace_bytes = kQueueBytes;
+    return RFM_OK;
+  }
+
   // scratch for tiles that are neither staged nor row-contiguous in the source
   int64_t scratch = 0;
   for (int p = 0; p < num_problems; ++p) {
@@ -704,6 +776,8 @@ extern "C" int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, 
   plan->num_ctas = num_ctas;
   plan->cta_smem_bytes = static_cast<int32_t>(cta_smem);
   plan->tile_cap_floats = static_cast<int32_t>(cap);
+  plan->flags = 0;
+  plan->reserved = 0;
   plan->stride_q = stride_q;
   plan->stride_t = stride_t;
   plan->workspace_bytes = scratch * 4;
@@ -717,12 +791,16 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   if (plan == nullptr || plan->num_problems < 0 || plan->num_ctas < 0 || plan->max_rows < 1 ||
       plan->workspace_bytes < 0 || plan->stride_q < 0 || plan->stride_t < 0 ||
       plan->tile_cap_floats < 0 || plan->cta_smem_bytes < 0 || plan->cta_smem_bytes > kSmemPerBlockMax ||
+      (plan->flags & ~RFM_PLAN_PERSISTENT) != 0 ||
       cols_per_lane_for(32 * plan->cols_per_lane) != plan->cols_per_lane) {
     return RFM_ERR_INVALID_ARGUMENT;
   }
-  if (plan->num_problems == 0 || plan->num_ctas == 0) return RFM_OK;
-  if (cost == nullptr || problems == nullptr || ctas == nullptr || query_out == nullptr ||
-      target_out == nullptr || (plan->workspace_bytes > 0 && workspace == nullptr)) {
+  const bool persistent = (plan->flags & RFM_PLAN_PERSISTENT) != 0;
+  if (plan->num_problems == 0 || (!persistent && plan->num_ctas == 0)) return RFM_OK;
+  if (cost == nullptr || problems == nullptr || (!persistent && ctas == nullptr) ||
+      query_out == nullptr || target_out == nullptr ||
+      (plan->workspace_bytes > 0 && workspace == nullptr) ||
+      (persistent && plan->workspace_bytes < kQueueBytes)) {
     return RFM_ERR_INVALID_ARGUMENT;
   }
   LsapArgs a;
@@ -735,15 +813,28 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   a.dense_w = 0;
   a.dense_t = 0;
   a.dense_warps = 0;
-  a.dense_slot = 0;
+  a.slot = 0;
+  a.queue = nullptr;
   a.tile_cap = plan->tile_cap_floats;
   a.max_rows = plan->max_rows;
   a.workspace = static_cast<float*>(workspace);
   a.q_out = query_out;
   a.t_out = target_out;
   a.status = status;
-  return launch<false>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta, plan->cta_smem_bytes,
-                       stream);
+  if (!persistent) {
+    return launch<false>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta, plan->cta_smem_bytes,
+                         stream);
+  }
+  a.queue = static_cast<int*>(workspace);
+  a.workspace = reinterpret_cast<float*>(static_cast<char*>(workspace) + kQueueBytes);
+  a.slot = plan->cta_smem_bytes / kMaxWarpsPerCta;
+  if (cudaMemsetAsync(a.queue, 0, sizeof(int), as_stream(stream)) != cudaSuccess) return launch_status();
+  const int ctas_per_sm = resident_ctas(plan->cols_per_lane, plan->cta_smem_bytes);
+  if (ctas_per_sm < 1) return launch_status() != RFM_OK ? RFM_ERR_LAUNCH : RFM_ERR_UNSUPPORTED;
+  const int grid = ctas_per_sm * sm_count();
+  const int needed = (plan->num_problems + kMaxWarpsPerCta - 1) / kMaxWarpsPerCta;
+  return launch<false>(a, plan->cols_per_lane, grid < needed ? grid : needed, kMaxWarpsPerCta,
+                       plan->cta_smem_bytes, stream);
 }
 
 namespace {
@@ -803,7 +894,8 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.dense_w = num_workers;
   a.dense_t = num_tasks;
   a.dense_warps = dp.warps;
-  a.dense_slot = static_cast<int>(dp.slot);
+  a.slot = static_cast<int>(dp.slot);
+  a.queue = nullptr;
   a.tile_cap = static_cast<int>(dp.tile_cap);
   a.max_rows = dp.max_rows;
   a.workspace = static_cast<float*>(workspace);

@@ -46,7 +46,7 @@ def test_problem_struct_layout_matches_header():
     assert [f[1] for f in fields] == list(_lib.PROBLEM_DTYPE.names)
     sizes = {"int64_t": 8, "int32_t": 4}
     assert [sizes[f[0]] for f in fields] == [_lib.PROBLEM_DTYPE[n].itemsize for n in _lib.PROBLEM_DTYPE.names]
-    assert ctypes.sizeof(_lib.LsapPlan) == 48
+    assert ctypes.sizeof(_lib.LsapPlan) == 56
 
 
 def test_invalid_arguments_are_rejected_before_any_cuda_call():
@@ -62,7 +62,7 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call():
     # zero-sized output: nothing to do
     assert lib.rfm_cost(None, None, None, None, None, 1, 1, 1, 1, 0, 0, qm, 1.0, 1.0, 1.0, 0.25, None, None) == 0
     plan = _lib.LsapPlan(cols_per_lane=10, max_rows=1, num_problems=3, num_ctas=1, cta_smem_bytes=4096,
-                         tile_cap_floats=0, stride_q=1, stride_t=8, workspace_bytes=0)
+                         tile_cap_floats=0, flags=0, reserved=0, stride_q=1, stride_t=8, workspace_bytes=0)
     assert lib.rfm_lsap(None, None, None, ctypes.byref(plan), None, None, None, None, None) == 1
     assert lib.rfm_lsap(None, None, None, None, None, None, None, None, None) == 1
     plan.cols_per_lane = 7
@@ -95,6 +95,7 @@ def test_planner_modes_and_workspace():
     assert plan.stride_q == 1000 and plan.stride_t == 1 and plan.tile_cap_floats == 16384
     _cta_cover(ctas, 5)
     assert plan.cta_smem_bytes == max(c * s for _, c, s, _ in ctas.tolist())
+    assert plan.flags == 0
     # target-major source (q: 1, t: 4000): tall problems' solver rows are contiguous and are read
     # in place; only the square one (solver rows = queries, strided here) needs scratch
     pr2 = pr.copy()
@@ -104,13 +105,17 @@ def test_planner_modes_and_workspace():
     pr3 = pr.copy()
     plan3, ctas3 = _lib.make_plan(pr3, 1, 4000, tile_cap=0)
     assert plan3.workspace_bytes == 300 * 300 * 4 and ctas3.tolist()[0][1] == 4
-    # small staged tiles share CTAs
+    # small staged tiles share CTAs (query-major source)
     small = np.zeros(9, dtype=_lib.PROBLEM_DTYPE)
     small["num_queries"] = 300
     small["num_targets"] = [12, 12, 10, 9, 8, 8, 8, 8, 3]
-    plan4, ctas4 = _lib.make_plan(small, 1, 4000)
+    plan4, ctas4 = _lib.make_plan(small, 1000, 1)
     _cta_cover(ctas4, 9)
     assert plan4.workspace_bytes == 0 and plan4.num_ctas < 9
+    # every problem row-contiguous: persistent warps, a queue word in the workspace, no CTA table
+    plan5, ctas5 = _lib.make_plan(small.copy(), 1, 4000)
+    assert plan5.flags == _lib.PLAN_PERSISTENT and plan5.num_ctas == 0 and len(ctas5) == 0
+    assert plan5.workspace_bytes == 256 and plan5.cta_smem_bytes % 4 == 0
     wide = np.zeros(1, dtype=_lib.PROBLEM_DTYPE)
     wide["num_queries"] = 64
     wide["num_targets"] = 1025

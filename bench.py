@@ -59,6 +59,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--cpu-images", type=int, default=64, help="images in one CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sharded", action="store_true",
+                    help="also time the strong-scaled sharded sweep (runs by default when N > 1)")
     return ap.parse_args()
 
 
@@ -360,6 +362,11 @@ def run_rfm(args) -> None:
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": float(e2e_t.item()) / args.steps}
 
+    # ---- sharded sweep: ONE 1024-image batch split across the ranks + NCCL all-gather of the pairs
+    sharded_info = None
+    if world > 1 or args.sharded:
+        sharded_info = run_sharded_sweep(args, world, rank, device, barrier)
+
     # ---- roofline of the cost kernel (HBM-bound) and the solver figures
     peak, peak_kind = peak_hbm()
     cb = cost_bytes(wl)
@@ -393,13 +400,52 @@ def run_rfm(args) -> None:
             "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32 cost, fp64 LSAP duals", "data": "synthetic",
             "config": workload_config(wl), "roofline": roofline, "lsap": lsap, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": launches, "clocks": clocks, "impl": "rfm",
+            "gpu_launches": launches, "clocks": clocks, "impl": "rfm", "sharded_sweep": sharded_info,
             "library": _lib.version(), "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms),
                                                   "max": max(step_ms)},
         }
         print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def run_sharded_sweep(args, world: int, rank: int, device, barrier) -> dict:
+    """Strong scaling: the sweep's one 1024-image batch split by image over the ranks, every rank
+    matching its range, then one all-gather of the packed int64 pairs (NCCL over NVLink)."""
+    from rfdetr_training_throughput_b200 import sharded, workloads
+
+    wl = workloads.make(args.workload, images=args.images)  # the same batch on every rank
+    lo, hi = sharded.shard_bounds(wl.images, world)[rank]
+    offs = np.concatenate([[0], np.cumsum(wl.sizes)])
+    logits = wl.pred_logits[:, lo:hi].to(device)
+    boxes = wl.pred_boxes[:, lo:hi].to(device)
+    labels = torch.cat([t["labels"] for t in wl.targets])[offs[lo]:offs[hi]].to(device)
+    tboxes = torch.cat([t["boxes"] for t in wl.targets])[offs[lo]:offs[hi]].to(device)
+
+    def step():
+        return sharded.sharded_match(logits, boxes, labels, tboxes, wl.sizes, wl.group_detr, weights=wl.weights)
+
+    for _ in range(max(args.warmup, 1)):
+        pairs, _per = step()
+    steps = max(1, min(args.steps, 100))
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier()
+    torch.cuda.synchronize(device)
+    for k in range(steps):
+        starts[k].record()
+        pairs, _per = step()
+        ends[k].record()
+    torch.cuda.synchronize(device)
+    barrier()
+    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    total_ms = float(ms.item())
+    return {"images": wl.images, "problems_per_step": wl.num_problems, "steps": steps,
+            "ms_per_step": total_ms / steps, "problems_per_s": wl.num_problems * steps / (total_ms / 1e3),
+            "gathered_pairs": int(pairs.shape[1]), "scaling": "strong",
+            "collective": "all_gather_into_tensor of int64 [2, pairs] per rank" if world > 1 else "none (1 rank)"}
 
 
 def main() -> None:

@@ -12,6 +12,7 @@ rank's chunk is padded to the largest rank's pair count.
 
 from __future__ import annotations
 
+from functools import lru_cache
 from typing import Callable, Sequence
 
 import numpy as np
@@ -37,6 +38,19 @@ def pairs_per_image(sizes: Sequence[int], layers: int, queries: int, group_detr:
     qg = queries // group_detr
     per = group_detr * np.minimum(np.asarray(sizes, dtype=np.int64), qg)
     return np.tile(per, layers)
+
+
+@lru_cache(maxsize=64)
+def _layout(sizes: tuple[int, ...], layers: int, queries: int, group_detr: int, world: int):
+    """Host-only split of a batch: image bounds, pair count per rank, per-(layer, image) counts."""
+    bounds = shard_bounds(len(sizes), world)
+    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    counts, per = [], []
+    for a, b in bounds:
+        pi = pairs_per_image(sizes[a:b], layers, queries, group_detr)
+        counts.append(int(pi.sum()))
+        per.extend(int(x) for x in pi)
+    return bounds, offsets, counts, per
 
 
 def gather_pairs(local_pairs: torch.Tensor, counts: Sequence[int], group=None) -> torch.Tensor:
@@ -68,11 +82,10 @@ def sharded_match(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: t
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    sizes = [int(s) for s in sizes]
-    bounds = shard_bounds(len(sizes), world)
-    lo, hi = bounds[rank]
-    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    sizes = tuple(int(s) for s in sizes)
     layers, nimg_in, queries, _ = pred_logits.shape
+    bounds, offsets, counts, per = _layout(sizes, layers, queries, group_detr, world)
+    lo, hi = bounds[rank]
     if nimg_in == len(sizes):  # whole batch given: slice this rank's images and targets
         pred_logits = pred_logits[:, lo:hi]
         pred_boxes = pred_boxes[:, lo:hi]
@@ -84,14 +97,9 @@ def sharded_match(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: t
     if local_solver is None:
         from .matcher import PackedTargets, match_packed
 
-        res = match_packed(pred_logits, pred_boxes, PackedTargets(labels, boxes, tuple(local_sizes)),
-                           group_detr, weights=weights)
+        res = match_packed(pred_logits, pred_boxes, PackedTargets(labels, boxes, local_sizes), group_detr,
+                           weights=weights)
         local = res.pairs
     else:
-        local = local_solver(pred_logits, pred_boxes, labels, boxes, local_sizes, group_detr)
-    counts = [int(pairs_per_image(sizes[a:b], layers, queries, group_detr).sum()) for a, b in bounds]
-    gathered = gather_pairs(local, counts, group)
-    per = []
-    for a, b in bounds:
-        per.extend(int(x) for x in pairs_per_image(sizes[a:b], layers, queries, group_detr))
-    return gathered, per
+        local = local_solver(pred_logits, pred_boxes, labels, boxes, list(local_sizes), group_detr)
+    return gather_pairs(local, counts, group), per

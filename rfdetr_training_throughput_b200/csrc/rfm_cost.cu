@@ -24,12 +24,17 @@
 // row then starts 16-byte aligned; the caller pads ld and the pad columns are
 // written with 0); any other ld takes a scalar-store variant.
 //
-// Arithmetic.  Every add, subtract and multiply of the box terms is an explicitly
-// rounded float32 operation (scalar, or the packed f32x2 pair with the same
-// per-lane rounding) in the reference chain's order (kernels_matcher.py:98-127);
-// the two GIoU quotients are a * rcp(b), the focal term uses fast exp/log, and
-// the weighted sum is two explicit FMAs (all well inside the 1e-5 relative bar).
-// Both layouts evaluate the same operations and produce bit-identical matrices.
+// Arithmetic.  Every operation is explicitly rounded: scalar add/sub/mul.rn,
+// packed f32x2 ops (same per-lane rounding) and explicit FMAs.  ptxas contracts
+// a packed multiply feeding a packed add into an FMA even with .rn, so every
+// product that is added to something is written as an explicit FMA, in both
+// layouts: union = fma(-iw, ih, area_p + area_t), hull - union, the GIoU
+// difference and the weighted sum.  The L1 and intersection terms follow the
+// reference chain (kernels_matcher.py:98-120); the hull extents use the interval
+// identity max(a1,b1) - min(a0,b0) = (a1-a0) + (b1-b0) - (min(a1,b1) -
+// max(a0,b0)); quotients are a * rcp(b); the focal term uses fast exp/log.  All
+// of it is well inside the 1e-5 relative bar, and both layouts evaluate the same
+// operations, so they produce bit-identical matrices.
 #include "rfm_common.cuh"
 
 namespace rfm {
@@ -70,13 +75,16 @@ __device__ __forceinline__ Corners corners(const float4 b) {
   return c;
 }
 
-// a / b as a * rcp(b): PTX rcp.approx (max error about 1 ulp) and one rounded
-// multiply.  b is never below the 1e-7 clamp, so flushing subnormals is moot.
-__device__ __forceinline__ float quot(float a, float b) {
+// 1 / b by PTX rcp.approx (max error about 1 ulp); quotients are a * rcp(b) with
+// one rounded multiply.  b is never below the 1e-7 clamp, so flushing
+// subnormals is moot.
+__device__ __forceinline__ float rcp_approx(float b) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(b));
-  return __fmul_rn(a, r);
+  return r;
 }
+
+__device__ __forceinline__ float quot(float a, float b) { return __fmul_rn(a, rcp_approx(b)); }
 
 // alpha (1-p)^2 (-logsigmoid(x)) - (1-alpha) p^2 (-logsigmoid(-x)), p = sigmoid(x)
 // (kernels_matcher.py:257-260), with logsigmoid(x) = min(x, 0) - log1p(exp(-|x|)).
@@ -112,13 +120,17 @@ __device__ __forceinline__ float pair_cost(const float4 pb, const Corners& pc, c
   // GIoU with clamped union and hull (kernels_matcher.py:118-127)
   const float iw = __fsub_rn(fminf(pc.x1, tc.x1), fmaxf(pc.x0, tc.x0));
   const float ih = __fsub_rn(fminf(pc.y1, tc.y1), fmaxf(pc.y0, tc.y0));
-  const float inter = __fmul_rn(fmaxf(iw, 0.0f), fmaxf(ih, 0.0f));
-  const float uni = __fsub_rn(__fadd_rn(pc.area, tc.area), inter);
-  const float iou = quot(inter, fmaxf(uni, kBoxEps));
-  const float ew = __fsub_rn(fmaxf(pc.x1, tc.x1), fminf(pc.x0, tc.x0));
-  const float eh = __fsub_rn(fmaxf(pc.y1, tc.y1), fminf(pc.y0, tc.y0));
-  const float hull = __fmul_rn(fmaxf(ew, 0.0f), fmaxf(eh, 0.0f));
-  const float giou = __fsub_rn(iou, quot(__fsub_rn(hull, uni), fmaxf(hull, kBoxEps)));
+  const float iwc = fmaxf(iw, 0.0f);
+  const float ihc = fmaxf(ih, 0.0f);
+  const float inter = __fmul_rn(iwc, ihc);
+  const float uni = __fmaf_rn(-iwc, ihc, __fadd_rn(pc.area, tc.area));
+  // hull extent = width_p + width_t - intersection extent (an identity for intervals)
+  const float ewc = fmaxf(__fsub_rn(__fadd_rn(__fsub_rn(pc.x1, pc.x0), __fsub_rn(tc.x1, tc.x0)), iw), 0.0f);
+  const float ehc = fmaxf(__fsub_rn(__fadd_rn(__fsub_rn(pc.y1, pc.y0), __fsub_rn(tc.y1, tc.y0)), ih), 0.0f);
+  const float hull = __fmul_rn(ewc, ehc);
+  const float gap = __fmaf_rn(ewc, ehc, -uni);
+  const float iou = __fmul_rn(inter, rcp_approx(fmaxf(uni, kBoxEps)));
+  const float giou = __fmaf_rn(-gap, rcp_approx(fmaxf(hull, kBoxEps)), iou);
   return combine(l1, giou, wcls, a);
 }
 
@@ -234,11 +246,13 @@ struct TargetRow {
   int label;
   int image;
   int plain;   // w >= 0, h >= 0 and area >= 2e-7: the clamps are no-ops
+  float tw, th;  // corner extents x1 - x0, y1 - y0
+  float pad0, pad1;
 };
 
 // Prediction data of one pair of queries of one image.
 struct PredPair {
-  float2 cx, cy, w, h, x0, y0, x1, y1, area;
+  float2 cx, cy, w, h, x0, y0, x1, y1, area, pw, ph;
 };
 
 __device__ __forceinline__ PredPair pred_pair(const float4 a, const float4 b) {
@@ -253,7 +267,9 @@ __device__ __forceinline__ PredPair pred_pair(const float4 a, const float4 b) {
   p.y0 = sub2(p.cy, hh);
   p.x1 = add2(p.cx, hw);
   p.y1 = add2(p.cy, hh);
-  p.area = mul2(sub2(p.x1, p.x0), sub2(p.y1, p.y0));
+  p.pw = sub2(p.x1, p.x0);
+  p.ph = sub2(p.y1, p.y0);
+  p.area = mul2(p.pw, p.ph);
   return p;
 }
 
@@ -281,27 +297,25 @@ __device__ __forceinline__ float2 pair_cost2(const PredPair& p, const TargetRow&
                          make_float2(fmaxf(p.x0.x, t.xy.x), fmaxf(p.x0.y, t.xy.x)));
   const float2 ih = sub2(make_float2(fminf(p.y1.x, t.xy.w), fminf(p.y1.y, t.xy.w)),
                          make_float2(fmaxf(p.y0.x, t.xy.y), fmaxf(p.y0.y, t.xy.y)));
-  const float2 inter = mul2(make_float2(fmaxf(iw.x, 0.f), fmaxf(iw.y, 0.f)),
-                            make_float2(fmaxf(ih.x, 0.f), fmaxf(ih.y, 0.f)));
-  const float2 uni = sub2(add2(p.area, dup2(t.area)), inter);
-  const float2 ew = sub2(make_float2(fmaxf(p.x1.x, t.xy.z), fmaxf(p.x1.y, t.xy.z)),
-                         make_float2(fminf(p.x0.x, t.xy.x), fminf(p.x0.y, t.xy.x)));
-  const float2 eh = sub2(make_float2(fmaxf(p.y1.x, t.xy.w), fmaxf(p.y1.y, t.xy.w)),
-                         make_float2(fminf(p.y0.x, t.xy.y), fminf(p.y0.y, t.xy.y)));
-  float2 hull, uc, hc;
-  if (kUnclamped) {
-    hull = mul2(ew, eh);
-    uc = uni;
-    hc = hull;
-  } else {
-    hull = mul2(make_float2(fmaxf(ew.x, 0.f), fmaxf(ew.y, 0.f)),
-                make_float2(fmaxf(eh.x, 0.f), fmaxf(eh.y, 0.f)));
+  const float2 iwc = make_float2(fmaxf(iw.x, 0.f), fmaxf(iw.y, 0.f));
+  const float2 ihc = make_float2(fmaxf(ih.x, 0.f), fmaxf(ih.y, 0.f));
+  const float2 inter = mul2(iwc, ihc);
+  const float2 uni = fma2(make_float2(-iwc.x, -iwc.y), ihc, add2(p.area, dup2(t.area)));
+  // hull extent = width_p + width_t - intersection extent (an identity for intervals)
+  const float2 ew = sub2(add2(p.pw, dup2(t.tw)), iw);
+  const float2 eh = sub2(add2(p.ph, dup2(t.th)), ih);
+  float2 ewc = ew, ehc = eh, uc = uni;
+  if (!kUnclamped) {
+    ewc = make_float2(fmaxf(ew.x, 0.f), fmaxf(ew.y, 0.f));
+    ehc = make_float2(fmaxf(eh.x, 0.f), fmaxf(eh.y, 0.f));
     uc = make_float2(fmaxf(uni.x, kBoxEps), fmaxf(uni.y, kBoxEps));
-    hc = make_float2(fmaxf(hull.x, kBoxEps), fmaxf(hull.y, kBoxEps));
   }
-  const float2 iou = make_float2(quot(inter.x, uc.x), quot(inter.y, uc.y));
-  const float2 gap = sub2(hull, uni);
-  const float2 giou = sub2(iou, make_float2(quot(gap.x, hc.x), quot(gap.y, hc.y)));
+  const float2 hull = mul2(ewc, ehc);
+  const float2 gap = fma2(ewc, ehc, make_float2(-uni.x, -uni.y));
+  float2 hc = hull;
+  if (!kUnclamped) hc = make_float2(fmaxf(hull.x, kBoxEps), fmaxf(hull.y, kBoxEps));
+  const float2 iou = mul2(inter, make_float2(rcp_approx(uc.x), rcp_approx(uc.y)));
+  const float2 giou = fma2(make_float2(-gap.x, -gap.y), make_float2(rcp_approx(hc.x), rcp_approx(hc.y)), iou);
   return fma2(dup2(-a.w_giou), giou, fma2(dup2(a.w_bbox), l1, wcls));
 }
 
@@ -325,46 +339,103 @@ __device__ __forceinline__ void load_raw(PredRaw<NCLS>& r, const CostArgs& a, in
   }
 }
 
+// Costs of targets [c_begin, c_end) of one image run against the thread's four
+// queries, one 16-byte store per target row.
+template <int NCLS, bool kUnclamped, bool kTail>
+__device__ __forceinline__ void cost_targets(const TargetRow* s_t, int c_begin, int c_end, float* out_row,
+                                             const PredPair& p01, const PredPair& p23,
+                                             const float2 (&wcls01)[kSmallClasses],
+                                             const float2 (&wcls23)[kSmallClasses], int q0, int64_t pbase,
+                                             const CostArgs& a) {
+  float* dst = out_row + static_cast<int64_t>(c_begin) * a.ld;
+#pragma unroll 2
+  for (int c = c_begin; c < c_end; ++c, dst += a.ld) {
+    const TargetRow t = s_t[c];
+    float2 w01, w23;
+    if (NCLS > 0) {
+      w01 = wcls01[0];
+      w23 = wcls23[0];
+#pragma unroll
+      for (int cl = 1; cl < NCLS; ++cl) {
+        w01 = t.label == cl ? wcls01[cl] : w01;
+        w23 = t.label == cl ? wcls23[cl] : w23;
+      }
+    } else {
+      float f[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int q = q0 + k < a.Q ? q0 + k : a.Q - 1;
+        f[k] = __fmul_rn(a.w_class, focal_cost(__ldg(a.logits + (pbase + q) * a.C + t.label), a.alpha,
+                                               a.one_minus_alpha));
+      }
+      w01 = make_float2(f[0], f[1]);
+      w23 = make_float2(f[2], f[3]);
+    }
+    float2 r01 = pair_cost2<kUnclamped>(p01, t, w01, a);
+    float2 r23 = pair_cost2<kUnclamped>(p23, t, w23, a);
+    if (kTail && q0 + 4 > a.Q) {  // zero the pad queries of the last tile
+      if (q0 + 1 >= a.Q) r01.y = 0.f;
+      if (q0 + 2 >= a.Q) r23.x = 0.f;
+      if (q0 + 3 >= a.Q) r23.y = 0.f;
+    }
+    *reinterpret_cast<float4*>(dst) = make_float4(r01.x, r01.y, r23.x, r23.y);
+  }
+}
+
 template <int NCLS>
 __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs a) {
   __shared__ TargetRow s_t[kTmCols];
   __shared__ int s_seg[kTmCols + 1];
   __shared__ int s_nseg;
+  __shared__ int s_all_plain;
   const int layer = blockIdx.z;
   const int c_begin = blockIdx.x * kTmCols;
   const int n = min(kTmCols, a.S - c_begin);
   const int tid = threadIdx.x;
 
-  // stage this CTA's targets and split them into runs of one image
+  // stage this CTA's targets ...
+  for (int c = tid; c < n; c += kTmThreads) {
+    const int col = c_begin + c;
+    TargetRow t;
+    t.box = __ldg(a.tboxes + col);
+    const Corners cn = corners(t.box);
+    t.xy = make_float4(cn.x0, cn.y0, cn.x1, cn.y1);
+    t.area = cn.area;
+    const int64_t raw = __ldg(a.labels + col);
+    t.label = static_cast<int>(raw < 0 ? 0 : (raw >= a.C ? a.C - 1 : raw));
+    t.image = image_of(a.offsets, a.B, col);
+    t.plain = (t.box.z >= 0.0f && t.box.w >= 0.0f && cn.area >= 2e-7f) ? 1 : 0;
+    t.tw = __fsub_rn(cn.x1, cn.x0);
+    t.th = __fsub_rn(cn.y1, cn.y0);
+    t.pad0 = 0.0f;
+    t.pad1 = 0.0f;
+    s_t[c] = t;
+  }
+  __syncthreads();
+  // ... and split them into runs of one image (warp 0)
   if (tid < 32) {
-    int img = -1;
-    if (tid < n) {
-      const int col = c_begin + tid;
-      img = image_of(a.offsets, a.B, col);
-      TargetRow t;
-      t.box = __ldg(a.tboxes + col);
-      const Corners c = corners(t.box);
-      t.xy = make_float4(c.x0, c.y0, c.x1, c.y1);
-      t.area = c.area;
-      const int64_t raw = __ldg(a.labels + col);
-      t.label = static_cast<int>(raw < 0 ? 0 : (raw >= a.C ? a.C - 1 : raw));
-      t.image = img;
-      t.plain = (t.box.z >= 0.0f && t.box.w >= 0.0f && c.area >= 2e-7f) ? 1 : 0;
-      s_t[tid] = t;
+    int count = 0;
+    bool every = true;
+    for (int base0 = 0; base0 < n; base0 += 32) {
+      const int c = base0 + tid;
+      const bool in = c < n;
+      const bool start = in && (c == 0 || s_t[c].image != s_t[c - 1].image);
+      const unsigned starts = __ballot_sync(kFullMask, start);
+      if (start) s_seg[count + __popc(starts & ((1u << tid) - 1u))] = c;
+      count += __popc(starts);
+      every = __all_sync(kFullMask, !in || s_t[c].plain) && every;
     }
-    const int prev = __shfl_up_sync(kFullMask, img, 1);
-    const bool start = tid < n && (tid == 0 || prev != img);
-    const unsigned starts = __ballot_sync(kFullMask, start);
-    if (start) s_seg[__popc(starts & ((1u << tid) - 1u))] = tid;
     if (tid == 0) {
-      s_nseg = __popc(starts);
-      s_seg[__popc(starts)] = n;
+      s_nseg = count;
+      s_seg[count] = n;
+      s_all_plain = every ? 1 : 0;
     }
   }
   __syncthreads();
   const int q0 = (blockIdx.y * kTmThreads + tid) * 4;
   if (q0 >= a.ld) return;
   const int nseg = s_nseg;
+  const bool all_plain = s_all_plain != 0;
   const int64_t layer_base = static_cast<int64_t>(layer) * a.B;
 
   PredRaw<NCLS> raw;
@@ -394,44 +465,14 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
     if (sg + 1 < nseg) {
       load_raw<NCLS>(raw, a, (layer_base + s_t[s_seg[sg + 1]].image) * a.Q, q0);
     }
-    const int c_end = s_seg[sg + 1];
-    for (int c = s_seg[sg]; c < c_end; ++c) {
-      const TargetRow t = s_t[c];
-      float2 w01, w23;
-      if (NCLS > 0) {
-        w01 = wcls01[0];
-        w23 = wcls23[0];
-#pragma unroll
-        for (int cl = 1; cl < NCLS; ++cl) {
-          w01 = t.label == cl ? wcls01[cl] : w01;
-          w23 = t.label == cl ? wcls23[cl] : w23;
-        }
-      } else {
-        float f[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int q = q0 + k < a.Q ? q0 + k : a.Q - 1;
-          f[k] = __fmul_rn(a.w_class, focal_cost(__ldg(a.logits + (pbase + q) * a.C + t.label),
-                                                 a.alpha, a.one_minus_alpha));
-        }
-        w01 = make_float2(f[0], f[1]);
-        w23 = make_float2(f[2], f[3]);
-      }
-      float2 r01, r23;
-      if (preds_plain && t.plain) {
-        r01 = pair_cost2<true>(p01, t, w01, a);
-        r23 = pair_cost2<true>(p23, t, w23, a);
-      } else {
-        r01 = pair_cost2<false>(p01, t, w01, a);
-        r23 = pair_cost2<false>(p23, t, w23, a);
-      }
-      if (q0 + 4 > a.Q) {  // zero the pad queries of the last tile
-        if (q0 + 1 >= a.Q) r01.y = 0.f;
-        if (q0 + 2 >= a.Q) r23.x = 0.f;
-        if (q0 + 3 >= a.Q) r23.y = 0.f;
-      }
-      *reinterpret_cast<float4*>(out_row + static_cast<int64_t>(c) * a.ld) =
-          make_float4(r01.x, r01.y, r23.x, r23.y);
+    // one uniform choice per image run: clamp-free when every box of the run is
+    // plain, pad-query zeroing only in the last query tile
+    if (preds_plain && all_plain && q0 + 4 <= a.Q) {
+      cost_targets<NCLS, true, false>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, p23, wcls01, wcls23,
+                                      q0, pbase, a);
+    } else {
+      cost_targets<NCLS, false, true>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, p23, wcls01, wcls23,
+                                      q0, pbase, a);
     }
   }
 }

@@ -48,6 +48,8 @@
 #include <math_constants.h>
 
 #include <climits>
+#include <mutex>
+#include <vector>
 
 #include "rfm_common.cuh"
 
@@ -619,7 +621,7 @@ int sm_count() {
 }
 
 // CTAs of the pair-mode kernel that fit on one SM at this shared-memory size.
-int resident_ctas(int cols_per_lane, int64_t smem) {
+int query_resident_ctas(int cols_per_lane, int64_t smem) {
   const void* fn = nullptr;
   switch (cols_per_lane) {
     case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, false>); break;
@@ -637,6 +639,35 @@ int resident_ctas(int cols_per_lane, int64_t smem) {
                                                     static_cast<size_t>(smem)) != cudaSuccess) {
     cudaGetLastError();
     return 0;
+  }
+  return n;
+}
+
+// query_resident_ctas() memoised per (device, columns per lane, shared memory): the
+// occupancy query and the attribute call cost a few microseconds per launch.
+struct OccupancyEntry {
+  int device, cols_per_lane;
+  int64_t smem;
+  int ctas;
+};
+std::mutex g_occupancy_mutex;
+std::vector<OccupancyEntry> g_occupancy;
+
+int resident_ctas(int cols_per_lane, int64_t smem) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  {
+    std::lock_guard<std::mutex> lock(g_occupancy_mutex);
+    for (const OccupancyEntry& e : g_occupancy)
+      if (e.device == dev && e.cols_per_lane == cols_per_lane && e.smem == smem) return e.ctas;
+  }
+  const int n = query_resident_ctas(cols_per_lane, smem);
+  if (n > 0) {
+    std::lock_guard<std::mutex> lock(g_occupancy_mutex);
+    g_occupancy.push_back({dev, cols_per_lane, smem, n});
   }
   return n;
 }
@@ -923,8 +954,6 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
 // be cleared between calls.  All calls share this one buffer: calls whose work
 // overlaps on the GPU (for instance on two streams at once) race on it.
 static __device__ __align__(256) float g_noalloc_scratch[RFM_NOALLOC_SCRATCH_BYTES / sizeof(float)];
-
-#include <mutex>
 
 namespace {
 constexpr int kNoAllocMaxDevices = 64;

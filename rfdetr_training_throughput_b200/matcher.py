@@ -33,7 +33,7 @@ from __future__ import annotations
 
 import ctypes
 from collections import OrderedDict
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Any, Sequence
 
 import numpy as np
@@ -80,6 +80,12 @@ class PackedTargets:
     labels: torch.Tensor
     boxes: torch.Tensor
     sizes: tuple[int, ...]
+    total: int = field(init=False, repr=False)
+
+    def __post_init__(self) -> None:
+        if type(self.sizes) is not tuple or not all(type(s) is int for s in self.sizes):
+            self.sizes = tuple(int(s) for s in self.sizes)
+        self.total = sum(self.sizes)
 
     @staticmethod
     def from_list(targets: Sequence[dict], device: torch.device | None = None) -> "PackedTargets":
@@ -98,12 +104,16 @@ class PackedTargets:
     def checked(self) -> "PackedTargets":
         _require_cuda(self.labels, "labels")
         _require_cuda(self.boxes, "boxes")
-        total = sum(self.sizes)
+        total = self.total
         if self.labels.shape != (total,) or self.boxes.shape != (total, 4):
             raise ValueError("packed targets do not match their sizes")
         labels = self.labels if self.labels.dtype == torch.int64 else self.labels.long()
         boxes = self.boxes if self.boxes.dtype == torch.float32 else self.boxes.float()
-        return PackedTargets(labels.contiguous(), _aligned16(boxes.contiguous()), self.sizes)
+        labels = labels.contiguous()
+        boxes = _aligned16(boxes.contiguous())
+        if labels is self.labels and boxes is self.boxes:
+            return self
+        return PackedTargets(labels, boxes, self.sizes)
 
 
 class MatchResult:
@@ -219,11 +229,24 @@ def build_problems(sizes: Sequence[int], layers: int, queries: int, group_detr: 
 
 
 class _PlanCache:
+    """LRU of step plans keyed by sizes and shape; the last hit is also kept by the
+    identity of its sizes tuple, so a training loop that reuses one sizes object
+    skips hashing it."""
+
     def __init__(self, capacity: int = 64):
         self.capacity = capacity
         self._d: OrderedDict[tuple, StepPlan] = OrderedDict()
+        self._last: tuple | None = None  # (sizes object, rest of the key, plan)
 
     def get(self, key: tuple, make) -> StepPlan:
+        last = self._last
+        if last is not None and last[0] is key[0] and last[1] == key[1:]:
+            return last[2]
+        hit = self._get(key, make)
+        self._last = (key[0], key[1:], hit)
+        return hit
+
+    def _get(self, key: tuple, make) -> StepPlan:
         hit = self._d.get(key)
         if hit is not None:
             self._d.move_to_end(key)
@@ -236,6 +259,7 @@ class _PlanCache:
 
     def clear(self) -> None:
         self._d.clear()
+        self._last = None
 
 
 _PLANS = _PlanCache()
@@ -245,7 +269,8 @@ def plan_step(sizes: Sequence[int], layers: int, queries: int, group_detr: int, 
               device: torch.device, layout: int = _lib.LAYOUT_QUERY_MAJOR,
               tile_cap: int | None = None) -> StepPlan:
     """Cached host planning plus ONE non-blocking pinned upload of descriptors and offsets."""
-    sizes = tuple(int(s) for s in sizes)
+    if type(sizes) is not tuple:
+        sizes = tuple(int(s) for s in sizes)
     cap = _lib.default_tile_cap() if tile_cap is None else int(tile_cap)
     key = (sizes, layers, queries, group_detr, ld, layout, cap, str(device))
 
@@ -300,7 +325,8 @@ def _prepare_predictions(logits: torch.Tensor, boxes: torch.Tensor) -> tuple[tor
 
 
 def launch_cost(logits: torch.Tensor, boxes: torch.Tensor, labels: torch.Tensor, tgt_boxes: torch.Tensor,
-                offsets_ptr: int, sum_t: int, ld: int, layout: int, weights: dict, out: torch.Tensor) -> None:
+                offsets_ptr: int, sum_t: int, ld: int, layout: int, weights: dict, out: torch.Tensor,
+                stream: ctypes.c_void_p | None = None) -> None:
     """Enqueue ``rfm_cost`` for logits [L,B,Q,C] / boxes [L,B,Q,4] into ``out``."""
     layers, nimg, queries, ncls = logits.shape
     lib = _lib.load()
@@ -308,10 +334,11 @@ def launch_cost(logits: torch.Tensor, boxes: torch.Tensor, labels: torch.Tensor,
         _ptr(logits), _ptr(boxes), _ptr(labels), _ptr(tgt_boxes), ctypes.c_void_p(offsets_ptr),
         layers, nimg, queries, ncls, sum_t, ld, layout,
         float(weights["cost_class"]), float(weights["cost_bbox"]), float(weights["cost_giou"]),
-        float(weights["focal_alpha"]), _ptr(out), _stream_handle(out.device)))
+        float(weights["focal_alpha"]), _ptr(out), _stream_handle(out.device) if stream is None else stream))
 
 
-def launch_lsap(cost: torch.Tensor, plan: StepPlan, pairs: torch.Tensor, status: torch.Tensor | None) -> None:
+def launch_lsap(cost: torch.Tensor, plan: StepPlan, pairs: torch.Tensor, status: torch.Tensor | None,
+                stream: ctypes.c_void_p | None = None) -> None:
     """Enqueue ``rfm_lsap`` over a planned step; ``pairs`` is int64 [2, total_pairs]."""
     lib = _lib.load()
     ws = None
@@ -319,7 +346,8 @@ def launch_lsap(cost: torch.Tensor, plan: StepPlan, pairs: torch.Tensor, status:
         ws = torch.empty(int(plan.plan.workspace_bytes), dtype=torch.uint8, device=cost.device)
     _lib.check("rfm_lsap", lib.rfm_lsap(
         _ptr(cost), ctypes.c_void_p(plan.problems_ptr), ctypes.c_void_p(plan.ctas_ptr), ctypes.byref(plan.plan),
-        _ptr(pairs[0]), _ptr(pairs[1]), _ptr(status), _ptr(ws), _stream_handle(cost.device)))
+        _ptr(pairs[0]), _ptr(pairs[1]), _ptr(status), _ptr(ws),
+        _stream_handle(cost.device) if stream is None else stream))
 
 
 def raise_on_status(status: torch.Tensor) -> None:
@@ -360,20 +388,21 @@ def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: P
     layers, nimg, queries, _ = logits.shape
     if len(tg.sizes) != nimg:
         raise ValueError(f"{len(tg.sizes)} targets for a batch of {nimg} images")
-    sum_t = sum(tg.sizes)
+    sum_t = tg.total
     ld = _round4(queries)
     layout = _lib.LAYOUT_TARGET_MAJOR
     plan = plan_step(tg.sizes, layers, queries, group_detr, ld, device, layout)
     cost = torch.empty((layers, sum_t, ld), dtype=torch.float32, device=device)
     pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=device)
     status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=device) if check_status else None
+    stream = _stream_handle(device)
     if sum_t > 0:
         _record(events, "cost")
-        launch_cost(logits, boxes, tg.labels, tg.boxes, plan.offsets_ptr, sum_t, ld, layout, w, cost)
+        launch_cost(logits, boxes, tg.labels, tg.boxes, plan.offsets_ptr, sum_t, ld, layout, w, cost, stream)
         _record(events, "cost")
     if plan.problems.shape[0] > 0:
         _record(events, "lsap")
-        launch_lsap(cost, plan, pairs, status)
+        launch_lsap(cost, plan, pairs, status, stream)
         _record(events, "lsap")
     if status is not None:
         raise_on_status(status)

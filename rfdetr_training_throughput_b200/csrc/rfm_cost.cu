@@ -134,9 +134,9 @@ __device__ __forceinline__ float pair_cost(const float4 pb, const Corners& pc, c
   return combine(l1, giou, wcls, a);
 }
 
-// Largest image b with offsets[b] <= col (images with no targets are skipped).
-__device__ __forceinline__ int image_of(const int32_t* offsets, int B, int col) {
-  int lo = 0, hi = B;
+// Largest image b in [lo, hi) with offsets[b] <= col, given offsets[lo] <= col
+// < offsets[hi] (images with no targets are skipped).
+__device__ __forceinline__ int image_in_range(const int32_t* offsets, int lo, int hi, int col) {
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (__ldg(offsets + mid) <= col) {
@@ -148,9 +148,59 @@ __device__ __forceinline__ int image_of(const int32_t* offsets, int B, int col) 
   return lo;
 }
 
+// Image lookup for a CTA whose targets start at `first`.  The CTA narrows the
+// image of `first` with a 128-way search (no round at all for B <= 128: each
+// round is one load per thread, against the ten dependent loads of a binary
+// search over 1024 images), then stages offsets[lo .. lo + kImageWindow] in
+// shared memory; image_in_window() answers from there.  Needs >= 128 threads,
+// called by all of them.
+constexpr int kImageWindow = 128;
+
+__device__ __forceinline__ int stage_image_window(const int32_t* offsets, int B, int first, int* s_off,
+                                                  int tid, int nthreads) {
+  int lo = 0, hi = B;  // offsets[lo] <= first < offsets[hi] = S
+  while (hi - lo > kImageWindow) {
+    const int stride = (hi - lo + kImageWindow - 1) / kImageWindow;
+    const int idx = lo + tid * stride;
+    const int below = tid < kImageWindow && idx < hi && __ldg(offsets + idx) <= first;
+    const int count = __syncthreads_count(below);  // a prefix of the probes: offsets are sorted
+    lo += (count - 1) * stride;
+    hi = min(hi, lo + stride);
+  }
+  for (int e = tid; e <= kImageWindow; e += nthreads) s_off[e] = __ldg(offsets + min(lo + e, B));
+  __syncthreads();
+  return lo;
+}
+
+// Image of target `col` >= first; past the window (more than kImageWindow
+// images, most of them empty, before col) it searches global memory.
+__device__ __forceinline__ int image_in_window(const int* s_off, int lo, const int32_t* offsets, int B,
+                                               int col) {
+  if (lo + kImageWindow < B && col >= s_off[kImageWindow]) {
+    return image_in_range(offsets, lo + kImageWindow, B, col);
+  }
+  int l = 0, h = min(kImageWindow, B - lo);  // s_off[l] <= col < s_off[h]
+  while (h - l > 1) {
+    const int mid = (l + h) >> 1;
+    if (s_off[mid] <= col) {
+      l = mid;
+    } else {
+      h = mid;
+    }
+  }
+  return lo + l;
+}
+
 template <bool kVec>
 __global__ void __launch_bounds__(kThreads) cost_qmajor_kernel(const CostArgs a) {
+  __shared__ int s_off[kImageWindow + 1];
   const int64_t col0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  const int64_t cta_col = static_cast<int64_t>(blockIdx.x) * blockDim.x * 4;
+  const int tid = threadIdx.y * blockDim.x + threadIdx.x;
+  int win_lo = 0;
+  if (cta_col < a.S) {  // uniform across the CTA
+    win_lo = stage_image_window(a.offsets, a.B, static_cast<int>(cta_col), s_off, tid, kThreads);
+  }
   if (col0 >= a.ld) return;
   const int layer = blockIdx.z;
   const int q_begin = blockIdx.y * a.rows_per_cta;
@@ -165,7 +215,7 @@ __global__ void __launch_bounds__(kThreads) cost_qmajor_kernel(const CostArgs a)
     const int64_t col = col0 + c;
     valid[c] = col < a.S;
     if (valid[c]) {
-      image[c] = image_of(a.offsets, a.B, static_cast<int>(col));
+      image[c] = image_in_window(s_off, win_lo, a.offsets, a.B, static_cast<int>(col));
       tb[c] = __ldg(a.tboxes + col);
       const int64_t raw = __ldg(a.labels + col);
       label[c] = static_cast<int>(raw < 0 ? 0 : (raw >= a.C ? a.C - 1 : raw));
@@ -388,28 +438,43 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
   __shared__ int s_seg[kTmCols + 1];
   __shared__ int s_nseg;
   __shared__ int s_all_plain;
+  __shared__ int s_off[kImageWindow + 1];
   const int layer = blockIdx.z;
   const int c_begin = blockIdx.x * kTmCols;
   const int n = min(kTmCols, a.S - c_begin);
   const int tid = threadIdx.x;
+  static_assert(kTmCols <= kTmThreads, "one staged target per thread");
+  // this thread's target is requested first; its latency overlaps the image search
+  const bool has_target = tid < n;
+  float4 tbox = make_float4(0.f, 0.f, 0.f, 0.f);
+  int64_t tlabel = 0;
+  if (has_target) {
+    tbox = __ldg(a.tboxes + c_begin + tid);
+    tlabel = __ldg(a.labels + c_begin + tid);
+  }
+  const int win_lo = stage_image_window(a.offsets, a.B, c_begin, s_off, tid, kTmThreads);
+  const int q0 = (blockIdx.y * kTmThreads + tid) * 4;
+  const int64_t layer_base = static_cast<int64_t>(layer) * a.B;
+  // the first run's predictions are requested before the targets are staged
+  PredRaw<NCLS> raw;
+  load_raw<NCLS>(raw, a, (layer_base + image_in_window(s_off, win_lo, a.offsets, a.B, c_begin)) * a.Q, q0);
 
   // stage this CTA's targets ...
-  for (int c = tid; c < n; c += kTmThreads) {
-    const int col = c_begin + c;
+  if (has_target) {
+    const int col = c_begin + tid;
     TargetRow t;
-    t.box = __ldg(a.tboxes + col);
+    t.box = tbox;
     const Corners cn = corners(t.box);
     t.xy = make_float4(cn.x0, cn.y0, cn.x1, cn.y1);
     t.area = cn.area;
-    const int64_t raw = __ldg(a.labels + col);
-    t.label = static_cast<int>(raw < 0 ? 0 : (raw >= a.C ? a.C - 1 : raw));
-    t.image = image_of(a.offsets, a.B, col);
+    t.label = static_cast<int>(tlabel < 0 ? 0 : (tlabel >= a.C ? a.C - 1 : tlabel));
+    t.image = image_in_window(s_off, win_lo, a.offsets, a.B, col);
     t.plain = (t.box.z >= 0.0f && t.box.w >= 0.0f && cn.area >= 2e-7f) ? 1 : 0;
     t.tw = __fsub_rn(cn.x1, cn.x0);
     t.th = __fsub_rn(cn.y1, cn.y0);
     t.pad0 = 0.0f;
     t.pad1 = 0.0f;
-    s_t[c] = t;
+    s_t[tid] = t;
   }
   __syncthreads();
   // ... and split them into runs of one image (warp 0)
@@ -432,14 +497,9 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
     }
   }
   __syncthreads();
-  const int q0 = (blockIdx.y * kTmThreads + tid) * 4;
   if (q0 >= a.ld) return;
   const int nseg = s_nseg;
   const bool all_plain = s_all_plain != 0;
-  const int64_t layer_base = static_cast<int64_t>(layer) * a.B;
-
-  PredRaw<NCLS> raw;
-  load_raw<NCLS>(raw, a, (layer_base + s_t[0].image) * a.Q, q0);
   float* out_row = a.out + (static_cast<int64_t>(layer) * a.S + c_begin) * a.ld + q0;
   for (int sg = 0; sg < nseg; ++sg) {
     const int img = s_t[s_seg[sg]].image;

@@ -61,6 +61,10 @@ constexpr int kSmemPerCtaReserved = 1024;
 constexpr int kSmemPerBlockMax = 227 * 1024;
 constexpr int64_t kTileCapDefault = 16384;  // floats: 64 KB of staged cost per warp
 constexpr int kMaxWarpsPerCta = 4;
+// Register budget of the instantiations up to 320 columns: four CTAs of four
+// warps per SM (at most 128 registers a thread); the 1024-column one keeps its
+// per-lane arrays in registers instead.
+__host__ __device__ constexpr int min_ctas_per_sm(int cols_per_lane) { return cols_per_lane <= 10 ? 4 : 1; }
 // Shared-memory budget of one CTA: four CTAs of four warps fill an SM.
 constexpr int kCtaBudget = kSmemPerSm / 4 - kSmemPerCtaReserved;
 // Tie keys: a free column at position pos gets kKeyBase - 1 - pos, a matched one
@@ -168,8 +172,6 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;\n" ::: "memory");
 }
 
-__device__ __forceinline__ bool invalid_cost(float x) { return (x != x) || (x == -CUDART_INF_F); }
-
 template <int K>
 __device__ __forceinline__ void set_key(unsigned (&key)[K], int k_sel, unsigned value) {
 #pragma unroll
@@ -188,18 +190,22 @@ __device__ __forceinline__ float load_cost(const float* p) {
   return __ldcg(p);
 }
 
-// One scan step of the augmenting-path search over the lane's columns.
+// One scan step of the augmenting-path search over the lane's columns.  The
+// lane's loads are all issued before the first is used (a row read from
+// global memory then costs one round trip, not one per column).
 template <int K, int L>
 __device__ __forceinline__ void scan_row(const float* row, int lane, int i, double minv, double ui,
                                          const double (&v)[K], double (&spc)[K],
                                          const unsigned (&key)[K], unsigned rem, int16_t* path_s,
                                          double& bv, unsigned& bk) {
+  float cf[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) cf[k] = (rem & (1u << k)) ? load_cost<L>(row + lane + 32 * k) : 0.0f;
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     if (rem & (1u << k)) {
       const int j = lane + 32 * k;
-      const float cf = load_cost<L>(row + j);
-      const double r = ((minv + static_cast<double>(cf)) - ui) - v[k];
+      const double r = ((minv + static_cast<double>(cf[k])) - ui) - v[k];
       if (r < spc[k]) {
         spc[k] = r;
         path_s[j] = static_cast<int16_t>(i);
@@ -213,6 +219,7 @@ __device__ __forceinline__ void scan_row(const float* row, int lane, int i, doub
 }
 
 
+
 // Order-preserving map of a float (NaN excluded) onto uint32.
 __device__ __forceinline__ unsigned ordered32(float x) {
   const unsigned b = __float_as_uint(x);
@@ -223,30 +230,34 @@ __device__ __forceinline__ float from_ordered32(unsigned o) {
   return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
 }
 
+// NaN-propagating minimum (PTX min.NaN): a NaN operand makes the result NaN.
+__device__ __forceinline__ float min_nan(float x, float y) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(x), "f"(y));
+  return r;
+}
+
 // First pick of one row when every column is free and v = 0: the smallest
 // cost, ties to the smallest column; lane 0 records it (column -1 when the
-// row's minimum is +inf, which leaves the row to the full search).
+// row's minimum is +inf, which leaves the row to the full search).  Entries
+// past the row end hold +inf.  A row holding NaN is flagged by the caller's
+// check and never solved, so whatever it records here is unused.
 template <int K>
-__device__ __forceinline__ void record_first_pick(const float (&x)[K], unsigned valid, int lane,
-                                                  int nc, int row, double* pick_m_s,
-                                                  int16_t* pick_w_s) {
-  float bvf = CUDART_INF_F;
-  int bj = 0xffff;
+__device__ __forceinline__ void record_first_pick(const float (&x)[K], int lane, int nc, int row,
+                                                  double* pick_m_s, int16_t* pick_w_s) {
+  float m = x[0];
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const float c = x[k] + 0.0f;  // -0 and +0 tie, as the doubles (0 + c) do
-    if (((valid >> k) & 1u) && c < bvf) {
-      bvf = c;
-      bj = lane + 32 * k;
-    }
-  }
-  const unsigned o = ordered32(bvf);
+  for (int k = 1; k < K; ++k) m = fminf(m, x[k]);
+  unsigned bj = 0xffffu;
+#pragma unroll
+  for (int k = K - 1; k >= 0; --k) bj = x[k] == m ? static_cast<unsigned>(lane + 32 * k) : bj;
+  const unsigned o = ordered32(m + 0.0f);  // -0 and +0 tie, as the doubles (0 + c) do
   const unsigned mo = __reduce_min_sync(kFullMask, o);
-  const unsigned mj = __reduce_min_sync(kFullMask, o == mo ? static_cast<unsigned>(bj) : 0xffffu);
+  const unsigned mj = __reduce_min_sync(kFullMask, o == mo ? bj : 0xffffu);
   if (lane == 0) {
-    const float m = from_ordered32(mo);
-    pick_m_s[row] = static_cast<double>(m);
-    pick_w_s[row] = static_cast<int16_t>(m == CUDART_INF_F || mj >= static_cast<unsigned>(nc) ? -1 : static_cast<int>(mj));
+    const float mf = from_ordered32(mo);
+    pick_m_s[row] = static_cast<double>(mf);
+    pick_w_s[row] = static_cast<int16_t>(mf == CUDART_INF_F || mj >= static_cast<unsigned>(nc) ? -1 : static_cast<int>(mj));
   }
 }
 
@@ -328,6 +339,9 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
   bool bad = false;
   const float* rows = src;  // solver row i starts at rows + i * row_pitch
   int64_t row_pitch = s.rs;
+  // chk: running NaN-propagating minimum of every entry; NaN or -inf in the
+  // tile leaves it below -inf's successor (or NaN), which SciPy rejects
+  float chk = CUDART_INF_F;
   if (s.cs == 1) {
     // solver rows are contiguous in the source: one coalesced pass over them
     for (int i = 0; i < nr; i += 2) {
@@ -336,23 +350,23 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         const int j = lane + 32 * k;
-        const bool ok = (valid >> k) & 1u;
-        x0[k] = ok ? __ldg(src + i * s.rs + j) : CUDART_INF_F;
-        x1[k] = (ok && two) ? __ldg(src + (i + 1) * s.rs + j) : CUDART_INF_F;
+        x0[k] = j < nc ? __ldg(src + i * s.rs + j) : CUDART_INF_F;
+        x1[k] = (j < nc && two) ? __ldg(src + (i + 1) * s.rs + j) : CUDART_INF_F;
       }
 #pragma unroll
-      for (int k = 0; k < K; ++k) {
-        if ((valid >> k) & 1u) {
+      for (int k = 0; k < K; ++k) chk = min_nan(chk, min_nan(x0[k], x1[k]));
+      if (mode == kModeShared) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
           const int j = lane + 32 * k;
-          bad |= invalid_cost(x0[k]) || (two && invalid_cost(x1[k]));
-          if (mode == kModeShared) {
+          if (j < nc) {
             tile[i * nc + j] = x0[k];
             if (two) tile[(i + 1) * nc + j] = x1[k];
           }
         }
       }
-      record_first_pick<K>(x0, valid, lane, nc, i, pick_m_s, pick_w_s);
-      if (two) record_first_pick<K>(x1, valid, lane, nc, i + 1, pick_m_s, pick_w_s);
+      record_first_pick<K>(x0, lane, nc, i, pick_m_s, pick_w_s);
+      if (two) record_first_pick<K>(x1, lane, nc, i + 1, pick_m_s, pick_w_s);
     }
     if (mode == kModeShared) {
       rows = tile;
@@ -386,13 +400,13 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         const int j = lane + 32 * k;
-        const bool ok = (valid >> k) & 1u;
-        x[k] = !ok ? CUDART_INF_F : (mode == kModeShared ? rows[i * nc + j] : __ldcg(rows + i * nc + j));
-        bad |= ok && invalid_cost(x[k]);
+        x[k] = j >= nc ? CUDART_INF_F : (mode == kModeShared ? rows[i * nc + j] : __ldcg(rows + i * nc + j));
+        chk = min_nan(chk, x[k]);
       }
-      record_first_pick<K>(x, valid, lane, nc, i, pick_m_s, pick_w_s);
+      record_first_pick<K>(x, lane, nc, i, pick_m_s, pick_w_s);
     }
   }
+  bad = !(chk > -CUDART_INF_F);
   bad = __any_sync(kFullMask, bad);
 
   unsigned freem = valid;
@@ -568,7 +582,7 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
 }
 
 template <int K, bool kDense>
-__global__ void __launch_bounds__(32 * kMaxWarpsPerCta) lsap_kernel(const LsapArgs a) {
+__global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K)) lsap_kernel(const LsapArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;

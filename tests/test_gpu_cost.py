@@ -104,3 +104,27 @@ def test_empty_targets():
                 "boxes": torch.zeros(0, 4, device=dev)} for _ in range(2)]
     out = matcher.compute_compact_detection_cost_matrix(wl.outputs_list(dev)[0], targets, weights=wl.weights)
     assert out.shape == (wl.queries, 0)
+
+
+def test_image_lookup_across_many_empty_images():
+    """Targets of one CTA spread over hundreds of images, most of them empty: the
+    shared window of image offsets and its global-memory fallback both give each
+    target its own image's predictions (both layouts, against the oracle)."""
+    rng = np.random.default_rng(7)
+    nimg, queries = 700, 8
+    sizes = np.zeros(nimg, dtype=np.int64)
+    sizes[[0, 1, 130, 131, 300, 450, 451, 699]] = [2, 1, 3, 1, 2, 1, 4, 2]
+    logits = rng.normal(0.0, 1.5, (1, nimg, queries, 2)).astype(np.float32)
+    boxes = (1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.0, (1, nimg, queries, 4))))).astype(np.float32)
+    labels = [rng.integers(0, 2, int(t)).astype(np.int64) for t in sizes]
+    tboxes = [np.concatenate([rng.uniform(0.1, 0.9, (int(t), 2)), rng.uniform(0.02, 0.5, (int(t), 2))],
+                             axis=1).astype(np.float32) for t in sizes]
+    w = dict(cost_class=2.0, cost_bbox=5.0, cost_giou=2.0, focal_alpha=0.25)
+    ref = ocost.compact_cost(logits, boxes, labels, tboxes, **w)
+    gpu = _gpu_cost(logits, boxes, labels, tboxes, w)
+    _assert_close(gpu, ref)
+    dev = torch.device("cuda")
+    outputs = [{"pred_logits": torch.as_tensor(logits[0], device=dev),
+                "pred_boxes": torch.as_tensor(boxes[0], device=dev)}]
+    _, tmajor = matcher.match_layers(outputs, to_targets(labels, tboxes, dev), 1, weights=w, return_cost=True)
+    assert torch.equal(tmajor.cpu(), torch.as_tensor(gpu).reshape(tmajor.shape))

@@ -422,8 +422,10 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier) -> dict:
     labels = torch.cat([t["labels"] for t in wl.targets])[offs[lo]:offs[hi]].to(device)
     tboxes = torch.cat([t["boxes"] for t in wl.targets])[offs[lo]:offs[hi]].to(device)
 
+    sizes = tuple(wl.sizes)
+
     def step():
-        return sharded.sharded_match(logits, boxes, labels, tboxes, wl.sizes, wl.group_detr, weights=wl.weights)
+        return sharded.sharded_match(logits, boxes, labels, tboxes, sizes, wl.group_detr, weights=wl.weights)
 
     for _ in range(max(args.warmup, 1)):
         pairs, _per = step()

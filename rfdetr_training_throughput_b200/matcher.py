@@ -87,6 +87,15 @@ class PackedTargets:
             self.sizes = tuple(int(s) for s in self.sizes)
         self.total = sum(self.sizes)
 
+    @classmethod
+    def from_checked_sizes(cls, labels: torch.Tensor, boxes: torch.Tensor, sizes: tuple[int, ...],
+                           total: int) -> "PackedTargets":
+        """Construct without re-validating ``sizes`` (a tuple of ints summing to ``total``), for
+        callers that build the same split every step."""
+        obj = cls.__new__(cls)
+        obj.labels, obj.boxes, obj.sizes, obj.total = labels, boxes, sizes, total
+        return obj
+
     @staticmethod
     def from_list(targets: Sequence[dict], device: torch.device | None = None) -> "PackedTargets":
         sizes = tuple(int(t["labels"].shape[0]) for t in targets)
@@ -373,9 +382,12 @@ def _record(events: dict | None, name: str) -> None:
 
 def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: PackedTargets,
                  group_detr: int = 1, *, weights: dict | None = None, check_status: bool = False,
-                 extras: dict | None = None, events: dict | None = None) -> MatchResult:
+                 extras: dict | None = None, events: dict | None = None,
+                 out: torch.Tensor | None = None) -> MatchResult:
     """One matcher step over logits ``[L, B, Q, C]`` and boxes ``[L, B, Q, 4]``, two launches.
 
+    ``out``, when given, is an int64 ``[2, total_pairs]`` tensor (rows contiguous, e.g. a view
+    into a collective's send buffer) the pairs are written into.
     ``extras``, when given, receives the target-major cost buffer ``[L, S, ld]``
     (``"cost"``), its row stride and the step plan.  ``events``, when given,
     collects CUDA events recorded on the launching stream around each kernel
@@ -393,7 +405,13 @@ def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: P
     layout = _lib.LAYOUT_TARGET_MAJOR
     plan = plan_step(tg.sizes, layers, queries, group_detr, ld, device, layout)
     cost = torch.empty((layers, sum_t, ld), dtype=torch.float32, device=device)
-    pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=device)
+    if out is None:
+        pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=device)
+    else:
+        if (out.dtype != torch.int64 or out.device != device or tuple(out.shape) != (2, plan.total_pairs)
+                or (plan.total_pairs and out.stride(1) != 1)):
+            raise ValueError(f"out must be an int64 [2, {plan.total_pairs}] tensor with contiguous rows on {device}")
+        pairs = out
     status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=device) if check_status else None
     stream = _stream_handle(device)
     if sum_t > 0:

@@ -40,31 +40,56 @@ def pairs_per_image(sizes: Sequence[int], layers: int, queries: int, group_detr:
     return np.tile(per, layers)
 
 
+class _Shard:
+    """Host-only split of a batch for one rank: image bounds, pair counts per rank and per
+    (layer, image), this rank's sizes tuple (one object, so the matcher's plan cache hits by
+    identity) and its slice of the packed targets."""
+
+    def __init__(self, sizes: tuple[int, ...], layers: int, queries: int, group_detr: int, world: int, rank: int):
+        self.bounds = shard_bounds(len(sizes), world)
+        offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+        self.counts, self.per = [], []
+        for a, b in self.bounds:
+            pi = pairs_per_image(sizes[a:b], layers, queries, group_detr)
+            self.counts.append(int(pi.sum()))
+            self.per.extend(int(x) for x in pi)
+        self.lo, self.hi = self.bounds[rank]
+        self.t_lo, self.t_hi = int(offsets[self.lo]), int(offsets[self.hi])
+        self.local_sizes = tuple(sizes[self.lo:self.hi])
+        self.width = max(self.counts) if self.counts else 0
+        self.buffers: dict = {}
+
+    def gather_buffers(self, device, world: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Send ``[1, 2, width]`` and receive ``[world, 2, width]`` int64 buffers, reused across steps."""
+        key = (str(device), world)
+        if key not in self.buffers:
+            self.buffers[key] = (torch.empty((1, 2, self.width), dtype=torch.int64, device=device),
+                                 torch.empty((world, 2, self.width), dtype=torch.int64, device=device))
+        return self.buffers[key]
+
+
 @lru_cache(maxsize=64)
-def _layout(sizes: tuple[int, ...], layers: int, queries: int, group_detr: int, world: int):
-    """Host-only split of a batch: image bounds, pair count per rank, per-(layer, image) counts."""
-    bounds = shard_bounds(len(sizes), world)
-    offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
-    counts, per = [], []
-    for a, b in bounds:
-        pi = pairs_per_image(sizes[a:b], layers, queries, group_detr)
-        counts.append(int(pi.sum()))
-        per.extend(int(x) for x in pi)
-    return bounds, offsets, counts, per
+def _shard(sizes: tuple[int, ...], layers: int, queries: int, group_detr: int, world: int, rank: int) -> _Shard:
+    return _Shard(sizes, layers, queries, group_detr, world, rank)
+
+
+def _unpad(recv: torch.Tensor, counts: Sequence[int]) -> torch.Tensor:
+    return torch.cat([recv[r, :, : int(counts[r])] for r in range(recv.shape[0])], dim=1)
 
 
 def gather_pairs(local_pairs: torch.Tensor, counts: Sequence[int], group=None) -> torch.Tensor:
-    """All-gather ``[2, counts[rank]]`` int64 chunks; returns ``[2, sum(counts)]`` in rank order."""
+    """All-gather ``[2, counts[rank]]`` int64 chunks; returns ``[2, sum(counts)]`` in rank order.
+    Chunks are padded to the largest count; the padding is never read."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     width = max(int(c) for c in counts) if counts else 0
-    send = torch.zeros((2, width), dtype=local_pairs.dtype, device=local_pairs.device)
+    send = torch.empty((1, 2, width), dtype=local_pairs.dtype, device=local_pairs.device)
     n = int(counts[rank])
     if n:
-        send[:, :n] = local_pairs[:, :n]
+        send[0, :, :n] = local_pairs[:, :n]
     recv = torch.empty((world, 2, width), dtype=local_pairs.dtype, device=local_pairs.device)
-    dist.all_gather_into_tensor(recv, send.unsqueeze(0).contiguous(), group=group)
-    return torch.cat([recv[r, :, : int(counts[r])] for r in range(world)], dim=1)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    return _unpad(recv, counts)
 
 
 def sharded_match(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: torch.Tensor,
@@ -82,24 +107,26 @@ def sharded_match(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: t
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    sizes = tuple(int(s) for s in sizes)
+    if type(sizes) is not tuple:
+        sizes = tuple(int(s) for s in sizes)
     layers, nimg_in, queries, _ = pred_logits.shape
-    bounds, offsets, counts, per = _layout(sizes, layers, queries, group_detr, world)
-    lo, hi = bounds[rank]
+    sh = _shard(sizes, layers, queries, group_detr, world, rank)
     if nimg_in == len(sizes):  # whole batch given: slice this rank's images and targets
-        pred_logits = pred_logits[:, lo:hi]
-        pred_boxes = pred_boxes[:, lo:hi]
-        labels = labels[offsets[lo]:offsets[hi]]
-        boxes = boxes[offsets[lo]:offsets[hi]]
-    elif nimg_in != hi - lo:
-        raise ValueError(f"rank {rank} holds {nimg_in} images, its shard has {hi - lo}")
-    local_sizes = sizes[lo:hi]
+        pred_logits = pred_logits[:, sh.lo:sh.hi]
+        pred_boxes = pred_boxes[:, sh.lo:sh.hi]
+        labels = labels[sh.t_lo:sh.t_hi]
+        boxes = boxes[sh.t_lo:sh.t_hi]
+    elif nimg_in != sh.hi - sh.lo:
+        raise ValueError(f"rank {rank} holds {nimg_in} images, its shard has {sh.hi - sh.lo}")
+    n = sh.counts[rank]
     if local_solver is None:
         from .matcher import PackedTargets, match_packed
 
-        res = match_packed(pred_logits, pred_boxes, PackedTargets(labels, boxes, local_sizes), group_detr,
-                           weights=weights)
-        local = res.pairs
-    else:
-        local = local_solver(pred_logits, pred_boxes, labels, boxes, list(local_sizes), group_detr)
-    return gather_pairs(local, counts, group), per
+        # the local pairs land directly in the collective's send buffer
+        send, recv = sh.gather_buffers(pred_logits.device, world)
+        targets = PackedTargets.from_checked_sizes(labels, boxes, sh.local_sizes, sh.t_hi - sh.t_lo)
+        match_packed(pred_logits, pred_boxes, targets, group_detr, weights=weights, out=send[0, :, :n])
+        dist.all_gather_into_tensor(recv, send, group=group)
+        return _unpad(recv, sh.counts), sh.per
+    local = local_solver(pred_logits, pred_boxes, labels, boxes, list(sh.local_sizes), group_detr)
+    return gather_pairs(local, sh.counts, group), sh.per

@@ -1,0 +1,63 @@
+"""sharded_match on one GPU through a one-rank NCCL group: the device path writes its pairs into
+the all-gather's send buffer and must return exactly match_packed's pairs (integers: exact
+equality), on the same step twice so the reused buffers are exercised."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+
+from rfdetr_training_throughput_b200 import matcher, sharded, workloads
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.fixture
+def one_rank_group():
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(_free_port())
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    try:
+        yield
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_match_equals_match_packed_on_one_rank(one_rank_group):
+    dev = torch.device("cuda", 0)
+    wl = workloads.make("sweep", images=40)
+    logits, boxes = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)
+    packed = matcher.PackedTargets.from_list(wl.targets_on(dev), dev)
+    expect = matcher.match_packed(logits, boxes, packed, wl.group_detr, weights=wl.weights)
+    for _ in range(2):
+        pairs, per = sharded.sharded_match(logits, boxes, packed.labels, packed.boxes, wl.sizes, wl.group_detr,
+                                           weights=wl.weights)
+        torch.cuda.synchronize()
+        assert torch.equal(pairs, expect.pairs)
+        assert per == expect.per_image
+
+
+def test_match_packed_out_argument_is_checked():
+    dev = torch.device("cuda", 0)
+    wl = workloads.make("step", layers=1, images=2)
+    packed = matcher.PackedTargets.from_list(wl.targets_on(dev), dev)
+    res = matcher.match_packed(wl.pred_logits.to(dev), wl.pred_boxes.to(dev), packed, wl.group_detr,
+                               weights=wl.weights)
+    buf = torch.full((3, 2, res.pairs.shape[1] + 5), -9, dtype=torch.int64, device=dev)
+    view = buf[1, :, 2:2 + res.pairs.shape[1]]  # rows contiguous, row stride larger than the row
+    matcher.match_packed(wl.pred_logits.to(dev), wl.pred_boxes.to(dev), packed, wl.group_detr,
+                         weights=wl.weights, out=view)
+    torch.cuda.synchronize()
+    assert torch.equal(view, res.pairs)
+    assert bool((buf[0] == -9).all()) and bool((buf[2] == -9).all()) and bool((buf[1, :, :2] == -9).all())
+    with pytest.raises(ValueError):
+        matcher.match_packed(wl.pred_logits.to(dev), wl.pred_boxes.to(dev), packed, wl.group_detr,
+                             weights=wl.weights, out=torch.empty((2, 3), dtype=torch.int64, device=dev))

@@ -61,10 +61,16 @@ constexpr int kSmemPerCtaReserved = 1024;
 constexpr int kSmemPerBlockMax = 227 * 1024;
 constexpr int64_t kTileCapDefault = 16384;  // floats: 64 KB of staged cost per warp
 constexpr int kMaxWarpsPerCta = 4;
-// Register budget of the instantiations up to 320 columns: four CTAs of four
-// warps per SM (at most 128 registers a thread); the 1024-column one keeps its
-// per-lane arrays in registers instead.
-__host__ __device__ constexpr int min_ctas_per_sm(int cols_per_lane) { return cols_per_lane <= 10 ? 4 : 1; }
+// Register budget.  The instantiations up to 320 columns run four CTAs of four
+// warps per SM (at most 128 registers a thread), or six in the wide layout,
+// which keeps the column duals and tie keys in shared memory (at most 85): more
+// resident warps for large batches at a longer chain per problem.  The
+// 1024-column one keeps its per-lane arrays in registers.
+__host__ __device__ constexpr int min_ctas_per_sm(int cols_per_lane, bool wide) {
+  return cols_per_lane > 10 ? 1 : (wide ? 6 : 4);
+}
+// Batches with more than this many problems per SM use the wide layout.
+constexpr int kWideProblemsPerSm = 64;
 // Shared-memory budget of one CTA: four CTAs of four warps fill an SM.
 constexpr int kCtaBudget = kSmemPerSm / 4 - kSmemPerCtaReserved;
 // Tie keys: a free column at position pos gets kKeyBase - 1 - pos, a matched one
@@ -127,10 +133,11 @@ __host__ __device__ inline int choose_mode(const Shape& s, int64_t tile_cap, int
   return kModeScratch;
 }
 
-__host__ __device__ inline int64_t fixed_warp_bytes(int cols_cap, int max_rows) {
+__host__ __device__ inline int64_t fixed_warp_bytes(int cols_cap, int max_rows, bool wide = false) {
   // u and first-pick cost (float64), col4row and first-pick column (int16) per row;
-  // the 32 lanes' visited masks; row4col, path, remaining (int16) per column
-  const int64_t b = static_cast<int64_t>(max_rows) * 20 + 128 + static_cast<int64_t>(cols_cap) * 6;
+  // the 32 lanes' visited masks; row4col, path, remaining (int16) per column; in
+  // the wide layout also the column duals (float64) and tie keys (uint16)
+  const int64_t b = static_cast<int64_t>(max_rows) * 20 + 128 + static_cast<int64_t>(cols_cap) * (wide ? 16 : 6);
   return (b + 15) & ~int64_t(15);
 }
 
@@ -192,12 +199,14 @@ __device__ __forceinline__ float load_cost(const float* p) {
 
 // One scan step of the augmenting-path search over the lane's columns.  The
 // lane's loads are all issued before the first is used (a row read from
-// global memory then costs one round trip, not one per column).
-template <int K, int L>
+// global memory then costs one round trip, not one per column).  Column duals
+// and tie keys come from registers, or in the wide layout from shared memory
+// (a key only when its column ties or beats the lane's best so far).
+template <int K, int L, bool kWide>
 __device__ __forceinline__ void scan_row(const float* row, int lane, int i, double minv, double ui,
-                                         const double (&v)[K], double (&spc)[K],
-                                         const unsigned (&key)[K], unsigned rem, int16_t* path_s,
-                                         double& bv, unsigned& bk) {
+                                         const double (&v)[K], const double* v_s, double (&spc)[K],
+                                         const unsigned (&key)[K], const uint16_t* key_s, unsigned rem,
+                                         int16_t* path_s, double& bv, unsigned& bk) {
   float cf[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) cf[k] = (rem & (1u << k)) ? load_cost<L>(row + lane + 32 * k) : 0.0f;
@@ -205,18 +214,27 @@ __device__ __forceinline__ void scan_row(const float* row, int lane, int i, doub
   for (int k = 0; k < K; ++k) {
     if (rem & (1u << k)) {
       const int j = lane + 32 * k;
-      const double r = ((minv + static_cast<double>(cf[k])) - ui) - v[k];
+      const double r = ((minv + static_cast<double>(cf[k])) - ui) - (kWide ? v_s[j] : v[k]);
       if (r < spc[k]) {
         spc[k] = r;
         path_s[j] = static_cast<int16_t>(i);
       }
-      if (spc[k] < bv || (spc[k] == bv && key[k] < bk)) {
+      if (kWide) {
+        if (spc[k] < bv) {
+          bv = spc[k];
+          bk = key_s[j];
+        } else if (spc[k] == bv) {
+          const unsigned kj = key_s[j];
+          if (kj < bk) bk = kj;
+        }
+      } else if (spc[k] < bv || (spc[k] == bv && key[k] < bk)) {
         bv = spc[k];
         bk = key[k];
       }
     }
   }
 }
+
 
 
 
@@ -262,7 +280,7 @@ __device__ __forceinline__ void record_first_pick(const float (&x)[K], int lane,
 }
 
 // Solves problem p with the warp's shared-memory slot at `base` (`slot` bytes).
-template <int K, bool kDense>
+template <int K, bool kDense, bool kWide>
 __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned char* base, int slot,
                                               int lane) {
   constexpr int kCols = 32 * K;
@@ -300,12 +318,14 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
 
   double* u_s = reinterpret_cast<double*>(base);
   double* pick_m_s = u_s + a.max_rows;
-  unsigned* vis_s = reinterpret_cast<unsigned*>(pick_m_s + a.max_rows);
+  double* v_s = pick_m_s + a.max_rows;  // wide layout only
+  unsigned* vis_s = reinterpret_cast<unsigned*>(v_s + (kWide ? kCols : 0));
   int16_t* col4row_s = reinterpret_cast<int16_t*>(vis_s + 32);
   int16_t* pick_w_s = col4row_s + a.max_rows;
   int16_t* row4col_s = pick_w_s + a.max_rows;
   int16_t* path_s = row4col_s + kCols;
   int16_t* rem_s = path_s + kCols;
+  uint16_t* key_s = reinterpret_cast<uint16_t*>(rem_s + kCols);  // wide layout only
   unsigned valid = 0;
 #pragma unroll
   for (int k = 0; k < K; ++k) {
@@ -315,7 +335,10 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
     u_s[i] = 0.0;
     col4row_s[i] = -1;
   }
-  for (int j = lane; j < nc; j += 32) row4col_s[j] = -1;
+  for (int j = lane; j < nc; j += 32) {
+    row4col_s[j] = -1;
+    if (kWide) v_s[j] = 0.0;
+  }
 
   // ---- load the cost once: validate it (SciPy rejects NaN and -inf), keep
   // it on chip when it fits, and find every row's first pick ---------------
@@ -333,7 +356,7 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
   // only ever turn from free to matched, which raises their tie keys.  Should
   // rounding ever make a dual step negative, every pending pick is dropped.
   const float* src = a.cost + cost_off;
-  const int64_t fixed = fixed_warp_bytes(kCols, a.max_rows);
+  const int64_t fixed = fixed_warp_bytes(kCols, a.max_rows, kWide);
   float* tile = reinterpret_cast<float*>(base + fixed);
   const int mode = choose_mode(s, a.tile_cap, (slot - fixed) / 4);
   bool bad = false;
@@ -439,8 +462,12 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
       const int j = lane + 32 * k;
       const unsigned pos = static_cast<unsigned>(nc - 1 - j);  // remaining[it] = nc-1-it (reverse fill)
       spc[k] = CUDART_INF;
-      key[k] = (freem & (1u << k)) ? kKeyBase - 1u - pos : kKeyBase + pos;
-      if (j < nc) rem_s[nc - 1 - j] = static_cast<int16_t>(j);
+      const unsigned kv = (freem & (1u << k)) ? kKeyBase - 1u - pos : kKeyBase + pos;
+      if (!kWide) key[k] = kv;
+      if (j < nc) {
+        if (kWide) key_s[j] = static_cast<uint16_t>(kv);
+        rem_s[nc - 1 - j] = static_cast<int16_t>(j);
+      }
     }
     unsigned rem = valid;
     int i = cur;
@@ -455,11 +482,14 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
       unsigned bk = kNoKey;
       const float* row = rows + i * row_pitch;
       if (mode == kModeShared) {
-        scan_row<K, kLoadShared>(row, lane, i, minv, ui, v, spc, key, rem, path_s, bv, bk);
+        scan_row<K, kLoadShared, kWide>(row, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv,
+                                     bk);
       } else if (mode == kModeDirect) {
-        scan_row<K, kLoadGlobal>(row, lane, i, minv, ui, v, spc, key, rem, path_s, bv, bk);
+        scan_row<K, kLoadGlobal, kWide>(row, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv,
+                                     bk);
       } else {
-        scan_row<K, kLoadScratch>(row, lane, i, minv, ui, v, spc, key, rem, path_s, bv, bk);
+        scan_row<K, kLoadScratch, kWide>(row, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv,
+                                     bk);
       }
       warp_argmin(bv, bk);
       if (bv == CUDART_INF) {
@@ -475,7 +505,12 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
       if (lane == 0) rem_s[ps] = static_cast<int16_t>(jl);  // swap-with-last removal
       if ((jl & 31) == lane) {
         const int kl = jl >> 5;
-        set_key<K>(key, kl, ((freem >> kl) & 1u) ? kKeyBase - 1u - ps : kKeyBase + ps);
+        const unsigned kv = ((freem >> kl) & 1u) ? kKeyBase - 1u - ps : kKeyBase + ps;
+        if (kWide) {
+          key_s[jl] = static_cast<uint16_t>(kv);
+        } else {
+          set_key<K>(key, kl, kv);
+        }
       }
       if ((js & 31) == lane) rem &= ~(1u << (js >> 5));
       nrem = last;
@@ -503,7 +538,11 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
         const double d = minv - spc[k];
         raised |= d < 0.0;
         if (j != sink) u_s[row4col_s[j]] += d;
-        v[k] -= d;
+        if (kWide) {
+          v_s[j] -= d;
+        } else {
+          v[k] -= d;
+        }
       }
     }
     raised = __any_sync(kFullMask, raised);
@@ -581,15 +620,15 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
   if (a.status != nullptr && lane == 0) a.status[p] = code;
 }
 
-template <int K, bool kDense>
-__global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K)) lsap_kernel(const LsapArgs a) {
+template <int K, bool kDense, bool kWide>
+__global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kWide)) lsap_kernel(const LsapArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   if (kDense) {
     const int p = blockIdx.x * a.dense_warps + warp;
     if (p < a.num_problems) {
-      solve_problem<K, kDense>(a, p, smem_raw + static_cast<int64_t>(warp) * a.slot, a.slot, lane);
+      solve_problem<K, kDense, kWide>(a, p, smem_raw + static_cast<int64_t>(warp) * a.slot, a.slot, lane);
     }
   } else if (a.queue != nullptr) {
     // persistent warps: pull problems (sorted largest first) until none is left
@@ -599,13 +638,13 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K)) lsap
       if (lane == 0) p = atomicAdd(a.queue, 1);
       p = __shfl_sync(kFullMask, p, 0);
       if (p >= a.num_problems) break;
-      solve_problem<K, kDense>(a, p, base, a.slot, lane);
+      solve_problem<K, kDense, kWide>(a, p, base, a.slot, lane);
       __syncwarp();
     }
   } else {
     const int4 cta = a.ctas[blockIdx.x];
     if (warp < cta.y) {
-      solve_problem<K, kDense>(a, cta.x + warp, smem_raw + static_cast<int64_t>(warp) * cta.z, cta.z,
+      solve_problem<K, kDense, kWide>(a, cta.x + warp, smem_raw + static_cast<int64_t>(warp) * cta.z, cta.z,
                                lane);
     }
   }
@@ -634,14 +673,23 @@ int sm_count() {
   return n;
 }
 
-// CTAs of the pair-mode kernel that fit on one SM at this shared-memory size.
-int query_resident_ctas(int cols_per_lane, int64_t smem) {
-  const void* fn = nullptr;
+// The pair-mode kernel for a column count and layout (the wide layout exists
+// for up to 320 columns).
+const void* pair_kernel(int cols_per_lane, bool wide) {
   switch (cols_per_lane) {
-    case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, false>); break;
-    case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, false>); break;
-    default: fn = reinterpret_cast<const void*>(&lsap_kernel<32, false>); break;
+    case 4: return wide ? reinterpret_cast<const void*>(&lsap_kernel<4, false, true>)
+                        : reinterpret_cast<const void*>(&lsap_kernel<4, false, false>);
+    case 10: return wide ? reinterpret_cast<const void*>(&lsap_kernel<10, false, true>)
+                         : reinterpret_cast<const void*>(&lsap_kernel<10, false, false>);
+    case 32: return wide ? nullptr : reinterpret_cast<const void*>(&lsap_kernel<32, false, false>);
+    default: return nullptr;
   }
+}
+
+// CTAs of a pair-mode kernel that fit on one SM at this shared-memory size.
+int query_resident_ctas(int cols_per_lane, bool wide, int64_t smem) {
+  const void* fn = pair_kernel(cols_per_lane, wide);
+  if (fn == nullptr) return 0;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
           cudaSuccess) {
@@ -657,17 +705,18 @@ int query_resident_ctas(int cols_per_lane, int64_t smem) {
   return n;
 }
 
-// query_resident_ctas() memoised per (device, columns per lane, shared memory): the
+// query_resident_ctas() memoised per (device, kernel, shared memory): the
 // occupancy query and the attribute call cost a few microseconds per launch.
 struct OccupancyEntry {
   int device, cols_per_lane;
+  bool wide;
   int64_t smem;
   int ctas;
 };
 std::mutex g_occupancy_mutex;
 std::vector<OccupancyEntry> g_occupancy;
 
-int resident_ctas(int cols_per_lane, int64_t smem) {
+int resident_ctas(int cols_per_lane, bool wide, int64_t smem) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
@@ -675,26 +724,32 @@ int resident_ctas(int cols_per_lane, int64_t smem) {
   }
   {
     std::lock_guard<std::mutex> lock(g_occupancy_mutex);
-    for (const OccupancyEntry& e : g_occupancy)
-      if (e.device == dev && e.cols_per_lane == cols_per_lane && e.smem == smem) return e.ctas;
+    for (const OccupancyEntry& e : g_occupancy) {
+      if (e.device == dev && e.cols_per_lane == cols_per_lane && e.wide == wide && e.smem == smem) {
+        return e.ctas;
+      }
+    }
   }
-  const int n = query_resident_ctas(cols_per_lane, smem);
+  const int n = query_resident_ctas(cols_per_lane, wide, smem);
   if (n > 0) {
     std::lock_guard<std::mutex> lock(g_occupancy_mutex);
-    g_occupancy.push_back({dev, cols_per_lane, smem, n});
+    g_occupancy.push_back({dev, cols_per_lane, wide, smem, n});
   }
   return n;
 }
 
-template <bool kDense>
+template <bool kDense, bool kWide>
 int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta, int64_t smem,
            void* stream) {
   if (smem > kSmemPerBlockMax) return RFM_ERR_UNSUPPORTED;
   const void* fn = nullptr;
   switch (cols_per_lane) {
-    case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense>); break;
-    case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, kDense>); break;
-    case 32: fn = reinterpret_cast<const void*>(&lsap_kernel<32, kDense>); break;
+    case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense, kWide>); break;
+    case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, kDense, kWide>); break;
+    case 32:
+      if (kWide) return RFM_ERR_INVALID_ARGUMENT;
+      fn = reinterpret_cast<const void*>(&lsap_kernel<32, kDense, false>);
+      break;
     default: return RFM_ERR_INVALID_ARGUMENT;
   }
   if (smem > 48 * 1024 &&
@@ -705,9 +760,9 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
   const dim3 grid(static_cast<unsigned>(num_ctas));
   const dim3 block(32 * warps_per_cta);
   switch (cols_per_lane) {
-    case 4: lsap_kernel<4, kDense><<<grid, block, smem, as_stream(stream)>>>(a); break;
-    case 10: lsap_kernel<10, kDense><<<grid, block, smem, as_stream(stream)>>>(a); break;
-    default: lsap_kernel<32, kDense><<<grid, block, smem, as_stream(stream)>>>(a); break;
+    case 4: lsap_kernel<4, kDense, kWide><<<grid, block, smem, as_stream(stream)>>>(a); break;
+    case 10: lsap_kernel<10, kDense, kWide><<<grid, block, smem, as_stream(stream)>>>(a); break;
+    default: lsap_kernel<32, kDense, false><<<grid, block, smem, as_stream(stream)>>>(a); break;
   }
   return launch_status();
 }
@@ -867,19 +922,27 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   a.t_out = target_out;
   a.status = status;
   if (!persistent) {
-    return launch<false>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta, plan->cta_smem_bytes,
-                         stream);
+    return launch<false, false>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta,
+                                plan->cta_smem_bytes, stream);
   }
+  // Persistent warps stage nothing, so each warp's slot is just its fixed arrays;
+  // large batches (more problems than 64 per SM) take the wide layout.
+  const int sms = sm_count();
+  const bool wide = plan->cols_per_lane <= 10 &&
+                    static_cast<int64_t>(plan->num_problems) > static_cast<int64_t>(kWideProblemsPerSm) * sms;
+  const int64_t smem = wide ? kMaxWarpsPerCta * fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows, true)
+                            : plan->cta_smem_bytes;
   a.queue = static_cast<int*>(workspace);
   a.workspace = reinterpret_cast<float*>(static_cast<char*>(workspace) + kQueueBytes);
-  a.slot = plan->cta_smem_bytes / kMaxWarpsPerCta;
+  a.slot = static_cast<int>(smem / kMaxWarpsPerCta);
   if (cudaMemsetAsync(a.queue, 0, sizeof(int), as_stream(stream)) != cudaSuccess) return launch_status();
-  const int ctas_per_sm = resident_ctas(plan->cols_per_lane, plan->cta_smem_bytes);
+  const int ctas_per_sm = resident_ctas(plan->cols_per_lane, wide, smem);
   if (ctas_per_sm < 1) return launch_status() != RFM_OK ? RFM_ERR_LAUNCH : RFM_ERR_UNSUPPORTED;
-  const int grid = ctas_per_sm * sm_count();
+  const int grid = ctas_per_sm * sms;
   const int needed = (plan->num_problems + kMaxWarpsPerCta - 1) / kMaxWarpsPerCta;
-  return launch<false>(a, plan->cols_per_lane, grid < needed ? grid : needed, kMaxWarpsPerCta,
-                       plan->cta_smem_bytes, stream);
+  const int num_ctas = grid < needed ? grid : needed;
+  if (wide) return launch<false, true>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
+  return launch<false, false>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
 }
 
 namespace {
@@ -948,7 +1011,7 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.t_out = nullptr;
   a.status = status;
   const int ctas = (num_problems + dp.warps - 1) / dp.warps;
-  return launch<true>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);
+  return launch<true, false>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);
 }
 
 // ---------------------------------------------------------------------------

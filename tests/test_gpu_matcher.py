@@ -138,3 +138,26 @@ def test_status_reports_invalid_costs():
     outs[0]["pred_logits"][0, 5, :] = float("nan")
     with pytest.raises(ValueError, match="invalid"):
         matcher.match_layers(outs, wl.targets_on(DEV), wl.group_detr, weights=wl.weights, check_status=True)
+
+
+def test_large_batch_of_narrow_groups_against_oracle():
+    """10,400 problems of 64 queries: a batch large enough for the solver's wide layout (duals and
+    tie keys in shared memory) with the 128-column instantiation; indices identical to the C oracle
+    on the device-computed matrix."""
+    rng = np.random.default_rng(21)
+    images, group_detr, qg = 800, 13, 64
+    queries = group_detr * qg
+    sizes = np.clip(rng.poisson(8, images), 1, 60)
+    logits = rng.normal(-2.0, 1.5, (1, images, queries, 2)).astype(np.float32)
+    boxes = (1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.0, (1, images, queries, 4))))).astype(np.float32)
+    targets = [{"labels": torch.as_tensor(rng.integers(0, 2, t), device=DEV),
+                "boxes": torch.as_tensor(np.concatenate([rng.uniform(0.1, 0.9, (t, 2)), rng.uniform(0.02, 0.5, (t, 2))],
+                                                        axis=1).astype(np.float32), device=DEV)} for t in sizes]
+    outputs = [{"pred_logits": torch.as_tensor(logits[0], device=DEV), "pred_boxes": torch.as_tensor(boxes[0], device=DEV)}]
+    res, cost = matcher.match_layers(outputs, targets, group_detr, return_cost=True)
+    torch.cuda.synchronize()
+    cost = cost[0, :, : int(sizes.sum())].cpu().numpy()
+    expect = solve_blocks(cost, [int(t) for t in sizes], group_detr, solver=oracle_lsa)
+    for b, (q, t) in enumerate(res[0]):
+        assert np.array_equal(q.cpu().numpy(), expect[b][0]), b
+        assert np.array_equal(t.cpu().numpy(), expect[b][1]), b

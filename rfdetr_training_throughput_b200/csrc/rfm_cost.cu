@@ -6,12 +6,16 @@
 // written directly, so there is no padded intermediate and no copy.
 //
 // Two output layouts.  TARGET-MAJOR (the transpose, out[l][col][q]) is the one
-// the fused matcher step uses: one CTA covers one image and a 512-query tile;
-// each thread owns four consecutive queries (one 16-byte vector of every output
-// row), loads their boxes and logits once, evaluates the focal cost once per
-// class when there are at most four classes, and then walks the image's
-// targets (staged in shared memory, read as broadcasts), so every store is a
-// fully coalesced 128-bit write along the row and every input is read once.
+// the fused matcher step uses: one CTA covers 32 consecutive target rows (runs
+// of one image each) and a 256-query tile; each thread owns two consecutive
+// queries (one 8-byte vector of every output row), loads their boxes and logits
+// once per image run (the next run's while computing the current one),
+// evaluates the focal cost once per class when there are at most four classes,
+// and then walks the run's targets (staged in shared memory, read as
+// broadcasts), so every warp store is a coalesced 256-byte write along the row
+// and every input is read once per run.  Two queries per thread keep the kernel
+// near 72 registers, several CTAs per SM, which hides more latency than wider
+// per-thread tiles do.
 //
 // QUERY-MAJOR (the compact matrix itself, out[l][q][col]) serves the drop-in
 // cost-matrix call.  Each thread owns four consecutive columns of the output (one
@@ -53,7 +57,7 @@ struct CostArgs {
   int B, Q, C, S;
   int64_t ld;
   int rows_per_cta;
-  float w_class, w_bbox, w_giou, alpha, one_minus_alpha;
+  float w_class, w_bbox, w_giou, alpha, alpha_m1;
   float* out;            // [L, Q, ld]
 };
 
@@ -84,24 +88,27 @@ __device__ __forceinline__ float rcp_approx(float b) {
   return r;
 }
 
-__device__ __forceinline__ float quot(float a, float b) { return __fmul_rn(a, rcp_approx(b)); }
 
 // alpha (1-p)^2 (-logsigmoid(x)) - (1-alpha) p^2 (-logsigmoid(-x)), p = sigmoid(x)
 // (kernels_matcher.py:257-260), with logsigmoid(x) = min(x, 0) - log1p(exp(-|x|)).
 // Fast exponent and logarithm: e = exp(-|x|), log1p(e) = log(1 + e),
-// sigmoid(x) = (x >= 0 ? 1 : e) / (1 + e); within ~1e-6 of the exact chain.  Every
-// rounding step is explicit so all call sites produce identical bits.
-__device__ __forceinline__ float focal_cost(float x, float alpha, float one_minus_alpha) {
+// sigmoid(x) = s * rcp(1 + e) with s = (x >= 0 ? 1 : e), 1 - p = fma(-s, rcp, 1),
+// and the final difference as fma(alpha (1-p)^2, -logsigmoid(x), (alpha-1) p^2
+// (-logsigmoid(-x))); within ~1e-6 of the exact chain.  Every rounding step is
+// explicit, and focal_cost2 evaluates the same operations on two logits at once,
+// so every call site produces identical bits.  alpha_m1 = -(1 - alpha).
+__device__ __forceinline__ float focal_cost(float x, float alpha, float alpha_m1) {
   const float e = __expf(-fabsf(x));
   const float onep = __fadd_rn(1.0f, e);
   const float l = __logf(onep);
-  const float p = quot(x >= 0.0f ? 1.0f : e, onep);
-  const float q = __fsub_rn(1.0f, p);
-  const float ls_pos = __fsub_rn(fminf(x, 0.0f), l);
-  const float ls_neg = __fsub_rn(fminf(-x, 0.0f), l);
-  const float neg = __fmul_rn(__fmul_rn(one_minus_alpha, __fmul_rn(p, p)), -ls_neg);
-  const float pos = __fmul_rn(__fmul_rn(alpha, __fmul_rn(q, q)), -ls_pos);
-  return __fsub_rn(pos, neg);
+  const float s = x >= 0.0f ? 1.0f : e;
+  const float r = rcp_approx(onep);
+  const float p = __fmul_rn(s, r);
+  const float q = __fmaf_rn(-s, r, 1.0f);
+  const float mpos = __fsub_rn(l, fminf(x, 0.0f));
+  const float mneg = __fsub_rn(l, fminf(-x, 0.0f));
+  const float nneg = __fmul_rn(__fmul_rn(alpha_m1, __fmul_rn(p, p)), mneg);
+  return __fmaf_rn(__fmul_rn(alpha, __fmul_rn(q, q)), mpos, nneg);
 }
 
 // cost_bbox * l1 + w_class_cost + cost_giou * (-giou), evaluated as
@@ -239,7 +246,7 @@ __global__ void __launch_bounds__(kThreads) cost_qmajor_kernel(const CostArgs a)
         const float4 pb = __ldg(a.pboxes + pq);
         const float x = __ldg(a.logits + pq * a.C + label[c]);
         r[c] = pair_cost(pb, corners(pb), tb[c], tc[c],
-                         __fmul_rn(a.w_class, focal_cost(x, a.alpha, a.one_minus_alpha)), a);
+                         __fmul_rn(a.w_class, focal_cost(x, a.alpha, a.alpha_m1)), a);
       }
     }
     float* dst = a.out + (static_cast<int64_t>(layer) * a.Q + q) * a.ld + col0;
@@ -255,7 +262,8 @@ __global__ void __launch_bounds__(kThreads) cost_qmajor_kernel(const CostArgs a)
 }
 
 
-constexpr int kTmThreads = 128;  // 4 queries each: 512 queries per CTA
+constexpr int kTmThreads = 128;  // 2 queries each: 256 queries per CTA
+constexpr int kQpt = 2;          // queries per thread (one f32x2 pair)
 constexpr int kTmCols = 32;      // target rows per CTA (may span several images)
 constexpr int kSmallClasses = 4;
 
@@ -329,6 +337,22 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return upk(r);
 }
 
+// focal_cost of two logits: the same operations, packed where they are add, sub,
+// mul or fma (no packed product feeds a packed add, so nothing is contracted).
+__device__ __forceinline__ float2 focal_cost2(float2 x, float alpha, float alpha_m1) {
+  const float2 e = make_float2(__expf(-fabsf(x.x)), __expf(-fabsf(x.y)));
+  const float2 onep = add2(dup2(1.0f), e);
+  const float2 l = make_float2(__logf(onep.x), __logf(onep.y));
+  const float2 sv = make_float2(x.x >= 0.0f ? 1.0f : e.x, x.y >= 0.0f ? 1.0f : e.y);
+  const float2 r = make_float2(rcp_approx(onep.x), rcp_approx(onep.y));
+  const float2 p = mul2(sv, r);
+  const float2 q = fma2(make_float2(-sv.x, -sv.y), r, dup2(1.0f));
+  const float2 mpos = sub2(l, make_float2(fminf(x.x, 0.0f), fminf(x.y, 0.0f)));
+  const float2 mneg = sub2(l, make_float2(fminf(-x.x, 0.0f), fminf(-x.y, 0.0f)));
+  const float2 nneg = mul2(mul2(dup2(alpha_m1), mul2(p, p)), mneg);
+  return fma2(mul2(dup2(alpha), mul2(q, q)), mpos, nneg);
+}
+
 // Cost of one target against a pair of queries (two packed lanes).  With
 // kUnclamped the hull and 1e-7 clamps are skipped: the caller guarantees they
 // are no-ops (both boxes have non-negative width and height, so the hull
@@ -372,14 +396,14 @@ __device__ __forceinline__ float2 pair_cost2(const PredPair& p, const TargetRow&
 // Loads of the next image's predictions, issued before they are needed.
 template <int NCLS>
 struct PredRaw {
-  float4 box[4];
-  float lg[4][NCLS > 0 ? NCLS : 1];
+  float4 box[kQpt];
+  float lg[kQpt][NCLS > 0 ? NCLS : 1];
 };
 
 template <int NCLS>
 __device__ __forceinline__ void load_raw(PredRaw<NCLS>& r, const CostArgs& a, int64_t pbase, int q0) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < kQpt; ++k) {
     const int q = q0 + k < a.Q ? q0 + k : a.Q - 1;  // pad queries reuse a valid row
     r.box[k] = __ldg(a.pboxes + pbase + q);
     if (NCLS > 0) {
@@ -389,46 +413,37 @@ __device__ __forceinline__ void load_raw(PredRaw<NCLS>& r, const CostArgs& a, in
   }
 }
 
-// Costs of targets [c_begin, c_end) of one image run against the thread's four
-// queries, one 16-byte store per target row.
+// Costs of targets [c_begin, c_end) of one image run against the thread's two
+// queries, one 8-byte store per target row.
 template <int NCLS, bool kUnclamped, bool kTail>
 __device__ __forceinline__ void cost_targets(const TargetRow* s_t, int c_begin, int c_end, float* out_row,
-                                             const PredPair& p01, const PredPair& p23,
-                                             const float2 (&wcls01)[kSmallClasses],
-                                             const float2 (&wcls23)[kSmallClasses], int q0, int64_t pbase,
-                                             const CostArgs& a) {
+                                             const PredPair& p01, const float2 (&wcls01)[kSmallClasses],
+                                             int q0, int64_t pbase, const CostArgs& a) {
   float* dst = out_row + static_cast<int64_t>(c_begin) * a.ld;
 #pragma unroll 2
   for (int c = c_begin; c < c_end; ++c, dst += a.ld) {
     const TargetRow t = s_t[c];
-    float2 w01, w23;
+    float2 w01;
     if (NCLS > 0) {
       w01 = wcls01[0];
-      w23 = wcls23[0];
 #pragma unroll
-      for (int cl = 1; cl < NCLS; ++cl) {
-        w01 = t.label == cl ? wcls01[cl] : w01;
-        w23 = t.label == cl ? wcls23[cl] : w23;
-      }
+      for (int cl = 1; cl < NCLS; ++cl) w01 = t.label == cl ? wcls01[cl] : w01;
     } else {
-      float f[4];
+      float f[2];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 2; ++k) {
         const int q = q0 + k < a.Q ? q0 + k : a.Q - 1;
         f[k] = __fmul_rn(a.w_class, focal_cost(__ldg(a.logits + (pbase + q) * a.C + t.label), a.alpha,
-                                               a.one_minus_alpha));
+                                               a.alpha_m1));
       }
       w01 = make_float2(f[0], f[1]);
-      w23 = make_float2(f[2], f[3]);
     }
     float2 r01 = pair_cost2<kUnclamped>(p01, t, w01, a);
-    float2 r23 = pair_cost2<kUnclamped>(p23, t, w23, a);
-    if (kTail && q0 + 4 > a.Q) {  // zero the pad queries of the last tile
-      if (q0 + 1 >= a.Q) r01.y = 0.f;
-      if (q0 + 2 >= a.Q) r23.x = 0.f;
-      if (q0 + 3 >= a.Q) r23.y = 0.f;
+    if (kTail && q0 + 2 > a.Q) {  // zero the pad queries (q >= Q, up to ld) of the last tile
+      if (q0 >= a.Q) r01.x = 0.f;
+      r01.y = 0.f;
     }
-    *reinterpret_cast<float4*>(dst) = make_float4(r01.x, r01.y, r23.x, r23.y);
+    *reinterpret_cast<float2*>(dst) = r01;
   }
 }
 
@@ -453,7 +468,7 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
     tlabel = __ldg(a.labels + c_begin + tid);
   }
   const int win_lo = stage_image_window(a.offsets, a.B, c_begin, s_off, tid, kTmThreads);
-  const int q0 = (blockIdx.y * kTmThreads + tid) * 4;
+  const int q0 = (blockIdx.y * kTmThreads + tid) * kQpt;
   const int64_t layer_base = static_cast<int64_t>(layer) * a.B;
   // the first run's predictions are requested before the targets are staged
   PredRaw<NCLS> raw;
@@ -505,21 +520,14 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
     const int img = s_t[s_seg[sg]].image;
     const int64_t pbase = (layer_base + img) * a.Q;
     const PredPair p01 = pred_pair(raw.box[0], raw.box[1]);
-    const PredPair p23 = pred_pair(raw.box[2], raw.box[3]);
     bool preds_plain = true;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) preds_plain = preds_plain && raw.box[k].z >= 0.0f && raw.box[k].w >= 0.0f;
-    float2 wcls01[kSmallClasses], wcls23[kSmallClasses];
+    for (int k = 0; k < 2; ++k) preds_plain = preds_plain && raw.box[k].z >= 0.0f && raw.box[k].w >= 0.0f;
+    float2 wcls01[kSmallClasses];
     if (NCLS > 0) {
 #pragma unroll
       for (int c = 0; c < NCLS; ++c) {
-        float f[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          f[k] = __fmul_rn(a.w_class, focal_cost(raw.lg[k][c], a.alpha, a.one_minus_alpha));
-        }
-        wcls01[c] = make_float2(f[0], f[1]);
-        wcls23[c] = make_float2(f[2], f[3]);
+        wcls01[c] = mul2(dup2(a.w_class), focal_cost2(make_float2(raw.lg[0][c], raw.lg[1][c]), a.alpha, a.alpha_m1));
       }
     }
     if (sg + 1 < nseg) {
@@ -527,12 +535,10 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
     }
     // one uniform choice per image run: clamp-free when every box of the run is
     // plain, pad-query zeroing only in the last query tile
-    if (preds_plain && all_plain && q0 + 4 <= a.Q) {
-      cost_targets<NCLS, true, false>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, p23, wcls01, wcls23,
-                                      q0, pbase, a);
+    if (preds_plain && all_plain && q0 + 2 <= a.Q) {
+      cost_targets<NCLS, true, false>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, wcls01, q0, pbase, a);
     } else {
-      cost_targets<NCLS, false, true>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, p23, wcls01, wcls23,
-                                      q0, pbase, a);
+      cost_targets<NCLS, false, true>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, wcls01, q0, pbase, a);
     }
   }
 }
@@ -588,11 +594,11 @@ extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
   a.w_giou = cost_giou;
   a.alpha = focal_alpha;
   // torch multiplies by the Python scalar (1 - alpha), rounded once to float32
-  a.one_minus_alpha = static_cast<float>(1.0 - static_cast<double>(focal_alpha));
+  a.alpha_m1 = -static_cast<float>(1.0 - static_cast<double>(focal_alpha));
   a.out = out;
 
   if (layout == RFM_LAYOUT_TARGET_MAJOR) {
-    const int64_t gy = (ld / 4 + kTmThreads - 1) / kTmThreads;
+    const int64_t gy = (ld / kQpt + kTmThreads - 1) / kTmThreads;
     const int64_t gx = (static_cast<int64_t>(sum_targets) + kTmCols - 1) / kTmCols;
     if (gy > 65535 || gx > 0x7fffffff) return RFM_ERR_UNSUPPORTED;
     const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy),

@@ -382,8 +382,10 @@ def run_rfm(args) -> None:
     lsap = {"kernel": "rfm lsap_kernel", "avg_launch_us": lsap_avg_s * 1e6,
             "problems_per_s": problems / lsap_avg_s, "algorithmic_bytes_per_launch": lb,
             "achieved_gbs": lb / lsap_avg_s / 1e9, "share_of_step": (sum(lsap_ms) / total_ms) if total_ms else None,
-            "cols_per_lane": plan.plan.cols_per_lane, "ctas": plan.plan.num_ctas,
-            "cta_smem_bytes": plan.plan.cta_smem_bytes, "workspace_bytes": int(plan.plan.workspace_bytes)}
+            "cols_per_lane": plan.plan.cols_per_lane,
+            "launch": "persistent warps (layout chosen at launch by batch size)"
+            if plan.plan.flags & _lib.PLAN_PERSISTENT else f"{plan.plan.num_ctas} planned CTAs",
+            "workspace_bytes": int(plan.plan.workspace_bytes)}
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:

@@ -140,6 +140,38 @@ def test_status_reports_invalid_costs():
         matcher.match_layers(outs, wl.targets_on(DEV), wl.group_detr, weights=wl.weights, check_status=True)
 
 
+def _narrow_batch(seed=21, images=800, group_detr=13, qg=64):
+    rng = np.random.default_rng(seed)
+    queries = group_detr * qg
+    sizes = np.clip(rng.poisson(8, images), 1, 60)
+    logits = rng.normal(-2.0, 1.5, (1, images, queries, 2)).astype(np.float32)
+    boxes = (1.0 / (1.0 + np.exp(-rng.normal(0.0, 1.0, (1, images, queries, 4))))).astype(np.float32)
+    labels = torch.as_tensor(np.concatenate([rng.integers(0, 2, t) for t in sizes]), device=DEV)
+    tboxes = torch.as_tensor(np.concatenate([np.concatenate([rng.uniform(0.1, 0.9, (t, 2)), rng.uniform(0.02, 0.5, (t, 2))],
+                                                            axis=1) for t in sizes]).astype(np.float32), device=DEV)
+    return (torch.as_tensor(logits, device=DEV), torch.as_tensor(boxes, device=DEV),
+            matcher.PackedTargets(labels, tboxes, tuple(int(t) for t in sizes)), group_detr)
+
+
+def test_large_batch_reports_invalid_problem_only():
+    """A NaN box in a 10,400-problem batch (the wide solver layout): exactly that (image, group)
+    problem reports invalid entries, writes -1 pairs, and every other pair is unchanged."""
+    logits, boxes, targets, group_detr = _narrow_batch()
+    clean = matcher.match_packed(logits, boxes, targets, group_detr)
+    bad_boxes = boxes.clone()
+    bad_boxes[0, 5, 70, 2] = float("nan")  # image 5, query 70 -> group 1
+    with pytest.raises(ValueError, match="invalid"):
+        matcher.match_packed(logits, bad_boxes, targets, group_detr, check_status=True)
+    res = matcher.match_packed(logits, bad_boxes, targets, group_detr)
+    torch.cuda.synchronize()
+    off = np.concatenate([[0], np.cumsum(res.per_image)])
+    t5 = targets.sizes[5]
+    lo = int(off[5]) + 1 * t5  # group 1 of image 5: pairs after group 0's t5 pairs
+    diff = (res.pairs != clean.pairs).any(dim=0).nonzero().flatten().cpu().numpy()
+    assert diff.min() >= lo and diff.max() < lo + t5
+    assert bool((res.pairs[:, lo:lo + t5] == -1).all())
+
+
 def test_large_batch_of_narrow_groups_against_oracle():
     """10,400 problems of 64 queries: a batch large enough for the solver's wide layout (duals and
     tie keys in shared memory) with the 128-column instantiation; indices identical to the C oracle

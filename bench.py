@@ -59,6 +59,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--cpu-images", type=int, default=64, help="images in one CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-production-step", action="store_true",
+                    help="skip the 5-layer x 8-image production-step timing (eager vs CUDA graph)")
     ap.add_argument("--sharded", action="store_true",
                     help="also time the strong-scaled sharded sweep (runs by default when N > 1)")
     return ap.parse_args()
@@ -362,6 +364,11 @@ def run_rfm(args) -> None:
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": float(e2e_t.item()) / args.steps}
 
+    # ---- production step (5 layers x 8 images x 13 groups, 520 problems): eager calls vs the CUDA graph
+    production = None
+    if world == 1 and not args.no_production_step:
+        production = production_step_timing(device, max(args.warmup, 3))
+
     # ---- sharded sweep: ONE 1024-image batch split across the ranks + NCCL all-gather of the pairs
     sharded_info = None
     if world > 1 or args.sharded:
@@ -403,12 +410,49 @@ def run_rfm(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32 cost, fp64 LSAP duals", "data": "synthetic",
             "config": workload_config(wl), "roofline": roofline, "lsap": lsap, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches, "clocks": clocks, "impl": "rfm", "sharded_sweep": sharded_info,
+            "production_step": production,
             "library": _lib.version(), "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms),
                                                   "max": max(step_ms)},
         }
         print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def production_step_timing(device, warmup: int, steps: int = 200) -> dict:
+    """The production step (5 decoder layers x 8 images x 13 groups of 300 queries, 520 problems),
+    inputs resident, steps issued back to back: wall-clock device time per step through
+    ``match_packed`` (host work on every call) and through a captured ``MatchGraph`` replay."""
+    from rfdetr_training_throughput_b200 import MatchGraph, matcher, workloads
+
+    wl = workloads.make("step")
+    logits, boxes = wl.pred_logits.to(device), wl.pred_boxes.to(device)
+    packed = matcher.PackedTargets.from_list(wl.targets_on(device), device)
+    graph = MatchGraph(wl.sizes, wl.layers, wl.queries, wl.classes, wl.group_detr, weights=wl.weights, device=device)
+    graph.logits.copy_(logits)
+    graph.boxes.copy_(boxes)
+    graph.labels.copy_(packed.labels)
+    graph.tgt_boxes.copy_(packed.boxes)
+
+    def eager():
+        matcher.match_packed(logits, boxes, packed, wl.group_detr, weights=wl.weights)
+
+    out = {"workload": "step: 5 layers x 8 images x 13 groups x 300 queries, 2 classes", "problems": wl.num_problems,
+           "steps": steps}
+    for name, fn in (("eager", eager), ("graph", graph.replay)):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / steps
+        out[f"{name}_ms_per_step"] = ms
+        out[f"{name}_problems_per_s"] = wl.num_problems / (ms / 1e3)
+    return out
 
 
 def run_sharded_sweep(args, world: int, rank: int, device, barrier) -> dict:

@@ -1,8 +1,10 @@
 """B200 (sm_100a) Hungarian matching for RF-DETR: fused cost kernel + exact batched LSAP.
 
 Public API: ``HungarianMatcher`` (drop-in for rf-detr's), ``match_layers``,
-``compute_compact_detection_cost_matrix``, ``assign_padded``,
-``batch_linear_assignment`` and ``install`` (monkeypatches an importable rf-detr).
+``match_packed``, ``compute_compact_detection_cost_matrix``, ``assign_padded``,
+``batch_linear_assignment``, ``MatchGraph`` / ``MatchGraphCache`` (the step as a
+CUDA graph for repeated shapes) and ``patches.apply_patches`` (monkeypatches an
+importable rf-detr).
 """
 
 from .matcher import (  # noqa: F401
@@ -11,4 +13,6 @@ from .matcher import (  # noqa: F401
     batch_linear_assignment,
     compute_compact_detection_cost_matrix,
     match_layers,
+    match_packed,
 )
+from .graph import MatchGraph, MatchGraphCache  # noqa: F401

@@ -686,13 +686,46 @@ const void* pair_kernel(int cols_per_lane, bool wide) {
   }
 }
 
+// Opts a kernel into `smem` bytes of dynamic shared memory once per device (the
+// attribute is then left raised): repeated launches, including launches being
+// captured into a CUDA graph, make no attribute call.
+struct SmemAttribute {
+  int device;
+  const void* fn;
+  int64_t smem;
+};
+std::mutex g_smem_mutex;
+std::vector<SmemAttribute> g_smem_attributes;
+
+bool ensure_dynamic_smem(const void* fn, int64_t smem) {
+  if (smem <= 48 * 1024) return true;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  std::lock_guard<std::mutex> lock(g_smem_mutex);
+  for (SmemAttribute& e : g_smem_attributes) {
+    if (e.device == dev && e.fn == fn) {
+      if (e.smem >= smem) return true;
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess) {
+        return false;
+      }
+      e.smem = smem;
+      return true;
+    }
+  }
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+      cudaSuccess) {
+    return false;
+  }
+  g_smem_attributes.push_back({dev, fn, smem});
+  return true;
+}
+
 // CTAs of a pair-mode kernel that fit on one SM at this shared-memory size.
 int query_resident_ctas(int cols_per_lane, bool wide, int64_t smem) {
   const void* fn = pair_kernel(cols_per_lane, wide);
   if (fn == nullptr) return 0;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-          cudaSuccess) {
+  if (!ensure_dynamic_smem(fn, smem)) {
     cudaGetLastError();
     return 0;
   }
@@ -752,11 +785,7 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
       break;
     default: return RFM_ERR_INVALID_ARGUMENT;
   }
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-          cudaSuccess) {
-    return launch_status();
-  }
+  if (!ensure_dynamic_smem(fn, smem)) return launch_status();
   const dim3 grid(static_cast<unsigned>(num_ctas));
   const dim3 block(32 * warps_per_cta);
   switch (cols_per_lane) {

@@ -366,8 +366,10 @@ def run_rfm(args) -> None:
 
     # ---- production step (5 layers x 8 images x 13 groups, 520 problems): eager calls vs the CUDA graph
     production = None
+    box_loss = None
     if world == 1 and not args.no_production_step:
         production = production_step_timing(device, max(args.warmup, 3))
+        box_loss = box_loss_timing(device, max(args.warmup, 3))
 
     # ---- sharded sweep: ONE 1024-image batch split across the ranks + NCCL all-gather of the pairs
     sharded_info = None
@@ -410,7 +412,7 @@ def run_rfm(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32 cost, fp64 LSAP duals", "data": "synthetic",
             "config": workload_config(wl), "roofline": roofline, "lsap": lsap, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches, "clocks": clocks, "impl": "rfm", "sharded_sweep": sharded_info,
-            "production_step": production,
+            "production_step": production, "box_loss": box_loss,
             "library": _lib.version(), "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms),
                                                   "max": max(step_ms)},
         }
@@ -452,6 +454,68 @@ def production_step_timing(device, warmup: int, steps: int = 200) -> dict:
         ms = e0.elapsed_time(e1) / steps
         out[f"{name}_ms_per_step"] = ms
         out[f"{name}_problems_per_s"] = wl.num_problems / (ms / 1e3)
+    return out
+
+
+def box_loss_timing(device, warmup: int, steps: int = 100) -> dict:
+    """The criterion's matched-box losses (L1 + GIoU, forward and backward) on the production step's
+    matched pairs: ``matched_box_losses`` (two kernels, no gathers) against the same loss written
+    with torch ops the way the DETR-family criterion writes it (index gathers, then the diagonal of
+    an N x N GIoU matrix per layer), both on the GPU."""
+    from rfdetr_training_throughput_b200 import matcher, workloads
+    from rfdetr_training_throughput_b200.loss import matched_box_losses
+
+    wl = workloads.make("step")
+    packed = matcher.PackedTargets.from_list(wl.targets_on(device), device)
+    pred0 = wl.pred_boxes.to(device)
+    res = matcher.match_packed(wl.pred_logits.to(device), pred0, packed, wl.group_detr, weights=wl.weights)
+    tgts = [t["boxes"] for t in wl.targets_on(device)]
+    per_layer = [res.layer(l) for l in range(wl.layers)]
+    batch_idx = [torch.cat([torch.full_like(q, b) for b, (q, _t) in enumerate(p)]) for p in per_layer]
+    src_idx = [torch.cat([q for q, _t in p]) for p in per_layer]
+    tgt_cat = [torch.cat([tgts[b][t] for b, (_q, t) in enumerate(p)]) for p in per_layer]
+
+    def xyxy(b):
+        cx, cy, w, h = b.unbind(-1)
+        return torch.stack([cx - 0.5 * w, cy - 0.5 * h, cx + 0.5 * w, cy + 0.5 * h], dim=-1)
+
+    def giou_matrix(b1, b2):
+        a1 = (b1[:, 2] - b1[:, 0]) * (b1[:, 3] - b1[:, 1])
+        a2 = (b2[:, 2] - b2[:, 0]) * (b2[:, 3] - b2[:, 1])
+        wh = (torch.min(b1[:, None, 2:], b2[:, 2:]) - torch.max(b1[:, None, :2], b2[:, :2])).clamp(min=0)
+        inter = wh[..., 0] * wh[..., 1]
+        union = a1[:, None] + a2 - inter
+        wh = (torch.max(b1[:, None, 2:], b2[:, 2:]) - torch.min(b1[:, None, :2], b2[:, :2])).clamp(min=0)
+        area = wh[..., 0] * wh[..., 1]
+        return inter / union - (area - union) / area
+
+    def torch_ops():
+        x = pred0.detach().requires_grad_(True)
+        total = 0.0
+        for l in range(wl.layers):
+            src = x[l][batch_idx[l], src_idx[l]]
+            total = total + torch.nn.functional.l1_loss(src, tgt_cat[l], reduction="none").sum()
+            total = total + (1 - torch.diag(giou_matrix(xyxy(src), xyxy(tgt_cat[l])))).sum()
+        total.backward()
+
+    def fused():
+        x = pred0.detach().requires_grad_(True)
+        l1, giou = matched_box_losses(x, packed, res)
+        (l1.sum() + giou.sum()).backward()
+
+    out = {"workload": "step matched pairs: 5 layers x 8 images x 13 groups", "pairs": int(res.pairs.shape[1]),
+           "steps": steps}
+    for name, fn in (("rfm", fused), ("torch_ops", torch_ops)):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        out[f"{name}_fwd_bwd_us"] = e0.elapsed_time(e1) * 1e3 / steps
     return out
 
 

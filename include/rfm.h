@@ -226,6 +226,41 @@ int rfm_lsap_dense(const float* cost, int num_problems, int num_workers, int num
 int rfm_lsap_dense_noalloc(const float* cost, int num_problems, int num_workers, int num_tasks,
                            int64_t* matching, int32_t* status, void* stream);
 
+/*
+ * Matched-box losses of the DETR-family criterion (SetCriterion.loss_boxes, the
+ * consumer of the matcher's indices: criterion.py:904/906 as cited at
+ * patches.py:339-341), read from the packed pairs rfm_lsap writes.  For every
+ * pair k of (layer l, image b) — query_idx[k], target_idx[k] for k in
+ * [pair_offsets[l*B + b], pair_offsets[l*B + b + 1]) — with p = pred_boxes[l, b, q]
+ * and t = tgt_boxes[off[b] + target] (cxcywh):
+ *
+ *   l1_part[l*B + b]   = sum_k |p - t|_1                         (4 coordinates)
+ *   giou_part[l*B + b] = sum_k (1 - GIoU(xyxy(p), xyxy(t)))       (unclamped GIoU)
+ *
+ * summed in a fixed order (deterministic).  Pairs holding -1 (an unsolved
+ * problem) or an index outside their image are skipped.  The caller sums the
+ * parts per layer and normalises by the number of boxes.
+ *
+ *   pred_boxes   [L, B, Q, 4] float32, 16-byte aligned
+ *   tgt_boxes    [S, 4] float32, 16-byte aligned; tgt_offsets [B + 1] int32
+ *   query_idx, target_idx  int64 pairs; pair_offsets [L*B + 1] int32
+ *
+ * rfm_box_loss_backward writes d/dpred of sum_l (grad_l1[l] * l1[l] +
+ * grad_giou[l] * giou[l]) into grad_pred [L, B, Q, 4] at every matched query's
+ * box (the caller zeroes the other entries); grad_l1, grad_giou are [L] device
+ * arrays.  Gradients follow torch's autograd of the same expressions (ties of
+ * min/max split evenly, clamp(min=0) passes at 0, |x| has slope sign(x)).
+ * No counterpart kernel in the reference.
+ */
+int rfm_box_loss_forward(const float* pred_boxes, const float* tgt_boxes, const int32_t* tgt_offsets,
+                         const int64_t* query_idx, const int64_t* target_idx, const int32_t* pair_offsets,
+                         int num_layers, int num_images, int num_queries, int sum_targets, float* l1_part,
+                         float* giou_part, void* stream);
+int rfm_box_loss_backward(const float* pred_boxes, const float* tgt_boxes, const int32_t* tgt_offsets,
+                          const int64_t* query_idx, const int64_t* target_idx, const int32_t* pair_offsets,
+                          int num_layers, int num_images, int num_queries, int sum_targets,
+                          const float* grad_l1, const float* grad_giou, float* grad_pred, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,8 @@ EXPORTS = (
     "rfm_lsap_dense_workspace_bytes",
     "rfm_lsap_dense",
     "rfm_lsap_dense_noalloc",
+    "rfm_box_loss_forward",
+    "rfm_box_loss_backward",
 )
 
 #: Size of the built-in scratch of rfm_lsap_dense_noalloc (RFM_NOALLOC_SCRATCH_BYTES).
@@ -127,6 +129,10 @@ def load() -> ctypes.CDLL:
     lib.rfm_lsap_dense_workspace_bytes.argtypes = [_i32, _i32, _i32]
     lib.rfm_lsap_dense.restype = _i32
     lib.rfm_lsap_dense.argtypes = [_p, _i32, _i32, _i32, _p, _p, _p, _p]
+    lib.rfm_box_loss_forward.restype = _i32
+    lib.rfm_box_loss_forward.argtypes = [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _p, _p]
+    lib.rfm_box_loss_backward.restype = _i32
+    lib.rfm_box_loss_backward.argtypes = [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _p, _p, _p]
     lib.rfm_lsap_dense_noalloc.restype = _i32
     lib.rfm_lsap_dense_noalloc.argtypes = [_p, _i32, _i32, _i32, _p, _p, _p]
     _lib = lib

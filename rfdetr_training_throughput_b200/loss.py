@@ -1,0 +1,102 @@
+"""Matched-box losses (L1 and GIoU over the matcher's pairs) with autograd, on the device.
+
+The DETR-family criterion's ``loss_boxes`` gathers the matched prediction boxes
+and target boxes with the matcher's index tensors (criterion.py:904/906, cited at
+patches.py:339-341), then takes the L1 of their cxcywh coordinates and the
+diagonal of an N x N generalized-IoU matrix, normalised by the number of boxes.
+``matched_box_losses`` computes the same two sums per decoder layer straight from
+a ``MatchResult`` (``rfm_box_loss_forward``), and its backward writes each matched
+query's box gradient in place (``rfm_box_loss_backward``): no gathers, no index
+tensors, no N x N matrix, no host synchronisation.  Normalisation (the criterion's
+``num_boxes``, which rf-detr averages over ranks) is left to the caller.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from functools import lru_cache
+
+import numpy as np
+import torch
+
+from . import _lib
+from .matcher import MatchResult, PackedTargets
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+@lru_cache(maxsize=64)
+def _offsets_cached(counts: tuple[int, ...], device: str) -> torch.Tensor:
+    off = np.zeros(len(counts) + 1, dtype=np.int32)
+    off[1:] = np.cumsum(counts)
+    return torch.from_numpy(off).to(device)
+
+
+_BY_ID: dict = {}
+
+
+def _offsets_on(counts: tuple[int, ...], device: str) -> torch.Tensor:
+    """Exclusive prefix sums of ``counts`` as a device int32 array, cached per counts tuple and,
+    for the tuples a training loop reuses every step, by the tuple object itself."""
+    key = (id(counts), device)
+    hit = _BY_ID.get(key)
+    if hit is not None and hit[0] is counts:
+        return hit[1]
+    t = _offsets_cached(counts, device)
+    if len(_BY_ID) >= 64:
+        _BY_ID.clear()
+    _BY_ID[key] = (counts, t)
+    return t
+
+
+class _MatchedBoxLoss(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pred_boxes, tgt_boxes, tgt_offsets, pairs, pair_offsets, layers, images):
+        queries = pred_boxes.shape[2]
+        parts = torch.empty((2, layers * images), dtype=torch.float32, device=pred_boxes.device)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(pred_boxes.device).cuda_stream)
+        _lib.check("rfm_box_loss_forward", _lib.load().rfm_box_loss_forward(
+            _ptr(pred_boxes), _ptr(tgt_boxes), _ptr(tgt_offsets), _ptr(pairs[0]), _ptr(pairs[1]),
+            _ptr(pair_offsets), layers, images, queries, tgt_boxes.shape[0], _ptr(parts[0]), _ptr(parts[1]),
+            stream))
+        ctx.save_for_backward(pred_boxes, tgt_boxes, tgt_offsets, pairs, pair_offsets)
+        ctx.layers, ctx.images = layers, images
+        sums = parts.view(2, layers, images).sum(dim=2)
+        return sums[0], sums[1]
+
+    @staticmethod
+    def backward(ctx, grad_l1, grad_giou):
+        pred_boxes, tgt_boxes, tgt_offsets, pairs, pair_offsets = ctx.saved_tensors
+        grad = torch.zeros_like(pred_boxes)
+        g1 = (torch.zeros(ctx.layers, device=pred_boxes.device) if grad_l1 is None else grad_l1).float().contiguous()
+        g2 = (torch.zeros(ctx.layers, device=pred_boxes.device) if grad_giou is None else grad_giou).float().contiguous()
+        stream = ctypes.c_void_p(torch.cuda.current_stream(pred_boxes.device).cuda_stream)
+        _lib.check("rfm_box_loss_backward", _lib.load().rfm_box_loss_backward(
+            _ptr(pred_boxes), _ptr(tgt_boxes), _ptr(tgt_offsets), _ptr(pairs[0]), _ptr(pairs[1]),
+            _ptr(pair_offsets), ctx.layers, ctx.images, pred_boxes.shape[2], tgt_boxes.shape[0], _ptr(g1),
+            _ptr(g2), _ptr(grad), stream))
+        return grad, None, None, None, None, None, None
+
+
+def matched_box_losses(pred_boxes: torch.Tensor, targets: PackedTargets,
+                       match: MatchResult) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-layer ``(sum of L1, sum of 1 - GIoU)`` over the matched pairs, differentiable in
+    ``pred_boxes`` ``[L, B, Q, 4]`` (cxcywh float32, the boxes the pairs were matched on)."""
+    if not pred_boxes.is_cuda:
+        raise ValueError("pred_boxes must be a CUDA tensor (this loss has no CPU path)")
+    if pred_boxes.dim() != 4 or pred_boxes.shape[-1] != 4:
+        raise ValueError("expected pred_boxes [L, B, Q, 4]")
+    layers, images = pred_boxes.shape[0], pred_boxes.shape[1]
+    if (match.layers, match.images) != (layers, images) or len(targets.sizes) != images:
+        raise ValueError("match, targets and pred_boxes disagree on layers or images")
+    pred = pred_boxes if pred_boxes.dtype == torch.float32 else pred_boxes.float()
+    pred = pred.contiguous()
+    if pred.data_ptr() % 16:
+        pred = pred.clone()
+    tg = targets.checked()
+    device = pred.device
+    tgt_offsets = _offsets_on(tg.sizes, str(device))
+    pair_offsets = _offsets_on(match.per_image_key, str(device))
+    return _MatchedBoxLoss.apply(pred, tg.boxes, tgt_offsets, match.pairs, pair_offsets, layers, images)

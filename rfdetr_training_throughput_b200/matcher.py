@@ -133,12 +133,21 @@ class MatchResult:
     per-image ``(query_idx, target_idx)`` views (no copy).
     """
 
-    def __init__(self, pairs: torch.Tensor, per_image: list[int], layers: int, images: int):
+    def __init__(self, pairs: torch.Tensor, per_image: list[int], layers: int, images: int,
+                 per_image_key: tuple[int, ...] | None = None):
         self.pairs = pairs
         self.per_image = per_image
         self.layers = layers
         self.images = images
         self._views = None
+        self._key = per_image_key
+
+    @property
+    def per_image_key(self) -> tuple[int, ...]:
+        """``per_image`` as a tuple (hashable; shared by every result of one step plan)."""
+        if self._key is None:
+            self._key = tuple(self.per_image)
+        return self._key
 
     def _split(self):
         if self._views is None:
@@ -175,6 +184,7 @@ class StepPlan:
     device_blob: torch.Tensor  # problems, then the int32 CTA table, then int32 offsets [B+1]
     ctas_byte: int
     offsets_byte: int
+    per_image_key: tuple = ()  # per_image as one shared tuple (a hashable cache key)
 
     @property
     def problems_ptr(self) -> int:
@@ -302,7 +312,7 @@ def plan_step(sizes: Sequence[int], layers: int, queries: int, group_detr: int, 
         host = torch.from_numpy(blob).pin_memory()
         dev = host.to(device, non_blocking=True)
         return StepPlan(sizes, layers, queries, group_detr, layout, ld, pr, order, plan, total, per_image, dev,
-                        ctas_byte, offsets_byte)
+                        ctas_byte, offsets_byte, tuple(per_image))
 
     return _PLANS.get(key, make)
 
@@ -426,7 +436,7 @@ def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: P
         raise_on_status(status)
     if extras is not None:
         extras.update(cost=cost, ld=ld, plan=plan, layout=layout)
-    return MatchResult(pairs, plan.per_image, layers, nimg)
+    return MatchResult(pairs, plan.per_image, layers, nimg, plan.per_image_key)
 
 
 def match_layers(outputs_list: Sequence[dict], targets: Sequence[dict] | PackedTargets, group_detr: int = 1, *,

@@ -80,23 +80,61 @@ class _MatchedBoxLoss(torch.autograd.Function):
         return grad, None, None, None, None, None, None
 
 
-def matched_box_losses(pred_boxes: torch.Tensor, targets: PackedTargets,
-                       match: MatchResult) -> tuple[torch.Tensor, torch.Tensor]:
-    """Per-layer ``(sum of L1, sum of 1 - GIoU)`` over the matched pairs, differentiable in
-    ``pred_boxes`` ``[L, B, Q, 4]`` (cxcywh float32, the boxes the pairs were matched on)."""
+def box_losses(pred_boxes: torch.Tensor, tgt_boxes: torch.Tensor, sizes: tuple[int, ...], pairs: torch.Tensor,
+               per_image: tuple[int, ...]) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-layer ``(sum of L1, sum of 1 - GIoU)`` over index pairs, differentiable in ``pred_boxes``.
+
+    ``pred_boxes`` ``[L, B, Q, 4]`` cxcywh; ``tgt_boxes`` ``[S, 4]`` packed, image ``b`` owning
+    ``sizes[b]`` rows; ``pairs`` int64 ``[2, N]`` (query index, target index within its image) in
+    ``L * B`` consecutive chunks of ``per_image`` pairs (layer-major).  Pairs holding -1 are skipped.
+    """
     if not pred_boxes.is_cuda:
         raise ValueError("pred_boxes must be a CUDA tensor (this loss has no CPU path)")
     if pred_boxes.dim() != 4 or pred_boxes.shape[-1] != 4:
         raise ValueError("expected pred_boxes [L, B, Q, 4]")
     layers, images = pred_boxes.shape[0], pred_boxes.shape[1]
-    if (match.layers, match.images) != (layers, images) or len(targets.sizes) != images:
-        raise ValueError("match, targets and pred_boxes disagree on layers or images")
+    if len(sizes) != images or len(per_image) != layers * images:
+        raise ValueError("sizes / per_image do not match pred_boxes' layers and images")
+    if pairs.dtype != torch.int64 or pairs.dim() != 2 or pairs.shape[0] != 2 or pairs.stride(1) != 1:
+        raise ValueError("pairs must be int64 [2, N] with contiguous rows")
     pred = pred_boxes if pred_boxes.dtype == torch.float32 else pred_boxes.float()
     pred = pred.contiguous()
     if pred.data_ptr() % 16:
         pred = pred.clone()
+    tgt = tgt_boxes.float().contiguous()
+    if tgt.data_ptr() % 16:
+        tgt = tgt.clone()
+    device = str(pred.device)
+    return _MatchedBoxLoss.apply(pred, tgt, _offsets_on(sizes, device), pairs, _offsets_on(per_image, device),
+                                 layers, images)
+
+
+def matched_box_losses(pred_boxes: torch.Tensor, targets: PackedTargets,
+                       match: MatchResult) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-layer ``(sum of L1, sum of 1 - GIoU)`` over a ``MatchResult``'s pairs, differentiable in
+    ``pred_boxes`` ``[L, B, Q, 4]`` (cxcywh float32, the boxes the pairs were matched on)."""
+    if (match.layers, match.images) != tuple(pred_boxes.shape[:2]) or len(targets.sizes) != pred_boxes.shape[1]:
+        raise ValueError("match, targets and pred_boxes disagree on layers or images")
     tg = targets.checked()
+    return box_losses(pred_boxes, tg.boxes, tg.sizes, match.pairs, match.per_image_key)
+
+
+def criterion_loss_boxes(outputs: dict, targets, indices, num_boxes) -> dict:
+    """DETR's ``SetCriterion.loss_boxes(outputs, targets, indices, num_boxes)`` contract on one
+    layer: ``{"loss_bbox": sum L1 / num_boxes, "loss_giou": sum (1 - GIoU) / num_boxes}`` over
+    ``indices`` (one ``(query_idx, target_idx)`` pair of int64 tensors per image)."""
+    pred = outputs["pred_boxes"]
+    if len(indices) != pred.shape[0] or len(targets) != pred.shape[0]:
+        raise ValueError("one (query_idx, target_idx) pair and one target dict per image expected")
+    counts = tuple(int(q.shape[0]) for q, _t in indices)  # host-known shapes: no synchronisation
     device = pred.device
-    tgt_offsets = _offsets_on(tg.sizes, str(device))
-    pair_offsets = _offsets_on(match.per_image_key, str(device))
-    return _MatchedBoxLoss.apply(pred, tg.boxes, tgt_offsets, match.pairs, pair_offsets, layers, images)
+    if sum(counts):
+        pairs = torch.stack([torch.cat([q.to(device, torch.int64) for q, _t in indices]),
+                             torch.cat([t.to(device, torch.int64) for _q, t in indices])])
+    else:
+        pairs = torch.zeros((2, 0), dtype=torch.int64, device=device)
+    sizes = tuple(int(t["boxes"].shape[0]) for t in targets)
+    tgt = torch.cat([t["boxes"].reshape(-1, 4) for t in targets]).to(device) if targets else \
+        torch.zeros((0, 4), device=device)
+    l1, giou = box_losses(pred.unsqueeze(0), tgt, sizes, pairs, counts)
+    return {"loss_bbox": l1[0] / num_boxes, "loss_giou": giou[0] / num_boxes}

@@ -15,6 +15,9 @@ which applies them in order, returns one description per patch and raises
                     (patches.py:235-249)
 ``matcher``         ``HungarianMatcher.forward`` -> the two-launch device step (new: the
                     whole matcher in one call, detection outputs only)
+``box_loss``        ``SetCriterion.loss_boxes`` -> ``rfm_box_loss_forward/backward`` on the
+                    matcher's index pairs (new: the criterion consumer of the indices,
+                    DETR's loss_boxes contract)
 
 Unlike the reference there is no fallback to the original implementation for
 CPU tensors or out-of-envelope inputs: the patched functions raise instead.
@@ -82,12 +85,24 @@ def _apply_matcher() -> str:
     return "matcher: HungarianMatcher.forward runs the two-launch device step"
 
 
+def _apply_box_loss() -> str:
+    cls = _module("rfdetr.models.criterion").SetCriterion
+    from .loss import criterion_loss_boxes
+
+    def loss_boxes(self, outputs, targets, indices, num_boxes):
+        return criterion_loss_boxes(outputs, targets, indices, num_boxes)
+
+    cls.loss_boxes = loss_boxes
+    return "box_loss: SetCriterion.loss_boxes computed from the index pairs by the sm_100a loss kernels"
+
+
 PATCHES: dict[str, Callable[[], str]] = {
     "triton_matcher": _apply_triton_matcher,
     "cuda_lap": _apply_cuda_lap,
     "device_indices": _apply_device_indices,
     "stacked_costs": _apply_stacked_costs,
     "matcher": _apply_matcher,
+    "box_loss": _apply_box_loss,
 }
 
 

@@ -98,3 +98,28 @@ def test_box_losses_are_deterministic_and_sync_free():
     torch.cuda.synchronize()
     for l1, giou in again:
         assert torch.equal(l1, first[0]) and torch.equal(giou, first[1])
+
+
+def test_criterion_contract_on_index_lists():
+    """criterion_loss_boxes (the box_loss patch): DETR's loss_boxes(outputs, targets, indices,
+    num_boxes) on one layer's per-image index tuples, against the torch reference."""
+    from rfdetr_training_throughput_b200.loss import criterion_loss_boxes
+
+    wl = workloads.make("step", layers=1)
+    targets = wl.targets_on(DEV)
+    outputs = wl.outputs_list(DEV)[0]
+    indices = matcher.match_layers([outputs], targets, wl.group_detr, weights=wl.weights)[0]
+    x = outputs["pred_boxes"].clone().requires_grad_(True)
+    num_boxes = 17.0
+    losses = criterion_loss_boxes({"pred_boxes": x}, targets, indices, num_boxes)
+    (losses["loss_bbox"] + 2.0 * losses["loss_giou"]).backward()
+    torch.cuda.synchronize()
+    ref = x.detach().cpu().requires_grad_(True)
+    src = torch.cat([ref[b, q.cpu()] for b, (q, _t) in enumerate(indices)])
+    tgt = torch.cat([targets[b]["boxes"].cpu()[t.cpu()] for b, (_q, t) in enumerate(indices)])
+    r_bbox = torch.nn.functional.l1_loss(src, tgt, reduction="none").sum() / num_boxes
+    r_giou = (1 - torch.diag(_generalized_box_iou(_xyxy(src), _xyxy(tgt)))).sum() / num_boxes
+    (r_bbox + 2.0 * r_giou).backward()
+    np.testing.assert_allclose(losses["loss_bbox"].item(), r_bbox.item(), rtol=1e-5)
+    np.testing.assert_allclose(losses["loss_giou"].item(), r_giou.item(), rtol=1e-5)
+    np.testing.assert_allclose(x.grad.cpu().numpy(), ref.grad.numpy(), rtol=1e-4, atol=1e-6)

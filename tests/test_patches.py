@@ -26,10 +26,12 @@ def fake_rfdetr(monkeypatch):
         "rfdetr.models": types.ModuleType("rfdetr.models"),
         "rfdetr.models.matcher": types.ModuleType("rfdetr.models.matcher"),
         "rfdetr.models._assignment": types.ModuleType("rfdetr.models._assignment"),
+        "rfdetr.models.criterion": types.ModuleType("rfdetr.models.criterion"),
         "torch_linear_assignment": types.ModuleType("torch_linear_assignment"),
         "torch_linear_assignment.assignment": types.ModuleType("torch_linear_assignment.assignment"),
     }
     mods["rfdetr.models.matcher"].HungarianMatcher = HungarianMatcher
+    mods["rfdetr.models.criterion"].SetCriterion = type("SetCriterion", (), {"loss_boxes": lambda *a: "upstream"})
     mods["rfdetr.models.matcher"]._STACKED_COST_ELEMENT_LIMIT = 350_000
     mods["rfdetr.models._assignment"]._assign_padded = lambda *a: "upstream"
     mods["torch_linear_assignment.assignment"].batch_linear_assignment = lambda c: "upstream"
@@ -40,8 +42,8 @@ def fake_rfdetr(monkeypatch):
 
 
 def test_apply_patches_rebinds_the_reference_names(fake_rfdetr):
-    done = patches.apply_patches("triton_matcher, cuda_lap,device_indices,stacked_costs,matcher")
-    assert len(done) == 5 and all(":" in d for d in done)
+    done = patches.apply_patches("triton_matcher, cuda_lap,device_indices,stacked_costs,matcher,box_loss")
+    assert len(done) == 6 and all(":" in d for d in done)
     cls = fake_rfdetr["rfdetr.models.matcher"].HungarianMatcher
     assert fake_rfdetr["torch_linear_assignment.assignment"].batch_linear_assignment is matcher.batch_linear_assignment
     assert fake_rfdetr["torch_linear_assignment"].batch_linear_assignment is matcher.batch_linear_assignment
@@ -55,6 +57,10 @@ def test_apply_patches_rebinds_the_reference_names(fake_rfdetr):
         m._compute_compact_detection_cost_matrix(outputs, targets)
     with pytest.raises(ValueError, match="CUDA"):
         fake_rfdetr["rfdetr.models._assignment"]._assign_padded([torch.zeros(3, 1)], [1], 3, 1)
+    crit = fake_rfdetr["rfdetr.models.criterion"].SetCriterion()
+    with pytest.raises(ValueError, match="CUDA"):
+        crit.loss_boxes({"pred_boxes": torch.zeros(1, 3, 4)}, targets,
+                        [(torch.zeros(1, dtype=torch.int64), torch.zeros(1, dtype=torch.int64))], 1.0)
 
 
 def test_unknown_patch_name_raises_keyerror():

@@ -171,6 +171,10 @@ def dist_init(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        # NCCL's own log lines (its version banner included) go to stderr: stdout carries only
+        # rank 0's JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     return world, rank, local
 
 

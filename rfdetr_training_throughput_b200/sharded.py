@@ -69,8 +69,23 @@ class _Shard:
 
 
 @lru_cache(maxsize=64)
-def _shard(sizes: tuple[int, ...], layers: int, queries: int, group_detr: int, world: int, rank: int) -> _Shard:
+def _shard_cached(sizes: tuple[int, ...], layers: int, queries: int, group_detr: int, world: int,
+                  rank: int) -> _Shard:
     return _Shard(sizes, layers, queries, group_detr, world, rank)
+
+
+_LAST_SHARD: list = [None]  # (sizes object, rest of the key, shard) of the last call
+
+
+def _shard(sizes: tuple[int, ...], layers: int, queries: int, group_detr: int, world: int, rank: int) -> _Shard:
+    """The cached split; a loop that passes the same sizes object every step skips hashing it."""
+    rest = (layers, queries, group_detr, world, rank)
+    last = _LAST_SHARD[0]
+    if last is not None and last[0] is sizes and last[1] == rest:
+        return last[2]
+    sh = _shard_cached(sizes, *rest)
+    _LAST_SHARD[0] = (sizes, rest, sh)
+    return sh
 
 
 def _unpad(recv: torch.Tensor, counts: Sequence[int]) -> torch.Tensor:

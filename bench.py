@@ -171,10 +171,6 @@ def dist_init(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        # NCCL's own log lines (its version banner included) go to stderr: stdout carries only
-        # rank 0's JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     return world, rank, local
 
 
@@ -253,7 +249,7 @@ def run_reference(args) -> None:
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     line["config"]["cpu_sample"] = sample
-    print(json.dumps(line))
+    emit(line)
 
 
 # --------------------------------------------------------------------------- GPU path
@@ -420,7 +416,7 @@ def run_rfm(args) -> None:
             "library": _lib.version(), "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms),
                                                   "max": max(step_ms)},
         }
-        print(json.dumps(line))
+        emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
 
@@ -564,8 +560,27 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier) -> dict:
             "collective": "all_gather_into_tensor of int64 [2, pairs] per rank" if world > 1 else "none (1 rank)"}
 
 
+_RESULT_FD: list = [None]
+
+
+def emit(line: dict) -> None:
+    """Write the one JSON result line to the process's original stdout."""
+    fd = _RESULT_FD[0]
+    text = json.dumps(line) + "\n"
+    if fd is None:
+        sys.stdout.write(text)
+        sys.stdout.flush()
+    else:
+        os.write(fd, text.encode())
+
+
 def main() -> None:
     args = parse()
+    # Everything else anything in the process writes to stdout (library banners such as NCCL's
+    # version line under torchrun) goes to stderr, so stdout carries the JSON line alone.
+    sys.stdout.flush()
+    _RESULT_FD[0] = os.dup(1)
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
     else:

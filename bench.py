@@ -521,7 +521,9 @@ def box_loss_timing(device, warmup: int, steps: int = 100) -> dict:
 
 def run_sharded_sweep(args, world: int, rank: int, device, barrier) -> dict:
     """Strong scaling: the sweep's one 1024-image batch split by image over the ranks, every rank
-    matching its range, then one all-gather of the packed int64 pairs (NCCL over NVLink)."""
+    matching its range, then one all-gather of the packed int64 pairs (NCCL over NVLink).  Timed
+    twice: through ``sharded_match`` (host planning work on every call) and through a
+    ``ShardedMatcher`` (this rank's step replayed as a CUDA graph into the gather's send buffer)."""
     from rfdetr_training_throughput_b200 import sharded, workloads
 
     wl = workloads.make(args.workload, images=args.images)  # the same batch on every rank
@@ -531,32 +533,49 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier) -> dict:
     boxes = wl.pred_boxes[:, lo:hi].to(device)
     labels = torch.cat([t["labels"] for t in wl.targets])[offs[lo]:offs[hi]].to(device)
     tboxes = torch.cat([t["boxes"] for t in wl.targets])[offs[lo]:offs[hi]].to(device)
-
     sizes = tuple(wl.sizes)
-
-    def step():
-        return sharded.sharded_match(logits, boxes, labels, tboxes, sizes, wl.group_detr, weights=wl.weights)
-
-    for _ in range(max(args.warmup, 1)):
-        pairs, _per = step()
     steps = max(1, min(args.steps, 100))
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    barrier()
-    torch.cuda.synchronize(device)
-    for k in range(steps):
-        starts[k].record()
-        pairs, _per = step()
-        ends[k].record()
-    torch.cuda.synchronize(device)
-    barrier()
-    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], dtype=torch.float64, device=device)
-    if world > 1:
-        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-    total_ms = float(ms.item())
+
+    def eager():
+        return sharded.sharded_match(logits, boxes, labels, tboxes, sizes, wl.group_detr, weights=wl.weights)[0]
+
+    matcher_graph = sharded.ShardedMatcher(sizes, wl.layers, wl.queries, wl.classes, wl.group_detr,
+                                           weights=wl.weights, device=device)
+    matcher_graph.graph.logits.copy_(logits)
+    matcher_graph.graph.boxes.copy_(boxes)
+    matcher_graph.graph.labels.copy_(labels)
+    matcher_graph.graph.tgt_boxes.copy_(tboxes)
+
+    def replayed():
+        matcher_graph.graph.replay()
+        return matcher_graph.gather()
+
+    def timed(fn) -> tuple[float, torch.Tensor]:
+        for _ in range(max(args.warmup, 1)):
+            out = fn()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        barrier()
+        torch.cuda.synchronize(device)
+        for k in range(steps):
+            starts[k].record()
+            out = fn()
+            ends[k].record()
+        torch.cuda.synchronize(device)
+        barrier()
+        ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], dtype=torch.float64, device=device)
+        if world > 1:
+            torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+        return float(ms.item()) / steps, out
+
+    eager_ms, pairs = timed(eager)
+    graph_ms, pairs_g = timed(replayed)
+    same = bool(torch.equal(pairs, pairs_g))
+    del matcher_graph  # its graph holds no collective, but release it before the process group goes
     return {"images": wl.images, "problems_per_step": wl.num_problems, "steps": steps,
-            "ms_per_step": total_ms / steps, "problems_per_s": wl.num_problems * steps / (total_ms / 1e3),
-            "gathered_pairs": int(pairs.shape[1]), "scaling": "strong",
+            "ms_per_step": graph_ms, "problems_per_s": wl.num_problems / (graph_ms / 1e3),
+            "eager_ms_per_step": eager_ms, "eager_problems_per_s": wl.num_problems / (eager_ms / 1e3),
+            "graph_equals_eager": same, "gathered_pairs": int(pairs.shape[1]), "scaling": "strong",
             "collective": "all_gather_into_tensor of int64 [2, pairs] per rank" if world > 1 else "none (1 rank)"}
 
 

@@ -12,8 +12,9 @@ crops, padded batches, a validation set) reuse one graph per distinct shape;
 
 The graph reads its inputs from its own device buffers (``logits``, ``boxes``,
 ``labels``, ``tgt_boxes``) and writes the pairs of every replay to the same
-``pairs`` buffer: copy new inputs in (``__call__`` does) and read or copy the
-result before the next replay.  Stream capture covers the cost kernel, the
+``pairs`` buffer (its own, or the ``out`` tensor given at construction): copy
+new inputs in (``__call__`` does) and read or copy the result before the next
+replay.  Stream capture covers the cost kernel, the
 solver's queue reset and the solver kernel; plans and launch parameters are
 host-side values fixed at capture time, which is exactly what a fixed shape
 pins.
@@ -33,7 +34,8 @@ class MatchGraph:
     """One matcher step of a fixed shape, captured as a CUDA graph on ``device``."""
 
     def __init__(self, sizes: Sequence[int], layers: int, queries: int, num_classes: int, group_detr: int, *,
-                 weights: dict | None = None, device: torch.device | None = None, warmup: int = 2):
+                 weights: dict | None = None, device: torch.device | None = None, warmup: int = 2,
+                 out: torch.Tensor | None = None):
         if not torch.cuda.is_available():
             raise RuntimeError("MatchGraph needs a CUDA device (there is no CPU path)")
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -48,6 +50,7 @@ class MatchGraph:
         self.labels = torch.zeros(total, dtype=torch.int64, device=device)
         self.tgt_boxes = torch.full((total, 4), 0.25, dtype=torch.float32, device=device)
         self._targets = PackedTargets.from_checked_sizes(self.labels, self.tgt_boxes, self.sizes, total)
+        self._out = out  # optional caller buffer the pairs are written into (e.g. a collective's send buffer)
 
         side = torch.cuda.Stream(device)
         side.wait_stream(torch.cuda.current_stream(device))
@@ -61,7 +64,8 @@ class MatchGraph:
         self.pairs = self.result.pairs
 
     def _step(self) -> MatchResult:
-        return match_packed(self.logits, self.boxes, self._targets, self.group_detr, weights=self.weights)
+        return match_packed(self.logits, self.boxes, self._targets, self.group_detr, weights=self.weights,
+                            out=self._out)
 
     def replay(self) -> MatchResult:
         """Re-run the captured step on the current contents of the input buffers."""

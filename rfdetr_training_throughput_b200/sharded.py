@@ -145,3 +145,38 @@ def sharded_match(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: t
         return _unpad(recv, sh.counts), sh.per
     local = local_solver(pred_logits, pred_boxes, labels, boxes, list(sh.local_sizes), group_detr)
     return gather_pairs(local, sh.counts, group), sh.per
+
+
+class ShardedMatcher:
+    """``sharded_match`` for a batch shape that repeats: this rank's step is a captured
+    ``MatchGraph`` writing straight into the all-gather's send buffer, so a call is one graph
+    replay, one ``all_gather_into_tensor`` and one concatenation.  Inputs are this rank's
+    image range (``pred_logits`` ``[L, hi - lo, Q, C]`` etc.); construct it on every rank of
+    ``group`` with the same arguments."""
+
+    def __init__(self, sizes: Sequence[int], layers: int, queries: int, num_classes: int, group_detr: int, *,
+                 weights: dict | None = None, group=None, device: torch.device | None = None):
+        from .graph import MatchGraph
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        sizes = tuple(int(s) for s in sizes)
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.shard = _shard(sizes, layers, queries, group_detr, self.world, self.rank)
+        self.send, self.recv = self.shard.gather_buffers(device, self.world)
+        n = self.shard.counts[self.rank]
+        self.graph = MatchGraph(self.shard.local_sizes, layers, queries, num_classes, group_detr, weights=weights,
+                                device=device, out=self.send[0, :, :n])
+        self.bounds = (self.shard.lo, self.shard.hi)
+        self.per_image = self.shard.per
+
+    def gather(self) -> torch.Tensor:
+        """All-gather the pairs the last replay wrote; ``[2, total]`` in rank order."""
+        dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        return _unpad(self.recv, self.shard.counts)
+
+    def __call__(self, pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: torch.Tensor,
+                 tgt_boxes: torch.Tensor) -> torch.Tensor:
+        self.graph(pred_logits, pred_boxes, labels, tgt_boxes)
+        return self.gather()

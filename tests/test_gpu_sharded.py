@@ -61,3 +61,18 @@ def test_match_packed_out_argument_is_checked():
     with pytest.raises(ValueError):
         matcher.match_packed(wl.pred_logits.to(dev), wl.pred_boxes.to(dev), packed, wl.group_detr,
                              weights=wl.weights, out=torch.empty((2, 3), dtype=torch.int64, device=dev))
+
+
+def test_sharded_matcher_graph_equals_match_packed(one_rank_group):
+    dev = torch.device("cuda", 0)
+    wl = workloads.make("sweep", images=40)
+    logits, boxes = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)
+    packed = matcher.PackedTargets.from_list(wl.targets_on(dev), dev)
+    expect = matcher.match_packed(logits, boxes, packed, wl.group_detr, weights=wl.weights)
+    sm = sharded.ShardedMatcher(wl.sizes, wl.layers, wl.queries, wl.classes, wl.group_detr, weights=wl.weights,
+                                device=dev)
+    for _ in range(2):
+        pairs = sm(logits, boxes, packed.labels, packed.boxes)
+        torch.cuda.synchronize()
+        assert torch.equal(pairs, expect.pairs)
+    assert sm.per_image == expect.per_image

@@ -61,16 +61,23 @@ constexpr int kSmemPerCtaReserved = 1024;
 constexpr int kSmemPerBlockMax = 227 * 1024;
 constexpr int64_t kTileCapDefault = 16384;  // floats: 64 KB of staged cost per warp
 constexpr int kMaxWarpsPerCta = 4;
+// Solver variants: REGS keeps column duals and tie keys in registers; WIDE keeps
+// them in shared memory (large batches); EARLY is REGS with each scan's row
+// requested as soon as the row is known, before the previous step's
+// bookkeeping, which pays off when searches run long (batches whose problems
+// have at least kEarlyMinRows rows).
+enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2 };
+constexpr int kEarlyMinRows = 64;
+// Batches with more than this many problems per SM use the wide layout.
+constexpr int kWideProblemsPerSm = 64;
 // Register budget.  The instantiations up to 320 columns run four CTAs of four
 // warps per SM (at most 128 registers a thread), or six in the wide layout,
 // which keeps the column duals and tie keys in shared memory (at most 85): more
 // resident warps for large batches at a longer chain per problem.  The
 // 1024-column one keeps its per-lane arrays in registers.
-__host__ __device__ constexpr int min_ctas_per_sm(int cols_per_lane, bool wide) {
-  return cols_per_lane > 10 ? 1 : (wide ? 6 : 4);
+__host__ __device__ constexpr int min_ctas_per_sm(int cols_per_lane, int variant) {
+  return cols_per_lane > 10 ? 1 : (variant == kVarWide ? 6 : 4);
 }
-// Batches with more than this many problems per SM use the wide layout.
-constexpr int kWideProblemsPerSm = 64;
 // Shared-memory budget of one CTA: four CTAs of four warps fill an SM.
 constexpr int kCtaBudget = kSmemPerSm / 4 - kSmemPerCtaReserved;
 // Tie keys: a free column at position pos gets kKeyBase - 1 - pos, a matched one
@@ -197,19 +204,24 @@ __device__ __forceinline__ float load_cost(const float* p) {
   return __ldcg(p);
 }
 
-// One scan step of the augmenting-path search over the lane's columns.  The
-// lane's loads are all issued before the first is used (a row read from
-// global memory then costs one round trip, not one per column).  Column duals
-// and tie keys come from registers, or in the wide layout from shared memory
-// (a key only when its column ties or beats the lane's best so far).
-template <int K, int L, bool kWide>
-__device__ __forceinline__ void scan_row(const float* row, int lane, int i, double minv, double ui,
+// Issues the loads of one row's costs at the lane's columns in `mask`.
+template <int K, int L>
+__device__ __forceinline__ void load_row(const float* row, int lane, unsigned mask, float (&cf)[K]) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) cf[k] = (mask & (1u << k)) ? load_cost<L>(row + lane + 32 * k) : 0.0f;
+}
+
+// One scan step of the augmenting-path search over the lane's columns, on a
+// row whose costs load_row() requested into cf (all of a lane's loads are in
+// flight before the first is used: a row read from memory costs one round
+// trip, not one per column).  Column duals and tie keys come from registers,
+// or in the wide layout from shared memory (a key only when its column ties or
+// beats the lane's best so far).
+template <int K, bool kWide>
+__device__ __forceinline__ void scan_row(const float (&cf)[K], int lane, int i, double minv, double ui,
                                          const double (&v)[K], const double* v_s, double (&spc)[K],
                                          const unsigned (&key)[K], const uint16_t* key_s, unsigned rem,
                                          int16_t* path_s, double& bv, unsigned& bk) {
-  float cf[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) cf[k] = (rem & (1u << k)) ? load_cost<L>(row + lane + 32 * k) : 0.0f;
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     if (rem & (1u << k)) {
@@ -234,6 +246,7 @@ __device__ __forceinline__ void scan_row(const float* row, int lane, int i, doub
     }
   }
 }
+
 
 
 
@@ -280,10 +293,12 @@ __device__ __forceinline__ void record_first_pick(const float (&x)[K], int lane,
 }
 
 // Solves problem p with the warp's shared-memory slot at `base` (`slot` bytes).
-template <int K, bool kDense, bool kWide>
+template <int K, bool kDense, int kVariant>
 __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned char* base, int slot,
                                               int lane) {
   constexpr int kCols = 32 * K;
+  constexpr bool kWide = kVariant == kVarWide;
+  constexpr bool kEarly = kVariant == kVarEarly;
   int64_t cost_off, out_off, scratch_off;
   int nq, nt, qbase;
   if (kDense) {
@@ -476,31 +491,35 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
     double minv = 0.0;
     __syncwarp();
 
+    float cf[K];
+    const auto issue_row = [&](int r) {
+      const float* row = rows + r * row_pitch;
+      if (mode == kModeShared) {
+        load_row<K, kLoadShared>(row, lane, rem, cf);
+      } else if (mode == kModeDirect) {
+        load_row<K, kLoadGlobal>(row, lane, rem, cf);
+      } else {
+        load_row<K, kLoadScratch>(row, lane, rem, cf);
+      }
+    };
+    if (kEarly) issue_row(cur);
     for (int it = 0; it < nc; ++it) {
+      if (!kEarly) issue_row(i);
       const double ui = u_s[i];
       double bv = CUDART_INF;
       unsigned bk = kNoKey;
-      const float* row = rows + i * row_pitch;
-      if (mode == kModeShared) {
-        scan_row<K, kLoadShared, kWide>(row, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv,
-                                     bk);
-      } else if (mode == kModeDirect) {
-        scan_row<K, kLoadGlobal, kWide>(row, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv,
-                                     bk);
-      } else {
-        scan_row<K, kLoadScratch, kWide>(row, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv,
-                                     bk);
-      }
+      scan_row<K, kWide>(cf, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv, bk);
       warp_argmin(bv, bk);
       if (bv == CUDART_INF) {
         code = RFM_STATUS_INFEASIBLE;
         break;
       }
       const int ps = static_cast<int>(bk < kKeyBase ? kKeyBase - 1u - bk : bk - kKeyBase);
-      const int last = nrem - 1;
       const int js = rem_s[ps];
-      const int jl = rem_s[last];
       const int rj = row4col_s[js];
+      if (kEarly && rj >= 0) issue_row(rj);  // the next scan's row, before this step's bookkeeping
+      const int last = nrem - 1;
+      const int jl = rem_s[last];
       __syncwarp();
       if (lane == 0) rem_s[ps] = static_cast<int16_t>(jl);  // swap-with-last removal
       if ((jl & 31) == lane) {
@@ -620,15 +639,15 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
   if (a.status != nullptr && lane == 0) a.status[p] = code;
 }
 
-template <int K, bool kDense, bool kWide>
-__global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kWide)) lsap_kernel(const LsapArgs a) {
+template <int K, bool kDense, int kVariant>
+__global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVariant)) lsap_kernel(const LsapArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   if (kDense) {
     const int p = blockIdx.x * a.dense_warps + warp;
     if (p < a.num_problems) {
-      solve_problem<K, kDense, kWide>(a, p, smem_raw + static_cast<int64_t>(warp) * a.slot, a.slot, lane);
+      solve_problem<K, kDense, kVariant>(a, p, smem_raw + static_cast<int64_t>(warp) * a.slot, a.slot, lane);
     }
   } else if (a.queue != nullptr) {
     // persistent warps: pull problems (sorted largest first) until none is left
@@ -638,13 +657,13 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kWide
       if (lane == 0) p = atomicAdd(a.queue, 1);
       p = __shfl_sync(kFullMask, p, 0);
       if (p >= a.num_problems) break;
-      solve_problem<K, kDense, kWide>(a, p, base, a.slot, lane);
+      solve_problem<K, kDense, kVariant>(a, p, base, a.slot, lane);
       __syncwarp();
     }
   } else {
     const int4 cta = a.ctas[blockIdx.x];
     if (warp < cta.y) {
-      solve_problem<K, kDense, kWide>(a, cta.x + warp, smem_raw + static_cast<int64_t>(warp) * cta.z, cta.z,
+      solve_problem<K, kDense, kVariant>(a, cta.x + warp, smem_raw + static_cast<int64_t>(warp) * cta.z, cta.z,
                                lane);
     }
   }
@@ -673,15 +692,22 @@ int sm_count() {
   return n;
 }
 
-// The pair-mode kernel for a column count and layout (the wide layout exists
+// The pair-mode kernel for a column count and variant (the wide layout exists
 // for up to 320 columns).
-const void* pair_kernel(int cols_per_lane, bool wide) {
+const void* pair_kernel(int cols_per_lane, int variant) {
   switch (cols_per_lane) {
-    case 4: return wide ? reinterpret_cast<const void*>(&lsap_kernel<4, false, true>)
-                        : reinterpret_cast<const void*>(&lsap_kernel<4, false, false>);
-    case 10: return wide ? reinterpret_cast<const void*>(&lsap_kernel<10, false, true>)
-                         : reinterpret_cast<const void*>(&lsap_kernel<10, false, false>);
-    case 32: return wide ? nullptr : reinterpret_cast<const void*>(&lsap_kernel<32, false, false>);
+    case 4:
+      if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarWide>);
+      if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarEarly>);
+      return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarRegs>);
+    case 10:
+      if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarWide>);
+      if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarEarly>);
+      return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarRegs>);
+    case 32:
+      if (variant == kVarWide) return nullptr;
+      if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarEarly>);
+      return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarRegs>);
     default: return nullptr;
   }
 }
@@ -722,8 +748,8 @@ bool ensure_dynamic_smem(const void* fn, int64_t smem) {
 }
 
 // CTAs of a pair-mode kernel that fit on one SM at this shared-memory size.
-int query_resident_ctas(int cols_per_lane, bool wide, int64_t smem) {
-  const void* fn = pair_kernel(cols_per_lane, wide);
+int query_resident_ctas(int cols_per_lane, int variant, int64_t smem) {
+  const void* fn = pair_kernel(cols_per_lane, variant);
   if (fn == nullptr) return 0;
   if (!ensure_dynamic_smem(fn, smem)) {
     cudaGetLastError();
@@ -742,14 +768,14 @@ int query_resident_ctas(int cols_per_lane, bool wide, int64_t smem) {
 // occupancy query and the attribute call cost a few microseconds per launch.
 struct OccupancyEntry {
   int device, cols_per_lane;
-  bool wide;
+  int variant;
   int64_t smem;
   int ctas;
 };
 std::mutex g_occupancy_mutex;
 std::vector<OccupancyEntry> g_occupancy;
 
-int resident_ctas(int cols_per_lane, bool wide, int64_t smem) {
+int resident_ctas(int cols_per_lane, int variant, int64_t smem) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
@@ -758,30 +784,30 @@ int resident_ctas(int cols_per_lane, bool wide, int64_t smem) {
   {
     std::lock_guard<std::mutex> lock(g_occupancy_mutex);
     for (const OccupancyEntry& e : g_occupancy) {
-      if (e.device == dev && e.cols_per_lane == cols_per_lane && e.wide == wide && e.smem == smem) {
+      if (e.device == dev && e.cols_per_lane == cols_per_lane && e.variant == variant && e.smem == smem) {
         return e.ctas;
       }
     }
   }
-  const int n = query_resident_ctas(cols_per_lane, wide, smem);
+  const int n = query_resident_ctas(cols_per_lane, variant, smem);
   if (n > 0) {
     std::lock_guard<std::mutex> lock(g_occupancy_mutex);
-    g_occupancy.push_back({dev, cols_per_lane, wide, smem, n});
+    g_occupancy.push_back({dev, cols_per_lane, variant, smem, n});
   }
   return n;
 }
 
-template <bool kDense, bool kWide>
+template <bool kDense, int kVariant>
 int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta, int64_t smem,
            void* stream) {
   if (smem > kSmemPerBlockMax) return RFM_ERR_UNSUPPORTED;
   const void* fn = nullptr;
   switch (cols_per_lane) {
-    case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense, kWide>); break;
-    case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, kDense, kWide>); break;
+    case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense, kVariant>); break;
+    case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, kDense, kVariant>); break;
     case 32:
-      if (kWide) return RFM_ERR_INVALID_ARGUMENT;
-      fn = reinterpret_cast<const void*>(&lsap_kernel<32, kDense, false>);
+      if (kVariant == kVarWide) return RFM_ERR_INVALID_ARGUMENT;
+      fn = reinterpret_cast<const void*>(&lsap_kernel<32, kDense, kVariant == kVarWide ? kVarRegs : kVariant>);
       break;
     default: return RFM_ERR_INVALID_ARGUMENT;
   }
@@ -789,9 +815,11 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
   const dim3 grid(static_cast<unsigned>(num_ctas));
   const dim3 block(32 * warps_per_cta);
   switch (cols_per_lane) {
-    case 4: lsap_kernel<4, kDense, kWide><<<grid, block, smem, as_stream(stream)>>>(a); break;
-    case 10: lsap_kernel<10, kDense, kWide><<<grid, block, smem, as_stream(stream)>>>(a); break;
-    default: lsap_kernel<32, kDense, false><<<grid, block, smem, as_stream(stream)>>>(a); break;
+    case 4: lsap_kernel<4, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
+    case 10: lsap_kernel<10, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
+    default:
+      lsap_kernel<32, kDense, kVariant == kVarWide ? kVarRegs : kVariant><<<grid, block, smem, as_stream(stream)>>>(a);
+      break;
   }
   return launch_status();
 }
@@ -950,28 +978,36 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   a.q_out = query_out;
   a.t_out = target_out;
   a.status = status;
+  const bool early = plan->max_rows >= kEarlyMinRows;
   if (!persistent) {
-    return launch<false, false>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta,
-                                plan->cta_smem_bytes, stream);
+    if (early) {
+      return launch<false, kVarEarly>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta,
+                                      plan->cta_smem_bytes, stream);
+    }
+    return launch<false, kVarRegs>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta,
+                                   plan->cta_smem_bytes, stream);
   }
   // Persistent warps stage nothing, so each warp's slot is just its fixed arrays;
-  // large batches (more problems than 64 per SM) take the wide layout.
+  // large batches (more problems than 64 per SM) take the wide layout, batches of
+  // long problems the early-load variant.
   const int sms = sm_count();
   const bool wide = plan->cols_per_lane <= 10 &&
                     static_cast<int64_t>(plan->num_problems) > static_cast<int64_t>(kWideProblemsPerSm) * sms;
+  const int variant = wide ? kVarWide : (early ? kVarEarly : kVarRegs);
   const int64_t smem = wide ? kMaxWarpsPerCta * fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows, true)
                             : plan->cta_smem_bytes;
   a.queue = static_cast<int*>(workspace);
   a.workspace = reinterpret_cast<float*>(static_cast<char*>(workspace) + kQueueBytes);
   a.slot = static_cast<int>(smem / kMaxWarpsPerCta);
   if (cudaMemsetAsync(a.queue, 0, sizeof(int), as_stream(stream)) != cudaSuccess) return launch_status();
-  const int ctas_per_sm = resident_ctas(plan->cols_per_lane, wide, smem);
+  const int ctas_per_sm = resident_ctas(plan->cols_per_lane, variant, smem);
   if (ctas_per_sm < 1) return launch_status() != RFM_OK ? RFM_ERR_LAUNCH : RFM_ERR_UNSUPPORTED;
   const int grid = ctas_per_sm * sms;
   const int needed = (plan->num_problems + kMaxWarpsPerCta - 1) / kMaxWarpsPerCta;
   const int num_ctas = grid < needed ? grid : needed;
-  if (wide) return launch<false, true>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
-  return launch<false, false>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
+  if (variant == kVarWide) return launch<false, kVarWide>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
+  if (variant == kVarEarly) return launch<false, kVarEarly>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
+  return launch<false, kVarRegs>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
 }
 
 namespace {
@@ -1040,7 +1076,8 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.t_out = nullptr;
   a.status = status;
   const int ctas = (num_problems + dp.warps - 1) / dp.warps;
-  return launch<true, false>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);
+  if (dp.max_rows >= kEarlyMinRows) return launch<true, kVarEarly>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);
+  return launch<true, kVarRegs>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -11,7 +11,7 @@
  *              (patches.py:123-149).
  *
  *   rfm_lsap   solves a batch of rectangular linear assignment problems read
- *              in place from that matrix, one CTA per problem, with the exact
+ *              in place from that matrix, one warp per problem, with the exact
  *              arithmetic and tie-breaking of SciPy's rectangular_lsap, and
  *              writes the (query, target) index pairs straight into their
  *              final packed position. Replaces batch_lap / lsap_kernel

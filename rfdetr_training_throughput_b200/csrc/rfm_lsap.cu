@@ -22,25 +22,35 @@
 //     removal.
 //
 // Layout.  Lane l owns solver columns l, l+32, ..., l+32(K-1).  Its columns'
-// duals v, path costs, tie keys, "still remaining" and "free" bits live in
-// registers, so the scan is register work plus one cost load per column; the
-// warp argmin is three redux.sync minimum steps over an order-preserving
-// integer image of the float64 cost and the key.  Row duals (float64), the
-// matching, the path and `remaining` (position -> column) live in shared
-// memory as int16.  The dual update needs no cross-lane traffic: every visited
-// non-sink column j owns exactly one tree row, row4col[j], so its lane applies
-// u[row4col[j]] += minv - spc[j] and v[j] -= minv - spc[j] itself.
+// path costs and "still remaining" and "free" bits live in registers; their
+// duals v and tie keys too (REGS and EARLY variants) or in shared memory (WIDE,
+// for batches of more than 64 problems per SM: fewer registers, more resident
+// warps).  The warp argmin is three redux.sync minimum steps over an
+// order-preserving integer image of the float64 cost and the key.  Row duals
+// (float64), the matching, the path and `remaining` (position -> column) live
+// in shared memory as int16.  The dual update needs no cross-lane traffic:
+// every visited non-sink column j owns exactly one tree row, row4col[j], so its
+// lane applies u[row4col[j]] += minv - spc[j] and v[j] -= minv - spc[j] itself.
+//
+// One pass over the tile validates it and computes every row's first pick (the
+// argmin of its first scan with u = v = 0 and all columns free); a row whose
+// pick is still valid at its turn commits it in O(1), which is exact (see the
+// comment at the shortcut).  A scan issues all of a lane's loads before the
+// first compare; the EARLY variant (problems with 64 or more rows: long
+// searches) issues the next scan's row as soon as the argmin names it, before
+// the current step's bookkeeping.
 //
 // Cost source.  Element (q, t) of a problem is read at
 // cost[cost_offset + q * stride_q + t * stride_t], so the solver reads either
 // the query-major compact matrix or its target-major transpose in place.  The
 // problem is used in the solver's orientation (rows = targets when
-// transposed): staged into shared memory with cp.async when the tile is
-// within the cap (SHARED); otherwise read straight from L2/HBM when solver
-// rows are contiguous in the source (DIRECT), or first transposed into the
-// caller's workspace (SCRATCH).  The host packs problems, sorted by tile
-// size, into CTAs of up to four warps under a shared-memory budget, so small
-// problems share a CTA and the SM holds as many warps as registers allow.
+// transposed).  When every problem's solver rows are contiguous in the source,
+// persistent warps pull problems (largest first) from a counter in the
+// workspace and read rows straight from L2/HBM (DIRECT).  Otherwise the host
+// packs problems, sorted by tile size, into CTAs of up to four warps under a
+// shared-memory budget; a tile within the cap is staged into shared memory
+// with cp.async (SHARED), a larger one read in place (DIRECT) or first
+// transposed into the caller's workspace (SCRATCH).
 //
 // Termination: every inner step removes one column from `remaining`, so each
 // augmentation is bounded by num_cols steps (kernels_lap.py:78-84,147-148);

@@ -128,3 +128,32 @@ def test_image_lookup_across_many_empty_images():
                 "pred_boxes": torch.as_tensor(boxes[0], device=dev)}]
     _, tmajor = matcher.match_layers(outputs, to_targets(labels, tboxes, dev), 1, weights=w, return_cost=True)
     assert torch.equal(tmajor.cpu(), torch.as_tensor(gpu).reshape(tmajor.shape))
+
+
+@pytest.mark.parametrize("queries", [5, 7, 9])
+def test_odd_query_counts_both_layouts_and_zero_padding(queries):
+    """Q not a multiple of the per-thread query pair: the last pair is half padding (q >= Q) or
+    all padding (ld - Q >= 2); pads are written as 0 and the real columns match the query-major
+    matrix bit for bit."""
+    rng = np.random.default_rng(queries)
+    sizes = [3, 1, 4]
+    logits = torch.as_tensor(rng.normal(0, 1.5, (1, 3, queries, 2)).astype(np.float32), device="cuda")
+    boxes = torch.as_tensor((1 / (1 + np.exp(-rng.normal(0, 1, (1, 3, queries, 4))))).astype(np.float32),
+                            device="cuda")
+    labels = torch.as_tensor(rng.integers(0, 2, sum(sizes)), device="cuda")
+    tboxes = torch.as_tensor(np.concatenate([rng.uniform(0.1, 0.9, (sum(sizes), 2)),
+                                             rng.uniform(0.02, 0.5, (sum(sizes), 2))], 1).astype(np.float32),
+                             device="cuda")
+    packed = matcher.PackedTargets(labels, tboxes, tuple(sizes))
+    w = dict(cost_class=2.0, cost_bbox=5.0, cost_giou=2.0, focal_alpha=0.25)
+    ex = {}
+    matcher.match_packed(logits, boxes, packed, 1, weights=w, extras=ex)
+    offs = np.concatenate([[0], np.cumsum(sizes)])
+    targets = [{"labels": labels[offs[b]:offs[b + 1]], "boxes": tboxes[offs[b]:offs[b + 1]]} for b in range(3)]
+    qmajor = matcher.compute_compact_detection_cost_matrix({"pred_logits": logits, "pred_boxes": boxes}, targets,
+                                                           weights=w)
+    torch.cuda.synchronize()
+    tm = ex["cost"]
+    assert tm.shape[-1] == (queries + 3) // 4 * 4
+    assert bool((tm[..., queries:] == 0).all())
+    assert torch.equal(tm[..., :queries].transpose(1, 2), qmajor)

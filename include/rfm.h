@@ -100,8 +100,9 @@ typedef struct rfm_lsap_plan {
   int64_t workspace_bytes;  /* device scratch rfm_lsap needs for this batch */
 } rfm_lsap_plan;
 
-/* rfm_lsap_plan.flags: the batch runs on persistent warps that pull problems
- * in order from a counter kept at the start of the workspace. */
+/* rfm_lsap_plan.flags: the batch runs on persistent warps; warp w starts on
+ * problem w, and the warps pull the rest in order from a counter kept at the
+ * start of the workspace. */
 #define RFM_PLAN_PERSISTENT 1
 
 /* Layouts rfm_cost can write. */

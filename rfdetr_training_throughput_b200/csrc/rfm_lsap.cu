@@ -45,8 +45,9 @@
 // the query-major compact matrix or its target-major transpose in place.  The
 // problem is used in the solver's orientation (rows = targets when
 // transposed).  When every problem's solver rows are contiguous in the source,
-// persistent warps pull problems (largest first) from a counter in the
-// workspace and read rows straight from L2/HBM (DIRECT).  Otherwise the host
+// persistent warps (warp w starts on problem w) pull further problems
+// (largest first) from a counter in the workspace, claiming the next one before
+// the current one's epilogue, and read rows straight from L2/HBM (DIRECT).  Otherwise the host
 // packs problems, sorted by tile size, into CTAs of up to four warps under a
 // shared-memory budget; a tile within the cap is staged into shared memory
 // with cp.async (SHARED), a larger one read in place (DIRECT) or first
@@ -109,6 +110,8 @@ struct LsapArgs {
   int dense_warps;
   int slot;              // dense and persistent modes: uniform shared-memory slot per warp
   int* queue;            // persistent mode: next-problem counter (zeroed before the launch)
+  int claim_base;        // persistent mode: warps launched; warp w starts on problem w and
+                         // claim c of the counter names problem claim_base + c
   int tile_cap;
   int max_rows;
   float* workspace;
@@ -302,10 +305,17 @@ __device__ __forceinline__ void record_first_pick(const float (&x)[K], int lane,
   }
 }
 
+// Persistent launches: lane 0 claims the warp's next problem.  It is called
+// before a problem's epilogue, so the atomic's round trip overlaps the stores.
+__device__ __forceinline__ int claim_next(const LsapArgs& a, int lane) {
+  return (a.queue != nullptr && lane == 0) ? atomicAdd(a.queue, 1) + a.claim_base : 0;
+}
+
 // Solves problem p with the warp's shared-memory slot at `base` (`slot` bytes).
+// Returns, in lane 0, the next problem a persistent warp claimed.
 template <int K, bool kDense, int kVariant>
-__device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned char* base, int slot,
-                                              int lane) {
+__device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned char* base, int slot,
+                                             int lane) {
   constexpr int kCols = 32 * K;
   constexpr bool kWide = kVariant == kVarWide;
   constexpr bool kEarly = kVariant == kVarEarly;
@@ -334,11 +344,12 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
   int64_t* t_out = kDense ? nullptr : a.t_out + out_off;
 
   if (nr == 0) {
+    const int next = claim_next(a, lane);
     if (kDense) {
       for (int w = lane; w < nq; w += 32) q_out[w] = -1;
     }
     if (a.status != nullptr && lane == 0) a.status[p] = RFM_STATUS_OK;
-    return;
+    return next;
   }
 
   double* u_s = reinterpret_cast<double*>(base);
@@ -391,30 +402,39 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
   // tile leaves it below -inf's successor (or NaN), which SciPy rejects
   float chk = CUDART_INF_F;
   if (s.cs == 1) {
-    // solver rows are contiguous in the source: one coalesced pass over them
-    for (int i = 0; i < nr; i += 2) {
-      const bool two = i + 1 < nr;
-      float x0[K], x1[K];
+    // solver rows are contiguous in the source: one coalesced pass over them,
+    // kLoadRows rows per round trip (as many as the variant's register budget
+    // holds without spilling: every row's loads are in flight together)
+    constexpr int kLoadRows = (kWide || K > 10) ? 2 : (kEarly ? 4 : 6);
+    for (int i = 0; i < nr; i += kLoadRows) {
+      float x[kLoadRows][K];
 #pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const int j = lane + 32 * k;
-        x0[k] = j < nc ? __ldg(src + i * s.rs + j) : CUDART_INF_F;
-        x1[k] = (j < nc && two) ? __ldg(src + (i + 1) * s.rs + j) : CUDART_INF_F;
-      }
-#pragma unroll
-      for (int k = 0; k < K; ++k) chk = min_nan(chk, min_nan(x0[k], x1[k]));
-      if (mode == kModeShared) {
+      for (int r = 0; r < kLoadRows; ++r) {
 #pragma unroll
         for (int k = 0; k < K; ++k) {
           const int j = lane + 32 * k;
-          if (j < nc) {
-            tile[i * nc + j] = x0[k];
-            if (two) tile[(i + 1) * nc + j] = x1[k];
+          x[r][k] = (j < nc && i + r < nr) ? __ldg(src + (i + r) * s.rs + j) : CUDART_INF_F;
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kLoadRows; ++r) {
+#pragma unroll
+        for (int k = 0; k < K; ++k) chk = min_nan(chk, x[r][k]);
+      }
+      if (mode == kModeShared) {
+#pragma unroll
+        for (int r = 0; r < kLoadRows; ++r) {
+#pragma unroll
+          for (int k = 0; k < K; ++k) {
+            const int j = lane + 32 * k;
+            if (j < nc && i + r < nr) tile[(i + r) * nc + j] = x[r][k];
           }
         }
       }
-      record_first_pick<K>(x0, lane, nc, i, pick_m_s, pick_w_s);
-      if (two) record_first_pick<K>(x1, lane, nc, i + 1, pick_m_s, pick_w_s);
+#pragma unroll
+      for (int r = 0; r < kLoadRows; ++r) {
+        if (i + r < nr) record_first_pick<K>(x[r], lane, nc, i + r, pick_m_s, pick_w_s);
+      }
     }
     if (mode == kModeShared) {
       rows = tile;
@@ -610,6 +630,7 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
   }
 
   // ---- epilogue: write the result in SciPy's order -------------------------
+  const int next = claim_next(a, lane);
   if (kDense) {
     // matching[w] = task of worker w, -1 if none (kernels_lap.py:336-341)
     if (code != RFM_STATUS_OK) {
@@ -647,6 +668,7 @@ __device__ __forceinline__ void solve_problem(const LsapArgs& a, int p, unsigned
     }
   }
   if (a.status != nullptr && lane == 0) a.status[p] = code;
+  return next;
 }
 
 template <int K, bool kDense, int kVariant>
@@ -660,14 +682,13 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVari
       solve_problem<K, kDense, kVariant>(a, p, smem_raw + static_cast<int64_t>(warp) * a.slot, a.slot, lane);
     }
   } else if (a.queue != nullptr) {
-    // persistent warps: pull problems (sorted largest first) until none is left
+    // persistent warps: warp w starts on problem w, then pulls problems (sorted
+    // largest first) from the counter until none is left
     unsigned char* base = smem_raw + static_cast<int64_t>(warp) * a.slot;
-    for (;;) {
-      int p = 0;
-      if (lane == 0) p = atomicAdd(a.queue, 1);
-      p = __shfl_sync(kFullMask, p, 0);
-      if (p >= a.num_problems) break;
-      solve_problem<K, kDense, kVariant>(a, p, base, a.slot, lane);
+    int p = blockIdx.x * kMaxWarpsPerCta + warp;
+    while (p < a.num_problems) {
+      const int next = solve_problem<K, kDense, kVariant>(a, p, base, a.slot, lane);
+      p = __shfl_sync(kFullMask, next, 0);
       __syncwarp();
     }
   } else {
@@ -982,6 +1003,7 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   a.dense_warps = 0;
   a.slot = 0;
   a.queue = nullptr;
+  a.claim_base = 0;
   a.tile_cap = plan->tile_cap_floats;
   a.max_rows = plan->max_rows;
   a.workspace = static_cast<float*>(workspace);
@@ -1015,6 +1037,7 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   const int grid = ctas_per_sm * sms;
   const int needed = (plan->num_problems + kMaxWarpsPerCta - 1) / kMaxWarpsPerCta;
   const int num_ctas = grid < needed ? grid : needed;
+  a.claim_base = num_ctas * kMaxWarpsPerCta;
   if (variant == kVarWide) return launch<false, kVarWide>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
   if (variant == kVarEarly) return launch<false, kVarEarly>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
   return launch<false, kVarRegs>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
@@ -1079,6 +1102,7 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.dense_warps = dp.warps;
   a.slot = static_cast<int>(dp.slot);
   a.queue = nullptr;
+  a.claim_base = 0;
   a.tile_cap = static_cast<int>(dp.tile_cap);
   a.max_rows = dp.max_rows;
   a.workspace = static_cast<float*>(workspace);

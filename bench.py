@@ -187,6 +187,27 @@ def traffic_per_launch() -> float | None:
 # --------------------------------------------------------------------------- CPU path
 
 
+def gpu_local_cpus(device: torch.device) -> set[int] | None:
+    """The host CPUs NVML names as nearest the GPU (its NUMA node), within this process's
+    allowed set, or None when NVML cannot tell.  Only read: nothing about the GPU is changed."""
+    try:
+        import pynvml
+
+        props = torch.cuda.get_device_properties(device)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = pynvml.nvmlDeviceGetCpuAffinity(handle, ((os.cpu_count() or 1) + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * w + b for w, word in enumerate(words) for b in range(64) if (int(word) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:  # no NVML, no such call, or a foreign bus id format: leave the process as it is
+        return None
+
+
 def cpu_path_rate(wl, images: int, budget_s: float, threads: int, min_reps: int = 1) -> dict:
     """problems/s of the reference CPU path on the first ``images`` images, repeated for ~budget_s."""
     from oracle.cpu_path import CpuMatcher
@@ -323,6 +344,12 @@ def run_rfm(args) -> None:
     # ---- end to end: pinned host inputs -> device -> match -> packed pairs back to host
     e2e = None
     if not args.no_e2e:
+        # pinned buffers on the GPU's own NUMA node (the thread that pins them runs on that node's
+        # CPUs), so the uploads do not cross the inter-socket link; the affinity is restored after
+        saved_cpus = os.sched_getaffinity(0)
+        local_cpus = gpu_local_cpus(device)
+        if local_cpus:
+            os.sched_setaffinity(0, local_cpus)
         h_logits = wl.pred_logits.pin_memory()
         h_boxes = wl.pred_boxes.pin_memory()
         h_labels = torch.cat([t["labels"] for t in wl.targets]).pin_memory()
@@ -364,10 +391,13 @@ def run_rfm(args) -> None:
         e2e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
         if world > 1:
             torch.distributed.all_reduce(e2e_t, op=torch.distributed.ReduceOp.MAX)
+        os.sched_setaffinity(0, saved_cpus)
         e2e = {"value": world * problems * args.steps / (float(e2e_t.item()) / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": float(e2e_t.item()) / args.steps,
-               "path": "PrefetchingMatcher: pinned H2D of step k+1 on a copy stream overlapping match + D2H of step k"}
+               "path": "PrefetchingMatcher: pinned H2D of step k+1 on a copy stream overlapping match + D2H of step k",
+               "host_buffers": (f"pinned by a thread on the {len(local_cpus)} GPU-local CPUs NVML reports"
+                                if local_cpus else "pinned without NUMA placement (NVML gave no CPU set)")}
 
     # ---- production step (5 layers x 8 images x 13 groups, 520 problems): eager calls vs the CUDA graph
     production = None

@@ -281,17 +281,25 @@ __device__ __forceinline__ float min_nan(float x, float y) {
   return r;
 }
 
-// First pick of one row when every column is free and v = 0: the smallest
-// cost, ties to the smallest column; lane 0 records it (column -1 when the
-// row's minimum is +inf, which leaves the row to the full search).  Entries
-// past the row end hold +inf.  A row holding NaN is flagged by the caller's
-// check and never solved, so whatever it records here is unused.
+// NaN-propagating minimum of the lane's entries of one row.
 template <int K>
-__device__ __forceinline__ void record_first_pick(const float (&x)[K], int lane, int nc, int row,
-                                                  double* pick_m_s, int16_t* pick_w_s) {
+__device__ __forceinline__ float lane_min(const float (&x)[K]) {
   float m = x[0];
 #pragma unroll
-  for (int k = 1; k < K; ++k) m = fminf(m, x[k]);
+  for (int k = 1; k < K; ++k) m = min_nan(m, x[k]);
+  return m;
+}
+
+// First pick of one row when every column is free and v = 0: the smallest
+// cost, ties to the smallest column; lane 0 records it (column -1 when the
+// row's minimum is +inf, which leaves the row to the full search).  m is
+// lane_min(x); entries past the row end hold +inf.  A row holding NaN has
+// m = NaN, is flagged by the caller's check (which takes the same m) and is
+// never solved, so whatever it records here is unused; without NaN, m is the
+// plain minimum.
+template <int K>
+__device__ __forceinline__ void record_first_pick(const float (&x)[K], float m, int lane, int nc, int row,
+                                                  double* pick_m_s, int16_t* pick_w_s) {
   unsigned bj = 0xffffu;
 #pragma unroll
   for (int k = K - 1; k >= 0; --k) bj = x[k] == m ? static_cast<unsigned>(lane + 32 * k) : bj;
@@ -416,10 +424,11 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
           x[r][k] = (j < nc && i + r < nr) ? __ldg(src + (i + r) * s.rs + j) : CUDART_INF_F;
         }
       }
+      float m[kLoadRows];
 #pragma unroll
       for (int r = 0; r < kLoadRows; ++r) {
-#pragma unroll
-        for (int k = 0; k < K; ++k) chk = min_nan(chk, x[r][k]);
+        m[r] = lane_min<K>(x[r]);
+        chk = min_nan(chk, m[r]);
       }
       if (mode == kModeShared) {
 #pragma unroll
@@ -433,7 +442,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
       }
 #pragma unroll
       for (int r = 0; r < kLoadRows; ++r) {
-        if (i + r < nr) record_first_pick<K>(x[r], lane, nc, i + r, pick_m_s, pick_w_s);
+        if (i + r < nr) record_first_pick<K>(x[r], m[r], lane, nc, i + r, pick_m_s, pick_w_s);
       }
     }
     if (mode == kModeShared) {
@@ -469,9 +478,10 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
       for (int k = 0; k < K; ++k) {
         const int j = lane + 32 * k;
         x[k] = j >= nc ? CUDART_INF_F : (mode == kModeShared ? rows[i * nc + j] : __ldcg(rows + i * nc + j));
-        chk = min_nan(chk, x[k]);
       }
-      record_first_pick<K>(x, lane, nc, i, pick_m_s, pick_w_s);
+      const float m = lane_min<K>(x);
+      chk = min_nan(chk, m);
+      record_first_pick<K>(x, m, lane, nc, i, pick_m_s, pick_w_s);
     }
   }
   bad = !(chk > -CUDART_INF_F);

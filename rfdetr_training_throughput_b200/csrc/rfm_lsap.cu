@@ -228,8 +228,8 @@ __device__ __forceinline__ void load_row(const float* row, int lane, unsigned ma
 // row whose costs load_row() requested into cf (all of a lane's loads are in
 // flight before the first is used: a row read from memory costs one round
 // trip, not one per column).  Column duals and tie keys come from registers,
-// or in the wide layout from shared memory (a key only when its column ties or
-// beats the lane's best so far).
+// or in the wide layout from shared memory (every remaining column's key is
+// read, so the (cost, key) comparison compiles to selects, not branches).
 template <int K, bool kWide>
 __device__ __forceinline__ void scan_row(const float (&cf)[K], int lane, int i, double minv, double ui,
                                          const double (&v)[K], const double* v_s, double (&spc)[K],
@@ -244,17 +244,10 @@ __device__ __forceinline__ void scan_row(const float (&cf)[K], int lane, int i, 
         spc[k] = r;
         path_s[j] = static_cast<int16_t>(i);
       }
-      if (kWide) {
-        if (spc[k] < bv) {
-          bv = spc[k];
-          bk = key_s[j];
-        } else if (spc[k] == bv) {
-          const unsigned kj = key_s[j];
-          if (kj < bk) bk = kj;
-        }
-      } else if (spc[k] < bv || (spc[k] == bv && key[k] < bk)) {
+      const unsigned kj = kWide ? static_cast<unsigned>(key_s[j]) : key[k];
+      if (spc[k] < bv || (spc[k] == bv && kj < bk)) {
         bv = spc[k];
-        bk = key[k];
+        bk = kj;
       }
     }
   }

@@ -76,8 +76,12 @@ constexpr int kMaxWarpsPerCta = 4;
 // them in shared memory (large batches); EARLY is REGS with each scan's row
 // requested as soon as the row is known, before the previous step's
 // bookkeeping, which pays off when searches run long (batches whose problems
-// have at least kEarlyMinRows rows).
-enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2 };
+// have at least kEarlyMinRows rows).  COOP is REGS with one problem per CTA
+// whose four warps share the load pass (a quarter of the rows each, so a
+// problem's rows cost a quarter of the round trips) before warp 0 solves it
+// alone: small batches, where every problem is resident at once and the
+// step's time is the slowest problem's latency.
+enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2, kVarCoop = 3 };
 constexpr int kEarlyMinRows = 64;
 // Batches with more than this many problems per SM use the wide layout.
 constexpr int kWideProblemsPerSm = 64;
@@ -320,6 +324,9 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   constexpr int kCols = 32 * K;
   constexpr bool kWide = kVariant == kVarWide;
   constexpr bool kEarly = kVariant == kVarEarly;
+  constexpr bool kCoop = kVariant == kVarCoop;
+  constexpr int kLoadWarps = kCoop ? kMaxWarpsPerCta : 1;
+  const int warp = kCoop ? static_cast<int>(threadIdx.x >> 5) : 0;
   int64_t cost_off, out_off, scratch_off;
   int nq, nt, qbase;
   if (kDense) {
@@ -349,7 +356,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
     if (kDense) {
       for (int w = lane; w < nq; w += 32) q_out[w] = -1;
     }
-    if (a.status != nullptr && lane == 0) a.status[p] = RFM_STATUS_OK;
+    if (a.status != nullptr && lane == 0 && warp == 0) a.status[p] = RFM_STATUS_OK;
     return next;
   }
 
@@ -368,13 +375,15 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   for (int k = 0; k < K; ++k) {
     if (lane + 32 * k < nc) valid |= 1u << k;
   }
-  for (int i = lane; i < nr; i += 32) {
-    u_s[i] = 0.0;
-    col4row_s[i] = -1;
-  }
-  for (int j = lane; j < nc; j += 32) {
-    row4col_s[j] = -1;
-    if (kWide) v_s[j] = 0.0;
+  if (warp == 0) {
+    for (int i = lane; i < nr; i += 32) {
+      u_s[i] = 0.0;
+      col4row_s[i] = -1;
+    }
+    for (int j = lane; j < nc; j += 32) {
+      row4col_s[j] = -1;
+      if (kWide) v_s[j] = 0.0;
+    }
   }
 
   // ---- load the cost once: validate it (SciPy rejects NaN and -inf), keep
@@ -407,7 +416,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
     // kLoadRows rows per round trip (as many as the variant's register budget
     // holds without spilling: every row's loads are in flight together)
     constexpr int kLoadRows = (kWide || K > 10) ? 2 : (kEarly ? 4 : 6);
-    for (int i = 0; i < nr; i += kLoadRows) {
+    for (int i = warp * kLoadRows; i < nr; i += kLoadWarps * kLoadRows) {
       float x[kLoadRows][K];
 #pragma unroll
       for (int r = 0; r < kLoadRows; ++r) {
@@ -442,7 +451,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
       rows = tile;
       row_pitch = nc;
     }
-  } else {
+  } else if (warp == 0) {
     // the source runs along solver rows: stage a transposed copy first
     const int total = nr * nc;
     if (mode == kModeShared) {
@@ -479,6 +488,11 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   }
   bad = !(chk > -CUDART_INF_F);
   bad = __any_sync(kFullMask, bad);
+  if (kCoop) {
+    // every warp's first picks and checks are in; warp 0 solves the problem alone
+    bad = __syncthreads_or(bad) != 0;
+    if (warp != 0) return 0;
+  }
 
   unsigned freem = valid;
   double v[K];
@@ -679,6 +693,11 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVari
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  if (kVariant == kVarCoop) {
+    // one problem per CTA, all four warps in its load pass
+    solve_problem<K, kDense, kVariant>(a, blockIdx.x, smem_raw, a.slot, lane);
+    return;
+  }
   if (kDense) {
     const int p = blockIdx.x * a.dense_warps + warp;
     if (p < a.num_problems) {
@@ -726,20 +745,22 @@ int sm_count() {
   return n;
 }
 
-// The pair-mode kernel for a column count and variant (the wide layout exists
-// for up to 320 columns).
+// The pair-mode kernel for a column count and variant (the wide and
+// cooperative layouts exist for up to 320 columns).
 const void* pair_kernel(int cols_per_lane, int variant) {
   switch (cols_per_lane) {
     case 4:
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarWide>);
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarEarly>);
+      if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarCoop>);
       return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarRegs>);
     case 10:
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarWide>);
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarEarly>);
+      if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarCoop>);
       return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarRegs>);
     case 32:
-      if (variant == kVarWide) return nullptr;
+      if (variant == kVarWide || variant == kVarCoop) return nullptr;
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarEarly>);
       return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarRegs>);
     default: return nullptr;
@@ -840,8 +861,9 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense, kVariant>); break;
     case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, kDense, kVariant>); break;
     case 32:
-      if (kVariant == kVarWide) return RFM_ERR_INVALID_ARGUMENT;
-      fn = reinterpret_cast<const void*>(&lsap_kernel<32, kDense, kVariant == kVarWide ? kVarRegs : kVariant>);
+      if (kVariant == kVarWide || kVariant == kVarCoop) return RFM_ERR_INVALID_ARGUMENT;
+      fn = reinterpret_cast<const void*>(
+          &lsap_kernel<32, kDense, (kVariant == kVarWide || kVariant == kVarCoop) ? kVarRegs : kVariant>);
       break;
     default: return RFM_ERR_INVALID_ARGUMENT;
   }
@@ -852,7 +874,8 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     case 4: lsap_kernel<4, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
     case 10: lsap_kernel<10, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
     default:
-      lsap_kernel<32, kDense, kVariant == kVarWide ? kVarRegs : kVariant><<<grid, block, smem, as_stream(stream)>>>(a);
+      lsap_kernel<32, kDense, (kVariant == kVarWide || kVariant == kVarCoop) ? kVarRegs : kVariant>
+          <<<grid, block, smem, as_stream(stream)>>>(a);
       break;
   }
   return launch_status();
@@ -1029,6 +1052,17 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   const bool wide = plan->cols_per_lane <= 10 &&
                     static_cast<int64_t>(plan->num_problems) > static_cast<int64_t>(kWideProblemsPerSm) * sms;
   const int variant = wide ? kVarWide : (early ? kVarEarly : kVarRegs);
+  if (!wide && !early && plan->cols_per_lane <= 10) {
+    // a small batch whose problems are all resident at once: one problem per
+    // CTA, the CTA's four warps sharing its load pass (no counter, no memset)
+    const int64_t coop_smem = fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows);
+    const int coop_ctas = resident_ctas(plan->cols_per_lane, kVarCoop, coop_smem);
+    if (coop_ctas > 0 && static_cast<int64_t>(plan->num_problems) <= static_cast<int64_t>(coop_ctas) * sms) {
+      a.slot = static_cast<int>(coop_smem);
+      return launch<false, kVarCoop>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, coop_smem,
+                                     stream);
+    }
+  }
   const int64_t smem = wide ? kMaxWarpsPerCta * fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows, true)
                             : plan->cta_smem_bytes;
   a.queue = static_cast<int*>(workspace);

@@ -6,7 +6,8 @@
 // written directly, so there is no padded intermediate and no copy.
 //
 // Two output layouts.  TARGET-MAJOR (the transpose, out[l][col][q]) is the one
-// the fused matcher step uses: one CTA covers 32 consecutive target rows (runs
+// the fused matcher step uses: one CTA covers 32 consecutive target rows (8 when
+// 32-row CTAs would not fill the GPU twice, as in the production step; runs
 // of one image each) and a 256-query tile; each thread owns two consecutive
 // queries (one 8-byte vector of every output row), loads their boxes and logits
 // once per image run (the next run's while computing the current one),
@@ -265,6 +266,7 @@ __global__ void __launch_bounds__(kThreads) cost_qmajor_kernel(const CostArgs a)
 constexpr int kTmThreads = 128;  // 2 queries each: 256 queries per CTA
 constexpr int kQpt = 2;          // queries per thread (one f32x2 pair)
 constexpr int kTmCols = 32;      // target rows per CTA (may span several images)
+constexpr int kTmColsSmall = 8;  // ... for batches too small to fill the GPU twice with 32-row CTAs
 constexpr int kSmallClasses = 4;
 
 // Packed float32 pairs: two queries per instruction (sm_100 f32x2 pipe), each
@@ -447,18 +449,18 @@ __device__ __forceinline__ void cost_targets(const TargetRow* s_t, int c_begin, 
   }
 }
 
-template <int NCLS>
+template <int NCLS, int kCols>
 __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs a) {
-  __shared__ TargetRow s_t[kTmCols];
-  __shared__ int s_seg[kTmCols + 1];
+  __shared__ TargetRow s_t[kCols];
+  __shared__ int s_seg[kCols + 1];
   __shared__ int s_nseg;
   __shared__ int s_all_plain;
   __shared__ int s_off[kImageWindow + 1];
   const int layer = blockIdx.z;
-  const int c_begin = blockIdx.x * kTmCols;
-  const int n = min(kTmCols, a.S - c_begin);
+  const int c_begin = blockIdx.x * kCols;
+  const int n = min(kCols, a.S - c_begin);
   const int tid = threadIdx.x;
-  static_assert(kTmCols <= kTmThreads, "one staged target per thread");
+  static_assert(kCols <= kTmThreads, "one staged target per thread");
   // this thread's target is requested first; its latency overlaps the image search
   const bool has_target = tid < n;
   float4 tbox = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -543,6 +545,17 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
   }
 }
 
+template <int kCols>
+void launch_tmajor(const CostArgs& a, dim3 grid, int num_classes, cudaStream_t stream) {
+  switch (num_classes) {
+    case 1: cost_tmajor_kernel<1, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
+    case 2: cost_tmajor_kernel<2, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
+    case 3: cost_tmajor_kernel<3, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
+    case 4: cost_tmajor_kernel<4, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
+    default: cost_tmajor_kernel<0, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
+  }
+}
+
 }  // namespace
 }  // namespace rfm
 
@@ -599,16 +612,19 @@ extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
 
   if (layout == RFM_LAYOUT_TARGET_MAJOR) {
     const int64_t gy = (ld / kQpt + kTmThreads - 1) / kTmThreads;
-    const int64_t gx = (static_cast<int64_t>(sum_targets) + kTmCols - 1) / kTmCols;
+    // 32 target rows per CTA, or 8 when that leaves fewer than two CTAs per SM
+    // (the production step: a few hundred CTAs, each then a quarter as long)
+    const int64_t gx32 = (static_cast<int64_t>(sum_targets) + kTmCols - 1) / kTmCols;
+    const bool small = gx32 * gy * num_layers < 2 * static_cast<int64_t>(device_sm_count());
+    const int cols = small ? kTmColsSmall : kTmCols;
+    const int64_t gx = (static_cast<int64_t>(sum_targets) + cols - 1) / cols;
     if (gy > 65535 || gx > 0x7fffffff) return RFM_ERR_UNSUPPORTED;
     const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy),
                     static_cast<unsigned>(num_layers));
-    switch (num_classes) {
-      case 1: cost_tmajor_kernel<1><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
-      case 2: cost_tmajor_kernel<2><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
-      case 3: cost_tmajor_kernel<3><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
-      case 4: cost_tmajor_kernel<4><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
-      default: cost_tmajor_kernel<0><<<grid, kTmThreads, 0, as_stream(stream)>>>(a); break;
+    if (small) {
+      launch_tmajor<kTmColsSmall>(a, grid, num_classes, as_stream(stream));
+    } else {
+      launch_tmajor<kTmCols>(a, grid, num_classes, as_stream(stream));
     }
     return launch_status();
   }

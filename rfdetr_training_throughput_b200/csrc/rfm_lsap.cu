@@ -735,16 +735,6 @@ int64_t slot_bytes(const Shape& s, int cols_cap, int max_rows, int64_t tile_cap)
   return warp_bytes_for(cols_cap, max_rows, (s.nr > 0 && t <= tile_cap) ? t : 0);
 }
 
-int sm_count() {
-  int dev = 0, n = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1) {
-    cudaGetLastError();
-    return 1;
-  }
-  return n;
-}
-
 // The pair-mode kernel for a column count and variant (the wide and
 // cooperative layouts exist for up to 320 columns).
 const void* pair_kernel(int cols_per_lane, int variant) {
@@ -1048,7 +1038,7 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   // Persistent warps stage nothing, so each warp's slot is just its fixed arrays;
   // large batches (more problems than 64 per SM) take the wide layout, batches of
   // long problems the early-load variant.
-  const int sms = sm_count();
+  const int sms = device_sm_count();
   const bool wide = plan->cols_per_lane <= 10 &&
                     static_cast<int64_t>(plan->num_problems) > static_cast<int64_t>(kWideProblemsPerSm) * sms;
   const int variant = wide ? kVarWide : (early ? kVarEarly : kVarRegs);

@@ -47,6 +47,9 @@ def _objective(cost_layer, sizes, pairs):
 @pytest.mark.parametrize("name,kw", [("cpu1", {}), ("step", {}), ("ties", {}), ("crowd", {}),
                                      ("sweep", {"images": 128})])
 def test_forward_matches_scipy_on_device_cost(name, kw):
+    """Every persistent solver layout: one problem per CTA (cpu1, step: small batches), the early-load
+    warps (ties, crowd: 64+ rows) and register warps pulling from the counter (sweep at 128 images:
+    1,664 problems, more than fit at once one per CTA); the full sweep's wide layout is tested below."""
     wl = workloads.make(name, **kw)
     res, cost = _run(wl)
     _check_same_matrix(wl, res, cost, scipy_lsa)

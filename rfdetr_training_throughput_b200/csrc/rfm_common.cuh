@@ -22,6 +22,11 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Waits until the grid this one was launched after (with programmatic stream
+// serialization) has completed and its memory operations are visible; returns
+// at once for a grid launched without that attribute.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // SMs of the current device (1 if the runtime cannot say).
 inline int device_sm_count() {
   int dev = 0, n = 0;

@@ -451,6 +451,10 @@ __device__ __forceinline__ void cost_targets(const TargetRow* s_t, int c_begin, 
 
 template <int NCLS, int kCols>
 __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs a) {
+  // A solver launched after this kernel with programmatic stream serialization
+  // may start its prologue now; it waits for this grid's completion (and its
+  // stores) before it reads the matrix.
+  asm volatile("griddepcontrol.launch_dependents;");
   __shared__ TargetRow s_t[kCols];
   __shared__ int s_seg[kCols + 1];
   __shared__ int s_nseg;

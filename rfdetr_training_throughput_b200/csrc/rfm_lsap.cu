@@ -352,6 +352,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   int64_t* t_out = kDense ? nullptr : a.t_out + out_off;
 
   if (nr == 0) {
+    if (kCoop) grid_dependency_wait();
     const int next = claim_next(a, lane);
     if (kDense) {
       for (int w = lane; w < nq; w += 32) q_out[w] = -1;
@@ -401,6 +402,9 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   // minv - spc >= 0), which raises those columns' reduced costs, and columns
   // only ever turn from free to matched, which raises their tie keys.  Should
   // rounding ever make a dual step negative, every pending pick is dropped.
+  // the one-problem-per-CTA launch may start while the cost kernel finishes:
+  // everything above only touched the descriptor and shared memory
+  if (kCoop) grid_dependency_wait();
   const float* src = a.cost + cost_off;
   const int64_t fixed = fixed_warp_bytes(kCols, a.max_rows, kWide);
   float* tile = reinterpret_cast<float*>(base + fixed);
@@ -860,6 +864,28 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
   if (!ensure_dynamic_smem(fn, smem)) return launch_status();
   const dim3 grid(static_cast<unsigned>(num_ctas));
   const dim3 block(32 * warps_per_cta);
+  if constexpr (kVariant == kVarCoop && !kDense) {
+    // programmatic stream serialization: the CTAs may launch while the kernel
+    // before this one (the cost kernel) finishes; they wait for it
+    // (griddepcontrol.wait) before reading the matrix
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cols_per_lane == 4 ? cudaLaunchKernelEx(&cfg, lsap_kernel<4, false, kVarCoop>, a)
+                                             : cudaLaunchKernelEx(&cfg, lsap_kernel<10, false, kVarCoop>, a);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) ? RFM_ERR_NO_DEVICE : RFM_ERR_LAUNCH;
+    }
+    return launch_status();
+  }
   switch (cols_per_lane) {
     case 4: lsap_kernel<4, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
     case 10: lsap_kernel<10, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;

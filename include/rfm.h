@@ -18,6 +18,10 @@
  *              (kernels_lap.py:271-305, :332-355) together with the device
  *              unpack of the patched _assign_padded (patches.py:379-418).
  *
+ *   rfm_match  rfm_cost (target-major) then rfm_lsap in one call, the two
+ *              kernels overlapped at their boundary: what the fused matcher
+ *              step (HungarianMatcher.forward) runs.
+ *
  *   rfm_lsap_dense  the same solver under the torch_linear_assignment
  *              contract: cost [P, W, T] -> matching [P, W] (task or -1).
  *              Replaces batch_lap (kernels_lap.py:332-355) behind the
@@ -194,6 +198,26 @@ int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, int64_t str
 int rfm_lsap(const float* cost, const rfm_problem* problems, const int32_t* ctas,
              const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out, int32_t* status,
              void* workspace, void* stream);
+
+/*
+ * The whole matcher step in one call: rfm_cost into the target-major `cost`
+ * ([num_layers, sum_targets, ld]) followed by rfm_lsap on it, with the same
+ * arguments and results as those two calls.  No counterpart in the reference
+ * (whose step is the Triton cost kernel, a padded copy and the solver launched
+ * separately, patches.py:123-149,379-418).  The plan must have been made for
+ * that matrix (stride_q 1, stride_t ld).  With a persistent plan the cost
+ * kernel resets the solver's counter in `workspace`, so no memset runs between
+ * the kernels, and the solver is launched with programmatic stream
+ * serialization: its CTAs start while the cost kernel finishes and wait for
+ * its completion before they read the matrix.
+ */
+int rfm_match(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+              const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
+              int num_queries, int num_classes, int sum_targets, int64_t ld, float cost_class,
+              float cost_bbox, float cost_giou, float focal_alpha, float* cost,
+              const rfm_problem* problems, const int32_t* ctas, const rfm_lsap_plan* plan,
+              int64_t* query_out, int64_t* target_out, int32_t* status, void* workspace,
+              void* stream);
 
 /*
  * torch_linear_assignment.batch_linear_assignment contract

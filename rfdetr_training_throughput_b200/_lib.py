@@ -35,6 +35,7 @@ EXPORTS = (
     "rfm_cost",
     "rfm_lsap_make_plan",
     "rfm_lsap",
+    "rfm_match",
     "rfm_lsap_dense_workspace_bytes",
     "rfm_lsap_dense",
     "rfm_lsap_dense_noalloc",
@@ -125,6 +126,9 @@ def load() -> ctypes.CDLL:
     lib.rfm_lsap_make_plan.argtypes = [_p, _i32, _i64, _i64, _i64, _p, ctypes.POINTER(LsapPlan)]
     lib.rfm_lsap.restype = _i32
     lib.rfm_lsap.argtypes = [_p, _p, _p, ctypes.POINTER(LsapPlan), _p, _p, _p, _p, _p]
+    lib.rfm_match.restype = _i32
+    lib.rfm_match.argtypes = [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _f32, _f32, _f32, _p,
+                              _p, _p, ctypes.POINTER(LsapPlan), _p, _p, _p, _p, _p]
     lib.rfm_lsap_dense_workspace_bytes.restype = _i64
     lib.rfm_lsap_dense_workspace_bytes.argtypes = [_i32, _i32, _i32]
     lib.rfm_lsap_dense.restype = _i32

@@ -27,6 +27,14 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // at once for a grid launched without that attribute.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// rfm_cost with `reset_word` (when not null, and the layout is target-major)
+// set to 0 by the cost kernel: rfm_match uses it for the solver's counter.
+int cost_run(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+             const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
+             int num_queries, int num_classes, int sum_targets, int64_t ld, int layout,
+             float cost_class, float cost_bbox, float cost_giou, float focal_alpha, float* out,
+             int* reset_word, void* stream);
+
 // SMs of the current device (1 if the runtime cannot say).
 inline int device_sm_count() {
   int dev = 0, n = 0;

@@ -60,6 +60,7 @@ struct CostArgs {
   int rows_per_cta;
   float w_class, w_bbox, w_giou, alpha, alpha_m1;
   float* out;            // [L, Q, ld]
+  int* reset_word;       // target-major only: set to 0 by one thread (a solver counter), or null
 };
 
 struct Corners {
@@ -455,6 +456,7 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
   // may start its prologue now; it waits for this grid's completion (and its
   // stores) before it reads the matrix.
   asm volatile("griddepcontrol.launch_dependents;");
+  if (a.reset_word != nullptr && (blockIdx.x | blockIdx.y | blockIdx.z | threadIdx.x) == 0) *a.reset_word = 0;
   __shared__ TargetRow s_t[kCols];
   __shared__ int s_seg[kCols + 1];
   __shared__ int s_nseg;
@@ -563,13 +565,12 @@ void launch_tmajor(const CostArgs& a, dim3 grid, int num_classes, cudaStream_t s
 }  // namespace
 }  // namespace rfm
 
-extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
-                        const int64_t* tgt_labels, const float* tgt_boxes,
-                        const int32_t* tgt_offsets, int num_layers, int num_images,
-                        int num_queries, int num_classes, int sum_targets, int64_t ld, int layout,
-                        float cost_class, float cost_bbox, float cost_giou, float focal_alpha,
-                        float* out, void* stream) {
-  using namespace rfm;
+namespace rfm {
+int cost_run(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+             const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
+             int num_queries, int num_classes, int sum_targets, int64_t ld, int layout,
+             float cost_class, float cost_bbox, float cost_giou, float focal_alpha, float* out,
+             int* reset_word, void* stream) {
   if (num_layers < 1 || num_layers > 65535 || num_images < 1 || num_queries < 1 ||
       num_classes < 1 || sum_targets < 0) {
     return RFM_ERR_INVALID_ARGUMENT;
@@ -613,6 +614,7 @@ extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
   // torch multiplies by the Python scalar (1 - alpha), rounded once to float32
   a.alpha_m1 = -static_cast<float>(1.0 - static_cast<double>(focal_alpha));
   a.out = out;
+  a.reset_word = reset_word;
 
   if (layout == RFM_LAYOUT_TARGET_MAJOR) {
     const int64_t gy = (ld / kQpt + kTmThreads - 1) / kTmThreads;
@@ -650,4 +652,17 @@ extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
     cost_qmajor_kernel<false><<<grid, block, 0, as_stream(stream)>>>(a);
   }
   return launch_status();
+}
+
+}  // namespace rfm
+
+extern "C" int rfm_cost(const float* pred_logits, const float* pred_boxes,
+                        const int64_t* tgt_labels, const float* tgt_boxes,
+                        const int32_t* tgt_offsets, int num_layers, int num_images,
+                        int num_queries, int num_classes, int sum_targets, int64_t ld, int layout,
+                        float cost_class, float cost_bbox, float cost_giou, float focal_alpha,
+                        float* out, void* stream) {
+  return rfm::cost_run(pred_logits, pred_boxes, tgt_labels, tgt_boxes, tgt_offsets, num_layers, num_images,
+                       num_queries, num_classes, sum_targets, ld, layout, cost_class, cost_bbox, cost_giou,
+                       focal_alpha, out, nullptr, stream);
 }

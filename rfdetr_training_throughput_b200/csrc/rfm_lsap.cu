@@ -352,7 +352,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   int64_t* t_out = kDense ? nullptr : a.t_out + out_off;
 
   if (nr == 0) {
-    if (kCoop) grid_dependency_wait();
+    grid_dependency_wait();
     const int next = claim_next(a, lane);
     if (kDense) {
       for (int w = lane; w < nq; w += 32) q_out[w] = -1;
@@ -402,9 +402,10 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   // minv - spc >= 0), which raises those columns' reduced costs, and columns
   // only ever turn from free to matched, which raises their tie keys.  Should
   // rounding ever make a dual step negative, every pending pick is dropped.
-  // the one-problem-per-CTA launch may start while the cost kernel finishes:
-  // everything above only touched the descriptor and shared memory
-  if (kCoop) grid_dependency_wait();
+  // a launch with programmatic stream serialization may start while the cost
+  // kernel finishes: everything above only touched the descriptor and shared
+  // memory, and every counter claim comes after this point
+  grid_dependency_wait();
   const float* src = a.cost + cost_off;
   const int64_t fixed = fixed_warp_bytes(kCols, a.max_rows, kWide);
   float* tile = reinterpret_cast<float*>(base + fixed);
@@ -848,7 +849,7 @@ int resident_ctas(int cols_per_lane, int variant, int64_t smem) {
 
 template <bool kDense, int kVariant>
 int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta, int64_t smem,
-           void* stream) {
+           void* stream, bool after_kernel = false) {
   if (smem > kSmemPerBlockMax) return RFM_ERR_UNSUPPORTED;
   const void* fn = nullptr;
   switch (cols_per_lane) {
@@ -864,10 +865,10 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
   if (!ensure_dynamic_smem(fn, smem)) return launch_status();
   const dim3 grid(static_cast<unsigned>(num_ctas));
   const dim3 block(32 * warps_per_cta);
-  if constexpr (kVariant == kVarCoop && !kDense) {
+  if (!kDense && kVariant != kVarEarly && cols_per_lane <= 10 && (kVariant == kVarCoop || after_kernel)) {
     // programmatic stream serialization: the CTAs may launch while the kernel
     // before this one (the cost kernel) finishes; they wait for it
-    // (griddepcontrol.wait) before reading the matrix
+    // (griddepcontrol.wait) before reading the matrix or the counter
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -878,8 +879,9 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     attr.val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
-    const cudaError_t e = cols_per_lane == 4 ? cudaLaunchKernelEx(&cfg, lsap_kernel<4, false, kVarCoop>, a)
-                                             : cudaLaunchKernelEx(&cfg, lsap_kernel<10, false, kVarCoop>, a);
+    constexpr int kV = (kDense || kVariant == kVarEarly) ? kVarRegs : kVariant;
+    const cudaError_t e = cols_per_lane == 4 ? cudaLaunchKernelEx(&cfg, lsap_kernel<4, false, kV>, a)
+                                             : cudaLaunchKernelEx(&cfg, lsap_kernel<10, false, kV>, a);
     if (e != cudaSuccess) {
       cudaGetLastError();
       return (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) ? RFM_ERR_NO_DEVICE : RFM_ERR_LAUNCH;
@@ -1014,10 +1016,14 @@ extern "C" int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, 
   return RFM_OK;
 }
 
-extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const int32_t* ctas,
-                        const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out,
-                        int32_t* status, void* workspace, void* stream) {
-  using namespace rfm;
+namespace rfm {
+namespace {
+// rfm_lsap; with `counter_zeroed` the persistent counter was reset by the cost
+// kernel that runs just before on the stream, so there is no memset and the
+// persistent launch overlaps that kernel's end.
+int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas, const rfm_lsap_plan* plan,
+             int64_t* query_out, int64_t* target_out, int32_t* status, void* workspace, void* stream,
+             bool counter_zeroed) {
   if (plan == nullptr || plan->num_problems < 0 || plan->num_ctas < 0 || plan->max_rows < 1 ||
       plan->workspace_bytes < 0 || plan->stride_q < 0 || plan->stride_t < 0 ||
       plan->tile_cap_floats < 0 || plan->cta_smem_bytes < 0 || plan->cta_smem_bytes > kSmemPerBlockMax ||
@@ -1084,16 +1090,54 @@ extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const in
   a.queue = static_cast<int*>(workspace);
   a.workspace = reinterpret_cast<float*>(static_cast<char*>(workspace) + kQueueBytes);
   a.slot = static_cast<int>(smem / kMaxWarpsPerCta);
-  if (cudaMemsetAsync(a.queue, 0, sizeof(int), as_stream(stream)) != cudaSuccess) return launch_status();
+  if (!counter_zeroed && cudaMemsetAsync(a.queue, 0, sizeof(int), as_stream(stream)) != cudaSuccess) {
+    return launch_status();
+  }
   const int ctas_per_sm = resident_ctas(plan->cols_per_lane, variant, smem);
   if (ctas_per_sm < 1) return launch_status() != RFM_OK ? RFM_ERR_LAUNCH : RFM_ERR_UNSUPPORTED;
   const int grid = ctas_per_sm * sms;
   const int needed = (plan->num_problems + kMaxWarpsPerCta - 1) / kMaxWarpsPerCta;
   const int num_ctas = grid < needed ? grid : needed;
   a.claim_base = num_ctas * kMaxWarpsPerCta;
-  if (variant == kVarWide) return launch<false, kVarWide>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
-  if (variant == kVarEarly) return launch<false, kVarEarly>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
-  return launch<false, kVarRegs>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
+  if (variant == kVarWide) {
+    return launch<false, kVarWide>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream, counter_zeroed);
+  }
+  if (variant == kVarEarly) {
+    return launch<false, kVarEarly>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream);
+  }
+  return launch<false, kVarRegs>(a, plan->cols_per_lane, num_ctas, kMaxWarpsPerCta, smem, stream, counter_zeroed);
+}
+}  // namespace
+}  // namespace rfm
+
+extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const int32_t* ctas,
+                        const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out,
+                        int32_t* status, void* workspace, void* stream) {
+  return rfm::lsap_run(cost, problems, ctas, plan, query_out, target_out, status, workspace, stream, false);
+}
+
+extern "C" int rfm_match(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+                         const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
+                         int num_queries, int num_classes, int sum_targets, int64_t ld, float cost_class,
+                         float cost_bbox, float cost_giou, float focal_alpha, float* cost,
+                         const rfm_problem* problems, const int32_t* ctas, const rfm_lsap_plan* plan,
+                         int64_t* query_out, int64_t* target_out, int32_t* status, void* workspace,
+                         void* stream) {
+  using namespace rfm;
+  // the solver must read the matrix this call writes: target-major, row stride ld
+  if (plan == nullptr || plan->stride_q != 1 || plan->stride_t != ld ||
+      (plan->num_problems > 0 && sum_targets < 1)) {
+    return RFM_ERR_INVALID_ARGUMENT;
+  }
+  const bool persistent = (plan->flags & RFM_PLAN_PERSISTENT) != 0;
+  const bool reset = persistent && plan->num_problems > 0 && workspace != nullptr &&
+                     plan->workspace_bytes >= kQueueBytes;
+  const int rc = cost_run(pred_logits, pred_boxes, tgt_labels, tgt_boxes, tgt_offsets, num_layers, num_images,
+                          num_queries, num_classes, sum_targets, ld, RFM_LAYOUT_TARGET_MAJOR, cost_class,
+                          cost_bbox, cost_giou, focal_alpha, cost, reset ? static_cast<int*>(workspace) : nullptr,
+                          stream);
+  if (rc != RFM_OK) return rc;
+  return lsap_run(cost, problems, ctas, plan, query_out, target_out, status, workspace, stream, reset);
 }
 
 namespace {

@@ -369,6 +369,25 @@ def launch_lsap(cost: torch.Tensor, plan: StepPlan, pairs: torch.Tensor, status:
         _stream_handle(cost.device) if stream is None else stream))
 
 
+def launch_match(logits: torch.Tensor, boxes: torch.Tensor, labels: torch.Tensor, tgt_boxes: torch.Tensor,
+                 plan: StepPlan, sum_t: int, weights: dict, cost: torch.Tensor, pairs: torch.Tensor,
+                 status: torch.Tensor | None, stream: ctypes.c_void_p | None = None) -> None:
+    """Enqueue ``rfm_match``: the cost kernel into the target-major ``cost`` [L, S, ld] and the solver over
+    it, overlapped at their boundary (no memset between them, programmatic launch of the solver)."""
+    layers, nimg, queries, ncls = logits.shape
+    lib = _lib.load()
+    ws = None
+    if plan.plan.workspace_bytes > 0:
+        ws = torch.empty(int(plan.plan.workspace_bytes), dtype=torch.uint8, device=cost.device)
+    _lib.check("rfm_match", lib.rfm_match(
+        _ptr(logits), _ptr(boxes), _ptr(labels), _ptr(tgt_boxes), ctypes.c_void_p(plan.offsets_ptr),
+        layers, nimg, queries, ncls, sum_t, plan.ld,
+        float(weights["cost_class"]), float(weights["cost_bbox"]), float(weights["cost_giou"]),
+        float(weights["focal_alpha"]), _ptr(cost), ctypes.c_void_p(plan.problems_ptr), ctypes.c_void_p(plan.ctas_ptr),
+        ctypes.byref(plan.plan), _ptr(pairs[0]), _ptr(pairs[1]), _ptr(status), _ptr(ws),
+        _stream_handle(cost.device) if stream is None else stream))
+
+
 def raise_on_status(status: torch.Tensor) -> None:
     """Host check of per-problem solver status (synchronises; SciPy's error messages)."""
     st = status.cpu()
@@ -401,7 +420,8 @@ def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: P
     ``extras``, when given, receives the target-major cost buffer ``[L, S, ld]``
     (``"cost"``), its row stride and the step plan.  ``events``, when given,
     collects CUDA events recorded on the launching stream around each kernel
-    (``"cost"`` and ``"lsap"``: start/end pairs).
+    (``"cost"`` and ``"lsap"``: start/end pairs); the step is then issued as two
+    calls (``rfm_cost``, ``rfm_lsap``) instead of the one ``rfm_match``.
     """
     w = DEFAULT_WEIGHTS if weights is None else weights
     logits, boxes = _prepare_predictions(pred_logits, pred_boxes)
@@ -424,14 +444,19 @@ def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: P
         pairs = out
     status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=device) if check_status else None
     stream = _stream_handle(device)
-    if sum_t > 0:
-        _record(events, "cost")
-        launch_cost(logits, boxes, tg.labels, tg.boxes, plan.offsets_ptr, sum_t, ld, layout, w, cost, stream)
-        _record(events, "cost")
-    if plan.problems.shape[0] > 0:
-        _record(events, "lsap")
-        launch_lsap(cost, plan, pairs, status, stream)
-        _record(events, "lsap")
+    if events is None and sum_t > 0 and plan.problems.shape[0] > 0:
+        # one call: the cost kernel and the solver overlapped at their boundary
+        launch_match(logits, boxes, tg.labels, tg.boxes, plan, sum_t, w, cost, pairs, status, stream)
+    else:
+        # two calls, so that events can be recorded around each kernel
+        if sum_t > 0:
+            _record(events, "cost")
+            launch_cost(logits, boxes, tg.labels, tg.boxes, plan.offsets_ptr, sum_t, ld, layout, w, cost, stream)
+            _record(events, "cost")
+        if plan.problems.shape[0] > 0:
+            _record(events, "lsap")
+            launch_lsap(cost, plan, pairs, status, stream)
+            _record(events, "lsap")
     if status is not None:
         raise_on_status(status)
     if extras is not None:

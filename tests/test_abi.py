@@ -67,6 +67,13 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call():
     assert lib.rfm_lsap(None, None, None, None, None, None, None, None, None) == 1
     plan.cols_per_lane = 7
     assert lib.rfm_lsap(None, None, None, ctypes.byref(plan), None, None, None, None, None) == 1
+    # rfm_match: the plan must address the target-major matrix the call writes (stride_q 1,
+    # stride_t ld), and a plan with problems needs targets
+    match_args = lambda p, ld, s: (None, None, None, None, None, 1, 1, 8, 1, s, ld, 1.0, 1.0, 1.0, 0.25, None,
+                                   None, None, p, None, None, None, None, None)
+    assert lib.rfm_match(*match_args(None, 8, 3)) == 1
+    assert lib.rfm_match(*match_args(ctypes.byref(plan), 12, 3)) == 1  # plan made for ld 8
+    assert lib.rfm_match(*match_args(ctypes.byref(plan), 8, 0)) == 1   # problems but no targets
     assert lib.rfm_lsap_dense(None, -1, 3, 3, None, None, None, None) == 1
     assert lib.rfm_lsap_dense(None, 4, 2000, 3, None, None, None, None) == 2
     assert lib.rfm_lsap_dense_workspace_bytes(-1, 3, 3) < 0

@@ -1,8 +1,8 @@
 """The matcher step captured as a CUDA graph, for batches whose shape repeats.
 
 ``match_packed`` already runs on the device without a host synchronisation, but
-every call still pays its host cost (plan lookup, three allocations, two FFI
-launches and a memset, ~30-50 us of Python and driver work).  On the production
+every call still pays its host cost (plan lookup, three allocations, the FFI
+call and its two kernel launches, ~30-50 us of Python and driver work).  On the production
 step (5 layers x 8 images x 13 groups) that is as long as the GPU work itself.
 ``MatchGraph`` records the step once for a fixed shape (targets per image,
 layers, queries, classes, group split, weights) and replays it with a single
@@ -14,8 +14,8 @@ The graph reads its inputs from its own device buffers (``logits``, ``boxes``,
 ``labels``, ``tgt_boxes``) and writes the pairs of every replay to the same
 ``pairs`` buffer (its own, or the ``out`` tensor given at construction): copy
 new inputs in (``__call__`` does) and read or copy the result before the next
-replay.  Stream capture covers the cost kernel, the
-solver's queue reset and the solver kernel; plans and launch parameters are
+replay.  Stream capture covers the cost kernel (which also resets the
+solver's counter) and the solver kernel; plans and launch parameters are
 host-side values fixed at capture time, which is exactly what a fixed shape
 pins.
 """

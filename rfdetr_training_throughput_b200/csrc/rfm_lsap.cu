@@ -1130,8 +1130,12 @@ extern "C" int rfm_match(const float* pred_logits, const float* pred_boxes, cons
     return RFM_ERR_INVALID_ARGUMENT;
   }
   const bool persistent = (plan->flags & RFM_PLAN_PERSISTENT) != 0;
-  const bool reset = persistent && plan->num_problems > 0 && workspace != nullptr &&
-                     plan->workspace_bytes >= kQueueBytes;
+  // a workspace the solver would reject is rejected before the cost kernel is enqueued
+  if (plan->workspace_bytes < 0 || (plan->workspace_bytes > 0 && workspace == nullptr) ||
+      (persistent && plan->num_problems > 0 && plan->workspace_bytes < kQueueBytes)) {
+    return RFM_ERR_INVALID_ARGUMENT;
+  }
+  const bool reset = persistent && plan->num_problems > 0;
   const int rc = cost_run(pred_logits, pred_boxes, tgt_labels, tgt_boxes, tgt_offsets, num_layers, num_images,
                           num_queries, num_classes, sum_targets, ld, RFM_LAYOUT_TARGET_MAJOR, cost_class,
                           cost_bbox, cost_giou, focal_alpha, cost, reset ? static_cast<int*>(workspace) : nullptr,

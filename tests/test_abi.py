@@ -74,6 +74,9 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call():
     assert lib.rfm_match(*match_args(None, 8, 3)) == 1
     assert lib.rfm_match(*match_args(ctypes.byref(plan), 12, 3)) == 1  # plan made for ld 8
     assert lib.rfm_match(*match_args(ctypes.byref(plan), 8, 0)) == 1   # problems but no targets
+    persistent = _lib.LsapPlan(cols_per_lane=10, max_rows=1, num_problems=3, num_ctas=0, cta_smem_bytes=4096,
+                               tile_cap_floats=0, flags=1, reserved=0, stride_q=1, stride_t=8, workspace_bytes=256)
+    assert lib.rfm_match(*match_args(ctypes.byref(persistent), 8, 3)) == 1  # persistent plan, no workspace
     assert lib.rfm_lsap_dense(None, -1, 3, 3, None, None, None, None) == 1
     assert lib.rfm_lsap_dense(None, 4, 2000, 3, None, None, None, None) == 2
     assert lib.rfm_lsap_dense_workspace_bytes(-1, 3, 3) < 0

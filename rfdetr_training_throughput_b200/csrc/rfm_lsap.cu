@@ -668,20 +668,24 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
       t_out[k] = -1;
     }
   } else if (s.transposed) {
-    // rows are targets: emit matched queries (solver columns) in ascending order
+    // rows are targets: emit matched queries (solver columns) in ascending
+    // order.  The ballots list the matched columns in shared memory (`remaining`
+    // is free by now); the warp then writes the pairs with coalesced stores.
+    int16_t* list = rem_s;
     int slot0 = 0;
     const unsigned lt_mask = (1u << lane) - 1u;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const bool matched = ((valid & ~freem) >> k) & 1u;
       const unsigned ballot = __ballot_sync(kFullMask, matched);
-      if (matched) {
-        const int j = lane + 32 * k;
-        const int slot = slot0 + __popc(ballot & lt_mask);
-        q_out[slot] = j + qbase;
-        t_out[slot] = row4col_s[j];
-      }
+      if (matched) list[slot0 + __popc(ballot & lt_mask)] = static_cast<int16_t>(lane + 32 * k);
       slot0 += __popc(ballot);
+    }
+    __syncwarp();
+    for (int e = lane; e < slot0; e += 32) {
+      const int j = list[e];
+      q_out[e] = j + qbase;
+      t_out[e] = row4col_s[j];
     }
   } else {
     for (int r = lane; r < nr; r += 32) {

@@ -18,9 +18,21 @@ Keys beyond the base contract:
                 CUDA-event duration, against the measured copy bandwidth;
   lsap          the solver kernel's device time and problems/s;
   cpu_baseline  the reference's CPU path (torch CPU op chain + SciPy on a thread
-                pool) on a bounded sample of the same workload, rank 0, N = 1.
+                pool of every host thread this process may use) on a bounded
+                sample of the same workload, rank 0, N = 1;
+  configs       (N = 1) every benchmark configuration -- step, crowd, ties and
+                sweep -- with its device time through ``match_packed`` and the
+                reference CPU path on the same inputs, serial (one thread, as the
+                unpatched matcher solves) and on the reference's 8-thread pool;
+  per_rank_step_ms  min / median / max / mean device ms of the timed steps on
+                every rank.
 
-``--impl reference`` times that CPU path alone, with every host thread.
+Timed regions start behind a short device-side delay (``torch.cuda._sleep``,
+outside the events), so the host has enqueued the first steps before the GPU
+reaches them and a late host launch cannot leave the GPU idle inside a step.
+
+``--impl reference`` times that CPU path alone, with the same thread setting as
+``cpu_baseline``.
 """
 
 from __future__ import annotations
@@ -45,6 +57,9 @@ METRIC = "matched problems/s (cost+LSAP) at 1/2/4/8 B200; cost-kernel HBM GB/s v
 UNIT = "problems/s"
 FALLBACK_HBM_GBS = 6650.0
 L2_FLUSH_BYTES = 256 << 20
+LEAD_CYCLES = 2_000_000  # ~1 ms at 1.9 GHz of device-side delay before each timed region
+CONFIG_NAMES = ("step", "crowd", "ties", "sweep")
+REFERENCE_POOL_THREADS = 8  # LAP_THREADS default of the parallel_lap patch (patches.py:210)
 
 
 def parse() -> argparse.Namespace:
@@ -63,6 +78,11 @@ def parse() -> argparse.Namespace:
                     help="skip the 5-layer x 8-image production-step timing (eager vs CUDA graph)")
     ap.add_argument("--sharded", action="store_true",
                     help="also time the strong-scaled sharded sweep (runs by default when N > 1)")
+    ap.add_argument("--sharded-images", type=int, nargs="*", default=[1024, 8192],
+                    help="batch sizes (images) of the strong-scaled sharded sweep")
+    ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration table (N = 1)")
+    ap.add_argument("--config-cpu-seconds", type=float, default=2.0,
+                    help="CPU time budget of each CPU leg of the per-configuration table")
     return ap.parse_args()
 
 
@@ -208,8 +228,19 @@ def gpu_local_cpus(device: torch.device) -> set[int] | None:
         return None
 
 
-def cpu_path_rate(wl, images: int, budget_s: float, threads: int, min_reps: int = 1) -> dict:
-    """problems/s of the reference CPU path on the first ``images`` images, repeated for ~budget_s."""
+def host_threads() -> int:
+    """Host CPUs this process may run on (its affinity set)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_path_rate(wl, images: int, budget_s: float, lap_threads: int, torch_threads: int,
+                  min_reps: int = 1) -> dict:
+    """problems/s of the reference CPU path on the first ``images`` images, repeated for ~budget_s:
+    the torch CPU op chain on ``torch_threads`` intra-op threads, then SciPy per block, serially when
+    ``lap_threads`` is 1, else on a pool of that many threads."""
     from oracle.cpu_path import CpuMatcher
 
     images = min(images, wl.images)
@@ -217,7 +248,9 @@ def cpu_path_rate(wl, images: int, budget_s: float, threads: int, min_reps: int 
     boxes = wl.pred_boxes[:, :images].contiguous()
     targets = wl.targets[:images]
     problems = wl.layers * wl.group_detr * sum(1 for t in targets if t["labels"].shape[0])
-    m = CpuMatcher(threads=threads)
+    saved = torch.get_num_threads()
+    torch.set_num_threads(torch_threads)
+    m = CpuMatcher(threads=lap_threads)
     try:
         m.match(logits, boxes, targets, wl.group_detr, wl.weights)  # warm
         reps, t0 = 0, time.perf_counter()
@@ -227,8 +260,17 @@ def cpu_path_rate(wl, images: int, budget_s: float, threads: int, min_reps: int 
         elapsed = time.perf_counter() - t0
     finally:
         m.close()
+        torch.set_num_threads(saved)
     return {"value": problems * reps / elapsed, "unit": UNIT, "seconds": elapsed, "reps": reps,
-            "problems_per_rep": problems}
+            "problems_per_rep": problems, "images": images, "scipy_threads": lap_threads,
+            "torch_threads": torch_threads}
+
+
+def cpu_baseline_setting() -> tuple[int, int]:
+    """(SciPy pool threads, torch threads) of the headline CPU baseline and of ``--impl reference``:
+    every host thread this process may use, for both."""
+    n = host_threads()
+    return n, n
 
 
 def run_reference(args) -> None:
@@ -237,18 +279,17 @@ def run_reference(args) -> None:
         return
     from rfdetr_training_throughput_b200 import workloads
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
+    lap_threads, torch_threads = cpu_baseline_setting()
     wl = workloads.make(args.workload, images=args.images)
     images = min(args.cpu_images, wl.images)
-    sample = {"images": images}
     from oracle.cpu_path import CpuMatcher
 
     logits = wl.pred_logits[:, :images].contiguous()
     boxes = wl.pred_boxes[:, :images].contiguous()
     targets = wl.targets[:images]
     problems = wl.layers * wl.group_detr * sum(1 for t in targets if t["labels"].shape[0])
-    m = CpuMatcher(threads=threads)
+    torch.set_num_threads(torch_threads)
+    m = CpuMatcher(threads=lap_threads)
     try:
         for _ in range(args.warmup):
             m.match(logits, boxes, targets, wl.group_detr, wl.weights)
@@ -260,20 +301,84 @@ def run_reference(args) -> None:
         m.close()
     value = problems * args.steps / elapsed
     sample_desc = (f"first {images} images of the {wl.name} workload per step ({problems} problems): torch CPU "
-                   f"op chain + scipy.optimize.linear_sum_assignment on a {threads}-thread pool")
+                   f"op chain ({torch_threads} threads) + scipy.optimize.linear_sum_assignment on a "
+                   f"{lap_threads}-thread pool; host has {os.cpu_count()} CPUs, {host_threads()} usable")
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 cost, fp64 LSAP",
         "data": "synthetic", "config": workload_config(wl),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample_desc},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": lap_threads, "kind": "port", "sample": sample_desc,
+                         "host_cpu_count": os.cpu_count(), "torch_threads": torch_threads},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    line["config"]["cpu_sample"] = sample
+    line["config"]["cpu_sample"] = {"images": images}
     emit(line)
 
 
 # --------------------------------------------------------------------------- GPU path
+
+
+def time_device_steps(fn, steps: int, warmup: int, flush: torch.Tensor, device, barrier=None) -> list[float]:
+    """Device ms of each of ``steps`` calls of ``fn`` (CUDA events on the launching stream), the L2
+    flushed between calls outside the events.  The region starts behind a device-side delay so the
+    host is ahead of the GPU from the first step on."""
+    for _ in range(max(warmup, 1)):
+        fn()
+    torch.cuda.synchronize(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if barrier is not None:
+        barrier()
+    torch.cuda.synchronize(device)
+    torch.cuda._sleep(LEAD_CYCLES)
+    for k in range(steps):
+        starts[k].record()
+        fn()
+        ends[k].record()
+        flush.zero_()
+    torch.cuda.synchronize(device)
+    if barrier is not None:
+        barrier()
+    return [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+
+def step_stats(ms: list[float]) -> dict:
+    return {"min": min(ms), "median": statistics.median(ms), "max": max(ms), "mean": statistics.mean(ms)}
+
+
+def config_table(device, args, flush, sweep_wl) -> dict:
+    """Every benchmark configuration on this GPU through ``match_packed`` (device time per step, L2
+    flushed between steps) with the reference CPU path on the same inputs beside it: serial (one
+    thread for the op chain and the solves) and on the reference's pool (8 SciPy threads, every host
+    thread for the op chain).  The sweep's CPU legs run on its first ``--cpu-images`` images."""
+    from rfdetr_training_throughput_b200 import matcher, workloads
+
+    out = {"host_cpu_count": os.cpu_count(), "host_threads_usable": host_threads()}
+    for name in CONFIG_NAMES:
+        wl = sweep_wl if name == "sweep" else workloads.make(name)
+        logits, boxes = wl.pred_logits.to(device), wl.pred_boxes.to(device)
+        packed = matcher.PackedTargets.from_list(wl.targets_on(device), device)
+
+        def fn():
+            matcher.match_packed(logits, boxes, packed, wl.group_detr, weights=wl.weights)
+
+        steps = max(3, min(args.steps, 50))
+        ms = time_device_steps(fn, steps, max(args.warmup, 3), flush, device)
+        mean = statistics.mean(ms)
+        entry = {"problems": wl.num_problems, "images": wl.images, "layers": wl.layers, "classes": wl.classes,
+                 "targets": int(sum(wl.sizes)), "max_targets": max(wl.sizes), "gpu_steps": steps,
+                 "gpu_ms_per_step": step_stats(ms), "gpu_problems_per_s": wl.num_problems / (mean / 1e3)}
+        if not args.no_cpu_baseline:
+            images = args.cpu_images if name == "sweep" else wl.images
+            serial = cpu_path_rate(wl, images, args.config_cpu_seconds, 1, 1)
+            pool = cpu_path_rate(wl, images, args.config_cpu_seconds, REFERENCE_POOL_THREADS, host_threads())
+            entry["cpu_serial"] = serial
+            entry["cpu_pool"] = pool
+            entry["gpu_over_cpu_pool"] = entry["gpu_problems_per_s"] / pool["value"]
+        out[name] = entry
+        del logits, boxes, packed
+    return out
 
 
 def run_rfm(args) -> None:
@@ -285,7 +390,7 @@ def run_rfm(args) -> None:
     device = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(device)
 
-    from rfdetr_training_throughput_b200 import _lib, matcher, workloads
+    from rfdetr_training_throughput_b200 import MatchGraph, _lib, matcher, workloads
 
     wl = workloads.make(args.workload, shard=rank, images=args.images)
     logits = wl.pred_logits.to(device)
@@ -304,25 +409,11 @@ def run_rfm(args) -> None:
     sampler = ClockSampler(device)
     sampler.start()
     extras: dict = {}
-    for _ in range(max(args.warmup, 1)):
-        step(extras=extras)
+    step(extras=extras)
     plan = extras["plan"]
-    ld = sum(wl.sizes)
-    torch.cuda.synchronize(device)
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize(device)
-    for k in range(args.steps):
-        starts[k].record()
-        step()  # the production call: rfm_match, cost kernel and solver overlapped at their boundary
-        ends[k].record()
-        flush.zero_()
-    torch.cuda.synchronize(device)
-    barrier()
+    # the production call: rfm_match, cost kernel and solver overlapped at their boundary
+    step_ms = time_device_steps(step, args.steps, args.warmup, flush, device, barrier)
     clocks = sampler.stop()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = float(sum(step_ms))
 
     # per-kernel durations (the roofline figures): the same steps issued as two calls with events
@@ -341,82 +432,48 @@ def run_rfm(args) -> None:
     lsap_ms = kernel_ms("lsap")
     launches = len(cost_ms) + len(lsap_ms)
 
-    total_t = torch.tensor([total_ms], dtype=torch.float64, device=device)
+    # the same step replayed as a captured CUDA graph (one host call per step)
+    graph = MatchGraph(wl.sizes, wl.layers, wl.queries, wl.classes, wl.group_detr, weights=wl.weights, device=device)
+    graph.logits.copy_(logits)
+    graph.boxes.copy_(boxes)
+    graph.labels.copy_(packed.labels)
+    graph.tgt_boxes.copy_(packed.boxes)
+    graph_ms = time_device_steps(graph.replay, args.steps, args.warmup, flush, device, barrier)
+    del graph
+
+    mine = torch.tensor([*step_stats(step_ms).values(), total_ms, float(sum(graph_ms))], dtype=torch.float64,
+                        device=device)
     if world > 1:
-        torch.distributed.all_reduce(total_t, op=torch.distributed.ReduceOp.MAX)
-    max_ms = float(total_t.item())
+        gathered = [torch.zeros_like(mine) for _ in range(world)]
+        torch.distributed.all_gather(gathered, mine)
+    else:
+        gathered = [mine]
+    per_rank = [dict(zip(("min", "median", "max", "mean", "total", "graph_total"), g.tolist())) for g in gathered]
+    max_ms = max(r["total"] for r in per_rank)
+    graph_max_ms = max(r["graph_total"] for r in per_rank)
     problems = wl.num_problems
     value = world * problems * args.steps / (max_ms / 1e3)
 
     # ---- end to end: pinned host inputs -> device -> match -> packed pairs back to host
     e2e = None
     if not args.no_e2e:
-        # pinned buffers on the GPU's own NUMA node (the thread that pins them runs on that node's
-        # CPUs), so the uploads do not cross the inter-socket link; the affinity is restored after
-        saved_cpus = os.sched_getaffinity(0)
-        local_cpus = gpu_local_cpus(device)
-        if local_cpus:
-            os.sched_setaffinity(0, local_cpus)
-        h_logits = wl.pred_logits.pin_memory()
-        h_boxes = wl.pred_boxes.pin_memory()
-        h_labels = torch.cat([t["labels"] for t in wl.targets]).pin_memory()
-        h_tboxes = torch.cat([t["boxes"] for t in wl.targets]).pin_memory()
-        sizes = wl.sizes
-        h_pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64).pin_memory()
-        h2d = sum(int(t.numel() * t.element_size()) for t in (h_logits, h_boxes, h_labels, h_tboxes))
-        d2h = int(h_pairs.numel() * h_pairs.element_size())
-
-        sizes = tuple(sizes)
-        from rfdetr_training_throughput_b200.pipeline import PrefetchingMatcher
-
-        pm = PrefetchingMatcher(wl.group_detr, weights=wl.weights, device=device)
-        host_batch = (h_logits, h_boxes, h_labels, h_tboxes, sizes)
-
-        def e2e_run(steps: int) -> None:
-            # every step copies its inputs from pinned host memory, matches them and reads its pairs
-            # back; the upload of step k+1 runs on its own stream while step k is matched
-            pm.copy_stream.wait_stream(torch.cuda.current_stream(device))
-            nxt = pm.prefetch(*host_batch)
-            for k in range(steps):
-                cur = nxt
-                if k + 1 < steps:
-                    nxt = pm.prefetch(*host_batch)
-                res = pm.match(cur)
-                h_pairs.copy_(res.pairs, non_blocking=True)
-
-        e2e_run(max(args.warmup, 1))
-        torch.cuda.synchronize(device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize(device)
-        e0.record()
-        e2e_run(args.steps)
-        e1.record()
-        torch.cuda.synchronize(device)
-        barrier()
-        e2e_ms = e0.elapsed_time(e1)
-        e2e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
-        if world > 1:
-            torch.distributed.all_reduce(e2e_t, op=torch.distributed.ReduceOp.MAX)
-        os.sched_setaffinity(0, saved_cpus)
-        e2e = {"value": world * problems * args.steps / (float(e2e_t.item()) / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "ms_per_step": float(e2e_t.item()) / args.steps,
-               "path": "PrefetchingMatcher: pinned H2D of step k+1 on a copy stream overlapping match + D2H of step k",
-               "host_buffers": (f"pinned by a thread on the {len(local_cpus)} GPU-local CPUs NVML reports"
-                                if local_cpus else "pinned without NUMA placement (NVML gave no CPU set)")}
+        e2e = e2e_timing(args, wl, plan, device, barrier, world, problems)
 
     # ---- production step (5 layers x 8 images x 13 groups, 520 problems): eager calls vs the CUDA graph
     production = None
     box_loss = None
+    configs = None
     if world == 1 and not args.no_production_step:
         production = production_step_timing(device, max(args.warmup, 3))
         box_loss = box_loss_timing(device, max(args.warmup, 3))
+    if world == 1 and not args.no_configs:
+        configs = config_table(device, args, flush, wl)
 
-    # ---- sharded sweep: ONE 1024-image batch split across the ranks + NCCL all-gather of the pairs
+    # ---- sharded sweep: ONE batch split across the ranks + NCCL all-gather of the pairs
     sharded_info = None
     if world > 1 or args.sharded:
-        sharded_info = run_sharded_sweep(args, world, rank, device, barrier)
+        sharded_info = [run_sharded_sweep(args, world, rank, device, barrier, images)
+                        for images in args.sharded_images]
 
     # ---- roofline of the cost kernel (HBM-bound) and the solver figures
     peak, peak_kind = peak_hbm()
@@ -440,12 +497,14 @@ def run_rfm(args) -> None:
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        threads = int(os.environ.get("LAP_THREADS", "8"))
-        r = cpu_path_rate(wl, args.cpu_images, args.cpu_seconds, threads)
-        cpu = {"value": r["value"], "unit": UNIT, "cores": max(threads, torch.get_num_threads()), "kind": "port",
-               "sample": (f"first {min(args.cpu_images, wl.images)} images of this workload "
-                          f"({r['problems_per_rep']} problems) x {r['reps']} reps in {r['seconds']:.1f} s: torch "
-                          f"CPU op chain ({torch.get_num_threads()} threads) + SciPy on a {threads}-thread pool")}
+        lap_threads, torch_threads = cpu_baseline_setting()
+        r = cpu_path_rate(wl, args.cpu_images, args.cpu_seconds, lap_threads, torch_threads)
+        cpu = {"value": r["value"], "unit": UNIT, "cores": lap_threads, "kind": "port",
+               "host_cpu_count": os.cpu_count(), "torch_threads": torch_threads,
+               "sample": (f"first {r['images']} images of this workload ({r['problems_per_rep']} problems) x "
+                          f"{r['reps']} reps in {r['seconds']:.1f} s: torch CPU op chain ({torch_threads} threads) "
+                          f"+ SciPy on a {lap_threads}-thread pool (every host thread this process may use; the "
+                          f"same setting as --impl reference)")}
 
     if rank == 0:
         line = {
@@ -454,13 +513,73 @@ def run_rfm(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "fp32 cost, fp64 LSAP duals", "data": "synthetic",
             "config": workload_config(wl), "roofline": roofline, "lsap": lsap, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches, "clocks": clocks, "impl": "rfm", "sharded_sweep": sharded_info,
-            "production_step": production, "box_loss": box_loss,
-            "library": _lib.version(), "step_ms": {"min": min(step_ms), "median": statistics.median(step_ms),
-                                                  "max": max(step_ms)},
+            "graph_replay": {"ms_per_step": graph_max_ms / args.steps,
+                             "problems_per_s": world * problems * args.steps / (graph_max_ms / 1e3),
+                             "what": "the same step through a captured MatchGraph (one host call per step)"},
+            "production_step": production, "box_loss": box_loss, "configs": configs,
+            "library": _lib.version(), "step_ms": step_stats(step_ms), "per_rank_step_ms": per_rank,
         }
         emit(line)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def e2e_timing(args, wl, plan, device, barrier, world: int, problems: int) -> dict:
+    """The headline metric end to end: every step copies its inputs from pinned host memory, matches
+    them and reads its packed pairs back, through ``PrefetchingMatcher`` (the upload of step k+1 on its
+    own stream while step k is matched)."""
+    # pinned buffers on the GPU's own NUMA node (the thread that pins them runs on that node's CPUs),
+    # so the uploads do not cross the inter-socket link; the affinity is restored after
+    saved_cpus = os.sched_getaffinity(0)
+    local_cpus = gpu_local_cpus(device)
+    if local_cpus:
+        os.sched_setaffinity(0, local_cpus)
+    h_logits = wl.pred_logits.pin_memory()
+    h_boxes = wl.pred_boxes.pin_memory()
+    h_labels = torch.cat([t["labels"] for t in wl.targets]).pin_memory()
+    h_tboxes = torch.cat([t["boxes"] for t in wl.targets]).pin_memory()
+    h_pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64).pin_memory()
+    h2d = sum(int(t.numel() * t.element_size()) for t in (h_logits, h_boxes, h_labels, h_tboxes))
+    d2h = int(h_pairs.numel() * h_pairs.element_size())
+    from rfdetr_training_throughput_b200.pipeline import PrefetchingMatcher
+
+    pm = PrefetchingMatcher(wl.group_detr, weights=wl.weights, device=device)
+    host_batch = (h_logits, h_boxes, h_labels, h_tboxes, tuple(wl.sizes))
+
+    def e2e_run(steps: int) -> None:
+        pm.copy_stream.wait_stream(torch.cuda.current_stream(device))
+        nxt = pm.prefetch(*host_batch)
+        for k in range(steps):
+            cur = nxt
+            if k + 1 < steps:
+                nxt = pm.prefetch(*host_batch)
+            res = pm.match(cur)
+            h_pairs.copy_(res.pairs, non_blocking=True)
+
+    e2e_run(max(args.warmup, 1))
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(device)
+    e0.record()
+    e2e_run(args.steps)
+    e1.record()
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    e2e_t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(e2e_t, op=torch.distributed.ReduceOp.MAX)
+    os.sched_setaffinity(0, saved_cpus)
+    ms_step = float(e2e_t.item()) / args.steps
+    return {"value": world * problems * args.steps / (float(e2e_t.item()) / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_step,
+            "h2d_gbs_per_gpu": h2d / (ms_step / 1e3) / 1e9,
+            "bound": ("host-to-device copy of the step's inputs (PCIe and host memory), not the kernels: the "
+                      "device-resident step takes a small fraction of this time"),
+            "path": "PrefetchingMatcher: pinned H2D of step k+1 on a copy stream overlapping match + D2H of step k",
+            "host_buffers": (f"pinned by a thread on the {len(local_cpus)} GPU-local CPUs NVML reports"
+                             if local_cpus else "pinned without NUMA placement (NVML gave no CPU set)")}
 
 
 def production_step_timing(device, warmup: int, steps: int = 200) -> dict:
@@ -561,14 +680,17 @@ def box_loss_timing(device, warmup: int, steps: int = 100) -> dict:
     return out
 
 
-def run_sharded_sweep(args, world: int, rank: int, device, barrier) -> dict:
-    """Strong scaling: the sweep's one 1024-image batch split by image over the ranks, every rank
-    matching its range, then one all-gather of the packed int64 pairs (NCCL over NVLink).  Timed
-    twice: through ``sharded_match`` (host planning work on every call) and through a
-    ``ShardedMatcher`` (this rank's step replayed as a CUDA graph into the gather's send buffer)."""
+def run_sharded_sweep(args, world: int, rank: int, device, barrier, images: int) -> dict:
+    """Strong scaling: one ``images``-image batch split by image over the ranks, every rank matching
+    its range, then one all-gather of the packed int64 pairs (NCCL over NVLink).  The headline figure
+    is a ``ShardedMatcher`` step: this rank's match replayed as a CUDA graph into the gather's send
+    buffer, then the all-gather, the result left in the gathered buffer (``GatheredPairs``: per-image
+    views at host-known offsets, no copy).  Beside it, each part timed alone (replay, all-gather,
+    the optional flat concatenation) and the eager ``sharded_match`` call.  Every figure is the max
+    over ranks of the mean device ms per step, L2 flushed between steps."""
     from rfdetr_training_throughput_b200 import sharded, workloads
 
-    wl = workloads.make(args.workload, images=args.images)  # the same batch on every rank
+    wl = workloads.make(args.workload, images=images)  # the same batch on every rank
     lo, hi = sharded.shard_bounds(wl.images, world)[rank]
     offs = np.concatenate([[0], np.cumsum(wl.sizes)])
     logits = wl.pred_logits[:, lo:hi].to(device)
@@ -576,49 +698,44 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier) -> dict:
     labels = torch.cat([t["labels"] for t in wl.targets])[offs[lo]:offs[hi]].to(device)
     tboxes = torch.cat([t["boxes"] for t in wl.targets])[offs[lo]:offs[hi]].to(device)
     sizes = tuple(wl.sizes)
-    steps = max(1, min(args.steps, 100))
+    steps = max(3, min(args.steps, 50))
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+
+    sm = sharded.ShardedMatcher(sizes, wl.layers, wl.queries, wl.classes, wl.group_detr, weights=wl.weights,
+                                device=device)
+    sm.graph.logits.copy_(logits)
+    sm.graph.boxes.copy_(boxes)
+    sm.graph.labels.copy_(labels)
+    sm.graph.tgt_boxes.copy_(tboxes)
+
+    def step():
+        sm.graph.replay()
+        return sm.gather(padded=True)
 
     def eager():
-        return sharded.sharded_match(logits, boxes, labels, tboxes, sizes, wl.group_detr, weights=wl.weights)[0]
+        return sharded.sharded_match(logits, boxes, labels, tboxes, sizes, wl.group_detr, weights=wl.weights,
+                                     padded=True)[0]
 
-    matcher_graph = sharded.ShardedMatcher(sizes, wl.layers, wl.queries, wl.classes, wl.group_detr,
-                                           weights=wl.weights, device=device)
-    matcher_graph.graph.logits.copy_(logits)
-    matcher_graph.graph.boxes.copy_(boxes)
-    matcher_graph.graph.labels.copy_(labels)
-    matcher_graph.graph.tgt_boxes.copy_(tboxes)
+    def mean_ms(fn) -> float:
+        return statistics.mean(time_device_steps(fn, steps, max(args.warmup, 2), flush, device, barrier))
 
-    def replayed():
-        matcher_graph.graph.replay()
-        return matcher_graph.gather()
-
-    def timed(fn) -> tuple[float, torch.Tensor]:
-        for _ in range(max(args.warmup, 1)):
-            out = fn()
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-        barrier()
-        torch.cuda.synchronize(device)
-        for k in range(steps):
-            starts[k].record()
-            out = fn()
-            ends[k].record()
-        torch.cuda.synchronize(device)
-        barrier()
-        ms = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], dtype=torch.float64, device=device)
-        if world > 1:
-            torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
-        return float(ms.item()) / steps, out
-
-    eager_ms, pairs = timed(eager)
-    graph_ms, pairs_g = timed(replayed)
-    same = bool(torch.equal(pairs, pairs_g))
-    del matcher_graph  # its graph holds no collective, but release it before the process group goes
+    parts = {"step": mean_ms(step), "replay": mean_ms(sm.graph.replay), "all_gather": mean_ms(lambda: sm.gather(True)),
+             "flat_concat": mean_ms(lambda: sm.gather(True).flat()), "eager_step": mean_ms(eager)}
+    same = bool(torch.equal(step().flat(), eager().flat()))
+    t = torch.tensor(list(parts.values()), dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = dict(zip(parts.keys(), t.tolist()))
+    gathered_pairs = int(sum(sm.shard.counts))
+    del sm  # its graph holds no collective, but release it before the process group goes
     return {"images": wl.images, "problems_per_step": wl.num_problems, "steps": steps,
-            "ms_per_step": graph_ms, "problems_per_s": wl.num_problems / (graph_ms / 1e3),
-            "eager_ms_per_step": eager_ms, "eager_problems_per_s": wl.num_problems / (eager_ms / 1e3),
-            "graph_equals_eager": same, "gathered_pairs": int(pairs.shape[1]), "scaling": "strong",
-            "collective": "all_gather_into_tensor of int64 [2, pairs] per rank" if world > 1 else "none (1 rank)"}
+            "ms_per_step": ms["step"], "problems_per_s": wl.num_problems / (ms["step"] / 1e3),
+            "breakdown_ms": {"replay": ms["replay"], "all_gather": ms["all_gather"],
+                             "all_gather_plus_flat_concat": ms["flat_concat"]},
+            "eager_ms_per_step": ms["eager_step"], "eager_problems_per_s": wl.num_problems / (ms["eager_step"] / 1e3),
+            "graph_equals_eager": same, "gathered_pairs": gathered_pairs, "scaling": "strong",
+            "result": "GatheredPairs (the all-gather's buffer, per-image views at host-known offsets)",
+            "collective": "all_gather_into_tensor of int64 [2, width] per rank" if world > 1 else "none (1 rank)"}
 
 
 _RESULT_FD: list = [None]

@@ -39,6 +39,14 @@
  *     device `status` array and are only visible after the stream completes.
  *   - Calls are thread-compatible: concurrent calls on different streams are
  *     safe as long as they write disjoint outputs.
+ *   - Per-context state is cached under the CUDA context's unique id: the
+ *     raised dynamic-shared-memory attribute of the solver kernels and the
+ *     device address of rfm_lsap_dense_noalloc's scratch.  A context that is
+ *     destroyed and recreated (cudaDeviceReset) gets both set up again on its
+ *     first call.  Occupancy figures are memoised per device.
+ *   - rfm_lsap reads its problem descriptors with ordinary stream ordering;
+ *     only inside rfm_match, after this library's own cost kernel, does the
+ *     solver start early (programmatic stream serialization).
  */
 #ifndef RFM_H_
 #define RFM_H_
@@ -242,8 +250,10 @@ int rfm_lsap_dense(const float* cost, int num_problems, int num_workers, int num
  *   - Returns RFM_ERR_UNSUPPORTED, without launching, when the batch needs more
  *     scratch than the built-in array (rfm_lsap_dense_workspace_bytes() >
  *     RFM_NOALLOC_SCRATCH_BYTES); use rfm_lsap_dense with a workspace then.
- *   - The first call on a device looks up the array's device address (once
- *     per device); make that first call before any stream capture.
+ *   - The first call in a CUDA context looks up the array's device address
+ *     (once per device while its primary context lives, again after the
+ *     context is destroyed and recreated); make that first call before any
+ *     stream capture.
  *   - All calls share the array: calls whose GPU work overlaps (e.g. on two
  *     streams at once) race on it.  Nothing in it needs clearing between calls.
  */

@@ -72,17 +72,22 @@ def compact_cost(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets, w
 
 
 class CpuMatcher:
-    """torch-CPU cost chain + SciPy per (image, group) block on a thread pool."""
+    """torch-CPU cost chain + SciPy per (image, group) block on a thread pool.
+
+    ``threads=1`` is the serial path: every block solved in turn in the calling
+    thread, as the parallel_lap patch does below its pool threshold
+    (patches.py:207-211) and as the unpatched matcher does always."""
 
     def __init__(self, threads: int | None = None):
         from scipy.optimize import linear_sum_assignment
 
         self._solve = linear_sum_assignment
         self.threads = int(threads or os.environ.get("LAP_THREADS", "8"))
-        self.pool = ThreadPoolExecutor(max_workers=self.threads, thread_name_prefix="lap")
+        self.pool = ThreadPoolExecutor(max_workers=self.threads, thread_name_prefix="lap") if self.threads > 1 else None
 
     def close(self) -> None:
-        self.pool.shutdown(wait=True)
+        if self.pool is not None:
+            self.pool.shutdown(wait=True)
 
     def match(self, pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets, group_detr: int,
               weights: dict):
@@ -97,7 +102,7 @@ class CpuMatcher:
                     blocks.append(cost[l, g * qg:(g + 1) * qg, col:col + t])
                     keys.append((l, b, g))
                 col += t
-        if len(blocks) < MIN_POOL_BATCH:
+        if self.pool is None or len(blocks) < MIN_POOL_BATCH:
             solved = list(map(self._solve, blocks))
         else:
             solved = list(self.pool.map(self._solve, blocks))

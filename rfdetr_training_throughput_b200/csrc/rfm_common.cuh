@@ -35,6 +35,15 @@ int cost_run(const float* pred_logits, const float* pred_boxes, const int64_t* t
              float cost_class, float cost_bbox, float cost_giou, float focal_alpha, float* out,
              int* reset_word, void* stream);
 
+// Unique id of the CUDA context current on the calling thread (the runtime's
+// primary context of the current device once the runtime has initialised it),
+// or 0 when no context is current or the driver cannot say.  Ids are never
+// reused within a process, so state that belongs to one context (a kernel
+// attribute, the device address of a module variable) is cached under this id
+// and is looked up afresh after the context is destroyed and recreated
+// (cudaDeviceReset).
+unsigned long long current_context_id();
+
 // SMs of the current device (1 if the runtime cannot say).
 inline int device_sm_count() {
   int dev = 0, n = 0;

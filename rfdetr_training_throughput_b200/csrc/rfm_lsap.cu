@@ -766,11 +766,14 @@ const void* pair_kernel(int cols_per_lane, int variant) {
   }
 }
 
-// Opts a kernel into `smem` bytes of dynamic shared memory once per device (the
-// attribute is then left raised): repeated launches, including launches being
-// captured into a CUDA graph, make no attribute call.
+// Opts a kernel into `smem` bytes of dynamic shared memory once per context
+// (the attribute is then left raised): repeated launches, including launches
+// being captured into a CUDA graph, make no attribute call.  The attribute
+// belongs to the context's copy of the module, so it is cached under the
+// context's id: after the context is destroyed and recreated the attribute is
+// set again.
 struct SmemAttribute {
-  int device;
+  unsigned long long context;
   const void* fn;
   int64_t smem;
 };
@@ -779,25 +782,28 @@ std::vector<SmemAttribute> g_smem_attributes;
 
 bool ensure_dynamic_smem(const void* fn, int64_t smem) {
   if (smem <= 48 * 1024) return true;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
   std::lock_guard<std::mutex> lock(g_smem_mutex);
-  for (SmemAttribute& e : g_smem_attributes) {
-    if (e.device == dev && e.fn == fn) {
-      if (e.smem >= smem) return true;
-      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-          cudaSuccess) {
-        return false;
-      }
-      e.smem = smem;
-      return true;
+  const unsigned long long ctx = current_context_id();
+  if (ctx != 0) {
+    for (const SmemAttribute& e : g_smem_attributes) {
+      if (e.context == ctx && e.fn == fn && e.smem >= smem) return true;
     }
   }
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess) {
     return false;
   }
-  g_smem_attributes.push_back({dev, fn, smem});
+  // the call above made the primary context current if it was not yet
+  const unsigned long long now = ctx != 0 ? ctx : current_context_id();
+  if (now != 0) {
+    for (SmemAttribute& e : g_smem_attributes) {
+      if (e.context == now && e.fn == fn) {
+        e.smem = smem;
+        return true;
+      }
+    }
+    g_smem_attributes.push_back({now, fn, smem});
+  }
   return true;
 }
 
@@ -820,6 +826,8 @@ int query_resident_ctas(int cols_per_lane, int variant, int64_t smem) {
 
 // query_resident_ctas() memoised per (device, kernel, shared memory): the
 // occupancy query and the attribute call cost a few microseconds per launch.
+// Occupancy is a property of the device and the kernel, so the memo stays
+// valid across contexts; the launch itself raises the attribute per context.
 struct OccupancyEntry {
   int device, cols_per_lane;
   int variant;
@@ -869,10 +877,13 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
   if (!ensure_dynamic_smem(fn, smem)) return launch_status();
   const dim3 grid(static_cast<unsigned>(num_ctas));
   const dim3 block(32 * warps_per_cta);
-  if (!kDense && kVariant != kVarEarly && cols_per_lane <= 10 && (kVariant == kVarCoop || after_kernel)) {
-    // programmatic stream serialization: the CTAs may launch while the kernel
-    // before this one (the cost kernel) finishes; they wait for it
-    // (griddepcontrol.wait) before reading the matrix or the counter
+  if (!kDense && kVariant != kVarEarly && cols_per_lane <= 10 && after_kernel) {
+    // programmatic stream serialization, only right after this library's cost
+    // kernel (rfm_match): the CTAs may launch while it finishes and wait for it
+    // (griddepcontrol.wait) before reading the matrix or the counter.  They
+    // read their descriptor before that wait, which is safe because the cost
+    // kernel does not write descriptors; after a caller's kernel (standalone
+    // rfm_lsap) the launch is an ordinary stream-ordered one.
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -1086,7 +1097,7 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
     if (coop_ctas > 0 && static_cast<int64_t>(plan->num_problems) <= static_cast<int64_t>(coop_ctas) * sms) {
       a.slot = static_cast<int>(coop_smem);
       return launch<false, kVarCoop>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, coop_smem,
-                                     stream);
+                                     stream, counter_zeroed);
     }
   }
   const int64_t smem = wide ? kMaxWarpsPerCta * fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows, true)
@@ -1229,8 +1240,11 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
 // with the framework's caching pool is not acceptable.  For them the scratch
 // lives in a file-scope __device__ array of RFM_NOALLOC_SCRATCH_BYTES that is
 // part of this module, so every GPU that loads the library holds it until the
-// process exits.  Host code only ever uses its device address, fetched once
-// per device with cudaGetSymbolAddress on the first call made on that device.
+// process exits.  Host code only ever uses its device address, fetched with
+// cudaGetSymbolAddress on the first call made in a CUDA context (once per
+// device while its primary context lives) and cached under the context's id:
+// a context destroyed and recreated (cudaDeviceReset) reloads the module,
+// possibly at another address, and the next call looks it up again.
 //
 // The solver writes every scratch element before reading it, so nothing has to
 // be cleared between calls.  All calls share this one buffer: calls whose work
@@ -1238,31 +1252,44 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
 static __device__ __align__(256) float g_noalloc_scratch[RFM_NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
 namespace {
-constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocAddress {
+  unsigned long long context;
+  void* address;
+};
+constexpr size_t kNoAllocCacheEntries = 64;
 std::mutex g_noalloc_mutex;
-void* g_noalloc_address[kNoAllocMaxDevices] = {};
+std::vector<NoAllocAddress> g_noalloc_addresses;
 
-// Device address of the built-in scratch on the current device (set up once).
+// Device address of the built-in scratch in the current context.
 int noalloc_scratch_address(void** out) {
   int dev = 0;
-  const cudaError_t e0 = cudaGetDevice(&dev);
-  if (e0 != cudaSuccess) {
+  if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
     return RFM_ERR_NO_DEVICE;
   }
-  if (dev < 0 || dev >= kNoAllocMaxDevices) return RFM_ERR_UNSUPPORTED;
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_address[dev] == nullptr) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      cudaGetLastError();
-      return (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) ? RFM_ERR_NO_DEVICE
-                                                                          : RFM_ERR_LAUNCH;
+  const unsigned long long ctx = rfm::current_context_id();
+  if (ctx != 0) {
+    for (const NoAllocAddress& e : g_noalloc_addresses) {
+      if (e.context == ctx) {
+        *out = e.address;
+        return RFM_OK;
+      }
     }
-    g_noalloc_address[dev] = p;
   }
-  *out = g_noalloc_address[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    cudaGetLastError();
+    return (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) ? RFM_ERR_NO_DEVICE : RFM_ERR_LAUNCH;
+  }
+  // the lookup made the primary context current if it was not yet
+  const unsigned long long now = ctx != 0 ? ctx : rfm::current_context_id();
+  if (now != 0) {
+    if (g_noalloc_addresses.size() >= kNoAllocCacheEntries) g_noalloc_addresses.erase(g_noalloc_addresses.begin());
+    g_noalloc_addresses.push_back({now, p});
+  }
+  *out = p;
   return RFM_OK;
 }
 }  // namespace

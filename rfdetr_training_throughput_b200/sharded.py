@@ -7,7 +7,10 @@ the packed int64 pairs of all ranks are then gathered with one
 ``all_gather_into_tensor`` (NCCL over NVLink on GPUs, gloo in the CPU tests), so
 every rank ends with the whole batch's per-image ``(query_idx, target_idx)``.
 Sizes are known on every host, so the gather needs no count exchange: each
-rank's chunk is padded to the largest rank's pair count.
+rank's chunk is padded to the largest rank's pair count.  With ``padded=True``
+the result is the gathered buffer itself (``GatheredPairs``: per-image views at
+host-known offsets, no copy); otherwise the padding is squeezed out with one
+concatenation into a flat ``[2, total]`` tensor.
 """
 
 from __future__ import annotations
@@ -48,11 +51,13 @@ class _Shard:
     def __init__(self, sizes: tuple[int, ...], layers: int, queries: int, group_detr: int, world: int, rank: int):
         self.bounds = shard_bounds(len(sizes), world)
         offsets = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
-        self.counts, self.per = [], []
+        self.counts, self.per, self.per_rank = [], [], []
         for a, b in self.bounds:
             pi = pairs_per_image(sizes[a:b], layers, queries, group_detr)
             self.counts.append(int(pi.sum()))
-            self.per.extend(int(x) for x in pi)
+            self.per_rank.append(tuple(int(x) for x in pi))
+            self.per.extend(self.per_rank[-1])
+        self.layers = layers
         self.lo, self.hi = self.bounds[rank]
         self.t_lo, self.t_hi = int(offsets[self.lo]), int(offsets[self.hi])
         self.local_sizes = tuple(sizes[self.lo:self.hi])
@@ -92,6 +97,45 @@ def _unpad(recv: torch.Tensor, counts: Sequence[int]) -> torch.Tensor:
     return torch.cat([recv[r, :, : int(counts[r])] for r in range(recv.shape[0])], dim=1)
 
 
+class GatheredPairs:
+    """Every rank's pairs as the all-gather left them, with no copy.
+
+    ``recv`` is ``[world, 2, width]`` int64: rank ``r``'s pairs are ``recv[r, :, :counts[r]]``, in
+    its (layer, image) order (layer-major, images in order), the rest of the row is padding that
+    is never read.  All offsets are host-known, so views need no synchronisation: ``layer(l)``
+    gives rf-detr's per-image ``(query_idx, target_idx)`` list for the whole batch, ``rank_pairs(r)``
+    one rank's ``[2, counts[r]]`` block, and ``flat()`` the ``[2, total]`` concatenation (one copy).
+    The buffer is reused by the next gather of the same matcher.
+    """
+
+    def __init__(self, recv: torch.Tensor, counts: Sequence[int], per_rank: Sequence[tuple[int, ...]], layers: int):
+        self.recv = recv
+        self.counts = list(counts)
+        self.per_rank = list(per_rank)
+        self.layers = layers
+        self._views: list | None = None
+
+    def rank_pairs(self, r: int) -> torch.Tensor:
+        return self.recv[r, :, : self.counts[r]]
+
+    def flat(self) -> torch.Tensor:
+        return _unpad(self.recv, self.counts)
+
+    def _split(self):
+        if self._views is None:
+            self._views = [(torch.split(self.recv[r, 0, : self.counts[r]], self.per_rank[r]),
+                            torch.split(self.recv[r, 1, : self.counts[r]], self.per_rank[r]))
+                           for r in range(len(self.counts))]
+        return self._views
+
+    def layer(self, l: int) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        out = []
+        for r, (qs, ts) in enumerate(self._split()):
+            n = len(self.per_rank[r]) // self.layers  # images of rank r
+            out.extend(zip(qs[l * n:(l + 1) * n], ts[l * n:(l + 1) * n]))
+        return out
+
+
 def gather_pairs(local_pairs: torch.Tensor, counts: Sequence[int], group=None) -> torch.Tensor:
     """All-gather ``[2, counts[rank]]`` int64 chunks; returns ``[2, sum(counts)]`` in rank order.
     Chunks are padded to the largest count; the padding is never read."""
@@ -109,15 +153,16 @@ def gather_pairs(local_pairs: torch.Tensor, counts: Sequence[int], group=None) -
 
 def sharded_match(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: torch.Tensor,
                   boxes: torch.Tensor, sizes: Sequence[int], group_detr: int, *,
-                  weights: dict | None = None, group=None,
-                  local_solver: Callable | None = None) -> tuple[torch.Tensor, list[int]]:
+                  weights: dict | None = None, group=None, padded: bool = False,
+                  local_solver: Callable | None = None) -> tuple[torch.Tensor | GatheredPairs, list[int]]:
     """Match a batch split by image across the ranks of ``group``.
 
     ``pred_logits`` ``[L, B, Q, C]`` / ``pred_boxes`` ``[L, B, Q, 4]`` and the packed
     ``labels``/``boxes`` may hold the whole batch or only this rank's image range
     (detected from the leading image dimension).  Returns the gathered ``[2, total]``
-    pairs (per rank, layer-major, images in order) and the per-(layer, image) pair
-    counts in the same order.  ``local_solver(logits, boxes, labels, boxes, sizes,
+    pairs (per rank, layer-major, images in order; with ``padded`` the
+    ``GatheredPairs`` buffer itself) and the per-(layer, image) pair counts in the
+    same order.  ``local_solver(logits, boxes, labels, boxes, sizes,
     group_detr) -> [2, n]`` replaces the device step (used by CPU tests).
     """
     world = dist.get_world_size(group)
@@ -142,15 +187,27 @@ def sharded_match(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: t
         targets = PackedTargets.from_checked_sizes(labels, boxes, sh.local_sizes, sh.t_hi - sh.t_lo)
         match_packed(pred_logits, pred_boxes, targets, group_detr, weights=weights, out=send[0, :, :n])
         dist.all_gather_into_tensor(recv, send, group=group)
+        if padded:
+            return GatheredPairs(recv, sh.counts, sh.per_rank, layers), sh.per
         return _unpad(recv, sh.counts), sh.per
     local = local_solver(pred_logits, pred_boxes, labels, boxes, list(sh.local_sizes), group_detr)
-    return gather_pairs(local, sh.counts, group), sh.per
+    flat = gather_pairs(local, sh.counts, group)
+    if padded:
+        width = max(sh.counts) if sh.counts else 0
+        recv = flat.new_zeros((world, 2, width))
+        start = 0
+        for r, c in enumerate(sh.counts):
+            recv[r, :, :c] = flat[:, start:start + c]
+            start += c
+        return GatheredPairs(recv, sh.counts, sh.per_rank, layers), sh.per
+    return flat, sh.per
 
 
 class ShardedMatcher:
     """``sharded_match`` for a batch shape that repeats: this rank's step is a captured
     ``MatchGraph`` writing straight into the all-gather's send buffer, so a call is one graph
-    replay, one ``all_gather_into_tensor`` and one concatenation.  Inputs are this rank's
+    replay and one ``all_gather_into_tensor`` (plus one concatenation unless the caller takes the
+    padded ``GatheredPairs``).  Inputs are this rank's
     image range (``pred_logits`` ``[L, hi - lo, Q, C]`` etc.); construct it on every rank of
     ``group`` with the same arguments."""
 
@@ -171,12 +228,15 @@ class ShardedMatcher:
         self.bounds = (self.shard.lo, self.shard.hi)
         self.per_image = self.shard.per
 
-    def gather(self) -> torch.Tensor:
-        """All-gather the pairs the last replay wrote; ``[2, total]`` in rank order."""
+    def gather(self, padded: bool = False) -> torch.Tensor | GatheredPairs:
+        """All-gather the pairs the last replay wrote: ``[2, total]`` in rank order, or with
+        ``padded`` the gathered buffer itself (no concatenation)."""
         dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+        if padded:
+            return GatheredPairs(self.recv, self.shard.counts, self.shard.per_rank, self.shard.layers)
         return _unpad(self.recv, self.shard.counts)
 
     def __call__(self, pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: torch.Tensor,
-                 tgt_boxes: torch.Tensor) -> torch.Tensor:
+                 tgt_boxes: torch.Tensor, padded: bool = False) -> torch.Tensor | GatheredPairs:
         self.graph(pred_logits, pred_boxes, labels, tgt_boxes)
-        return self.gather()
+        return self.gather(padded)

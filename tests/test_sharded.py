@@ -52,8 +52,14 @@ def _worker(rank, world, port, result_path):
         boxes = torch.cat([t["boxes"] for t in wl.targets])
         pairs, per = sharded.sharded_match(wl.pred_logits, wl.pred_boxes, labels, boxes, wl.sizes, wl.group_detr,
                                            local_solver=_cpu_solver)
+        gathered, per2 = sharded.sharded_match(wl.pred_logits, wl.pred_boxes, labels, boxes, wl.sizes,
+                                               wl.group_detr, local_solver=_cpu_solver, padded=True)
+        # the padded result holds the same pairs: flat() and the per-image views of every layer
+        flat = gathered.flat()
+        views = [torch.cat([torch.stack([q, t]) for q, t in gathered.layer(l)], dim=1) for l in range(wl.layers)]
         if rank == 0:
-            np.savez(result_path, pairs=pairs.numpy(), per=np.asarray(per))
+            np.savez(result_path, pairs=pairs.numpy(), per=np.asarray(per), flat=flat.numpy(),
+                     per2=np.asarray(per2), views=[v.numpy() for v in views])
     finally:
         dist.destroy_process_group()
 
@@ -81,3 +87,19 @@ def test_sharded_match_on_two_gloo_ranks(tmp_path):
     expect = np.concatenate(expect, axis=1)
     assert np.array_equal(got["pairs"], expect)
     assert int(got["per"].sum()) == expect.shape[1]
+    assert np.array_equal(got["flat"], expect) and np.array_equal(got["per2"], got["per"])
+    # per-layer views: every rank's block of that layer, ranks in order (images in batch order)
+    per = [int(c) for c in got["per"]]
+    first_pair, first_count = 0, 0
+    rank_blocks = []  # (pairs of the rank, its per-(layer, image) counts)
+    for a, b in bounds:
+        counts = per[first_count:first_count + (b - a) * wl.layers]
+        rank_blocks.append((expect[:, first_pair:first_pair + sum(counts)], counts, b - a))
+        first_pair += sum(counts)
+        first_count += len(counts)
+    for l in range(wl.layers):
+        pieces = []
+        for pairs_r, counts, n in rank_blocks:
+            off = sum(counts[: l * n])
+            pieces.append(pairs_r[:, off:off + sum(counts[l * n:(l + 1) * n])])
+        assert np.array_equal(got["views"][l], np.concatenate(pieces, axis=1)), l

@@ -313,7 +313,28 @@ def run_reference(args) -> None:
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     line["config"]["cpu_sample"] = {"images": images}
+    line["reference_gpu_lsap"] = reference_gpu_lsap()
+    line["reference_gpu_cost"] = {"unavailable": (
+        "the reference's cost kernel is Triton source JIT-compiled from the reference tree at run time "
+        "(kernels_matcher.py:179-234); that tree is not on the GPU box and its sources are not copied here")}
     emit(line)
+
+
+def reference_gpu_lsap() -> dict:
+    """The reference's own GPU solver (lsap_kernel / batch_lap_cuda, kernels_lap.py:69-305, built from
+    its source by oracle/build_ref.py) on the batches ``lsap_batches_rfm`` gives the repository's
+    solver: the same B200, the same inputs."""
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    from oracle import build_ref
+
+    mod = build_ref.load()
+    if mod is None:
+        return {"unavailable": "oracle/_ref holds no build of the reference solver (python -m oracle.build_ref)"}
+    device = torch.device("cuda", 0)
+    return {f"T{t}": time_solver(mod.batch_lap_cuda, lsap_batch(t, device), device) for t in LSAP_BATCH_TASKS} | {
+        "unit": "ms per 520-problem batch", "batches": "520 x [300 x T] uniform costs, seed 5000 + T",
+        "solver": "reference lsap_kernel (fp32 --use_fast_math, one 256-thread block per problem)"}
 
 
 # --------------------------------------------------------------------------- GPU path
@@ -463,11 +484,15 @@ def run_rfm(args) -> None:
     production = None
     box_loss = None
     configs = None
+    label_loss = None
     if world == 1 and not args.no_production_step:
         production = production_step_timing(device, max(args.warmup, 3))
         box_loss = box_loss_timing(device, max(args.warmup, 3))
+        label_loss = label_loss_timing(device, max(args.warmup, 3), wl, logits, boxes, packed)
+    lsap_batches = None
     if world == 1 and not args.no_configs:
         configs = config_table(device, args, flush, wl)
+        lsap_batches = lsap_batches_rfm(device)
 
     # ---- sharded sweep: ONE batch split across the ranks + NCCL all-gather of the pairs
     sharded_info = None
@@ -516,7 +541,8 @@ def run_rfm(args) -> None:
             "graph_replay": {"ms_per_step": graph_max_ms / args.steps,
                              "problems_per_s": world * problems * args.steps / (graph_max_ms / 1e3),
                              "what": "the same step through a captured MatchGraph (one host call per step)"},
-            "production_step": production, "box_loss": box_loss, "configs": configs,
+            "production_step": production, "box_loss": box_loss, "label_loss": label_loss, "configs": configs,
+            "lsap_batches": lsap_batches,
             "library": _lib.version(), "step_ms": step_stats(step_ms), "per_rank_step_ms": per_rank,
         }
         emit(line)
@@ -678,6 +704,171 @@ def box_loss_timing(device, warmup: int, steps: int = 100) -> dict:
         torch.cuda.synchronize(device)
         out[f"{name}_fwd_bwd_us"] = e0.elapsed_time(e1) * 1e3 / steps
     return out
+
+
+def label_loss_timing(device, warmup: int, sweep_wl, sweep_logits, sweep_boxes, sweep_packed,
+                      steps: int = 50) -> dict:
+    """The criterion's classification loss (IoU-aware BCE, RF-DETR's default) over the matched pairs,
+    forward + backward: ``matched_label_losses`` (two kernels over the logits, positives read from
+    the packed pairs) against the torch-op formulation of the same loss (index gathers, a dense
+    weight tensor, index_put of the positives), both on the GPU, on the production step; and the
+    kernels alone on the sweep's logits with their HBM figure (forward reads the logits, backward
+    reads them and writes the gradient)."""
+    import torch.nn.functional as F
+
+    from rfdetr_training_throughput_b200 import matcher, workloads
+    from rfdetr_training_throughput_b200.loss import matched_label_losses
+
+    wl = workloads.make("step")
+    packed = matcher.PackedTargets.from_list(wl.targets_on(device), device)
+    logits0, boxes0 = wl.pred_logits.to(device), wl.pred_boxes.to(device)
+    res = matcher.match_packed(logits0, boxes0, packed, wl.group_detr, weights=wl.weights)
+    tl = [t["labels"] for t in wl.targets_on(device)]
+    tb = [t["boxes"] for t in wl.targets_on(device)]
+    per_layer = [res.layer(l) for l in range(wl.layers)]
+    bidx = [torch.cat([torch.full_like(q, b) for b, (q, _t) in enumerate(p)]) for p in per_layer]
+    qidx = [torch.cat([q for q, _t in p]) for p in per_layer]
+    cls = [torch.cat([tl[b][t] for b, (_q, t) in enumerate(p)]) for p in per_layer]
+    tgt = [torch.cat([tb[b][t] for b, (_q, t) in enumerate(p)]) for p in per_layer]
+
+    def xyxy(b):
+        cx, cy, w, h = b.unbind(-1)
+        return torch.stack([cx - 0.5 * w, cy - 0.5 * h, cx + 0.5 * w, cy + 0.5 * h], dim=-1)
+
+    def torch_ops():
+        x = logits0.detach().requires_grad_(True)
+        total = 0.0
+        for l in range(wl.layers):
+            src = x[l]
+            a, b = xyxy(boxes0[l][bidx[l], qidx[l]]), xyxy(tgt[l])
+            wh = (torch.min(a[:, 2:], b[:, 2:]) - torch.max(a[:, :2], b[:, :2])).clamp(min=0)
+            inter = wh[:, 0] * wh[:, 1]
+            area = lambda z: (z[:, 2] - z[:, 0]) * (z[:, 3] - z[:, 1])  # noqa: E731
+            iou = inter / (area(a) + area(b) - inter)
+            prob = src.sigmoid()
+            pos_w = torch.zeros_like(src)
+            neg_w = prob ** 2
+            t = (prob[bidx[l], qidx[l], cls[l]].pow(0.25) * iou.pow(0.75)).clamp(min=0.01).detach()
+            pos_w[bidx[l], qidx[l], cls[l]] = t
+            neg_w[bidx[l], qidx[l], cls[l]] = 1 - t
+            total = total + (neg_w * src - F.logsigmoid(src) * (pos_w + neg_w)).sum()
+        total.backward()
+
+    def fused():
+        x = logits0.detach().requires_grad_(True)
+        loss, _correct = matched_label_losses(x, boxes0, packed, res, mode="ia_bce")
+        loss.sum().backward()
+
+    out = {"workload": "step matched pairs: 5 layers x 8 images x 13 groups, 2 classes", "mode": "ia_bce",
+           "pairs": int(res.pairs.shape[1]), "steps": steps}
+    for name, fn in (("rfm", fused), ("torch_ops", torch_ops)):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        out[f"{name}_fwd_bwd_us"] = e0.elapsed_time(e1) * 1e3 / steps
+
+    # the two kernels alone on the sweep's logits (C-ABI calls back to back between events on the
+    # launching stream, behind a device-side delay): forward reads the logits, backward reads them
+    # and writes the gradient
+    import ctypes
+
+    from rfdetr_training_throughput_b200 import _lib
+    from rfdetr_training_throughput_b200.loss import LABEL_LOSS_MODES, _offsets_on
+
+    sres = matcher.match_packed(sweep_logits, sweep_boxes, sweep_packed, sweep_wl.group_detr, weights=sweep_wl.weights)
+    L, B, Q, C = sweep_logits.shape
+    lib = _lib.load()
+    nparts = int(lib.rfm_label_loss_parts(L, B, Q, C))
+    parts = torch.empty(nparts, dtype=torch.float32, device=device)
+    correct = torch.empty(nparts, dtype=torch.int32, device=device)
+    grad = torch.empty_like(sweep_logits)
+    gl = torch.ones(L, dtype=torch.float32, device=device)
+    P = ctypes.c_void_p
+    toff = _offsets_on(sweep_packed.sizes, str(device))
+    poff = _offsets_on(sres.per_image_key, str(device))
+    common = [P(sweep_logits.data_ptr()), P(sweep_boxes.data_ptr()), P(sweep_packed.labels.data_ptr()),
+              P(sweep_packed.boxes.data_ptr()), P(toff.data_ptr()), P(sres.pairs[0].data_ptr()),
+              P(sres.pairs[1].data_ptr()), P(poff.data_ptr()), L, B, Q, C, sweep_packed.total,
+              LABEL_LOSS_MODES["ia_bce"], 0.25]
+    stream = P(torch.cuda.current_stream(device).cuda_stream)
+
+    def fwd():
+        _lib.check("rfm_label_loss_forward", lib.rfm_label_loss_forward(*common, P(parts.data_ptr()),
+                                                                        P(correct.data_ptr()), stream))
+
+    def bwd():
+        _lib.check("rfm_label_loss_backward", lib.rfm_label_loss_backward(*common, P(gl.data_ptr()),
+                                                                          P(grad.data_ptr()), stream))
+
+    def per_launch_us(fn, rep: int = 20) -> float:
+        samples = []
+        for _ in range(7):
+            fn()
+            torch.cuda.synchronize(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda._sleep(LEAD_CYCLES)
+            e0.record()
+            for _ in range(rep):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            samples.append(e0.elapsed_time(e1) * 1e3 / rep)
+        return statistics.median(samples)
+
+    f_us, b_us = per_launch_us(fwd), per_launch_us(bwd)
+    nbytes = sweep_logits.numel() * 4
+    peak, _kind = peak_hbm()
+    out["sweep"] = {"workload": "sweep logits [1, 1024, 3900, 2] and its 106k matched pairs", "logits_mb": nbytes / 1e6,
+                    "forward_us": f_us, "backward_us": b_us, "forward_gbs": nbytes / f_us / 1e3,
+                    "backward_gbs": 2 * nbytes / b_us / 1e3, "forward_frac_of_hbm": nbytes / f_us / 1e3 / peak,
+                    "backward_frac_of_hbm": 2 * nbytes / b_us / 1e3 / peak,
+                    "bytes": "forward reads the logits once; backward reads them and writes the gradient"}
+    return out
+
+
+#: The reference's own solver benchmark batches: 520 problems of [300 workers x T tasks] uniform
+#: costs (the production step's problem count, kernels_lap.py:50-51,440-473), T across the range
+#: it reports, up to its 256-task bound.
+LSAP_BATCH_TASKS = (12, 37, 60, 108, 219, 256)
+
+
+def lsap_batch(tasks: int, device) -> torch.Tensor:
+    g = torch.Generator().manual_seed(5000 + tasks)
+    return torch.rand((520, 300, tasks), generator=g, dtype=torch.float32).to(device)
+
+
+def time_solver(fn, cost: torch.Tensor, device, rep: int = 5) -> float:
+    """Median ms of one call (2 warm-up calls, then rep calls each between events, behind a delay)."""
+    for _ in range(2):
+        fn(cost)
+    torch.cuda.synchronize(device)
+    ms = []
+    for _ in range(rep):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(LEAD_CYCLES // 4)
+        e0.record()
+        fn(cost)
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms.append(e0.elapsed_time(e1))
+    return statistics.median(ms)
+
+
+def lsap_batches_rfm(device) -> dict:
+    """``batch_linear_assignment`` (the torch_linear_assignment contract behind the cuda_lap patch,
+    rfm_lsap_dense) on the reference's solver benchmark batches; the reference arm times the
+    reference's own solver on the same batches."""
+    from rfdetr_training_throughput_b200 import matcher
+
+    return {f"T{t}": time_solver(matcher.batch_linear_assignment, lsap_batch(t, device), device)
+            for t in LSAP_BATCH_TASKS} | {"unit": "ms per 520-problem batch",
+                                          "batches": "520 x [300 x T] uniform costs, seed 5000 + T"}
 
 
 def run_sharded_sweep(args, world: int, rank: int, device, barrier, images: int) -> dict:

@@ -296,6 +296,54 @@ int rfm_box_loss_backward(const float* pred_boxes, const float* tgt_boxes, const
                           int num_layers, int num_images, int num_queries, int sum_targets,
                           const float* grad_l1, const float* grad_giou, float* grad_pred, void* stream);
 
+/*
+ * Classification loss of the DETR-family criterion (SetCriterion.loss_labels,
+ * the criterion's other consumer of the matcher's indices: the target-class
+ * scatter at criterion.py:562 as cited at patches.py:339-341), evaluated over
+ * every logit with the matched (query, class) slots as positives, read from the
+ * packed pairs rfm_lsap writes (same pair layout as rfm_box_loss_forward).
+ * For every logit x = pred_logits[l, b, q, c], p = sigmoid(x), softplus(x) =
+ * log(1 + exp(x)), and y = 1 exactly when query q of (l, b) is matched to a
+ * target whose label is c:
+ *
+ *   RFM_LABEL_LOSS_FOCAL   sigmoid focal loss, gamma 2 (Deformable DETR):
+ *       y = 1: alpha (1-p)^2 softplus(-x)     y = 0: (1-alpha) p^2 softplus(x)
+ *   RFM_LABEL_LOSS_IA_BCE  IoU-aware BCE (LW-DETR, RF-DETR's criterion): with
+ *       u = IoU(pred_boxes[l,b,q], its target box) (inter / union, unclamped)
+ *       and t = max(p^alpha u^(1-alpha), 0.01) held constant:
+ *       y = 1: (1-t) x + softplus(-x)          y = 0: p^2 softplus(x)
+ *
+ * loss_part receives rfm_label_loss_parts(L, B, Q, C) partial sums, (l, b)
+ * major, each over a tile of about RFM_LABEL_LOSS_PART_ELEMS logits (a multiple
+ * of 32 queries, 64 to 4096), each reduced in a fixed order; the caller
+ * sums the parts of layer l (l * B * tiles .. (l+1) * B * tiles) and divides by
+ * num_boxes.  correct_part (optional) counts matched queries whose largest
+ * logit (smallest index among equal maxima) is their target's class, for the
+ * criterion's class_error.  Matched labels outside [0, C) make no positive;
+ * a query appears in at most one pair per (layer, image), as the matcher's
+ * pairs guarantee.
+ * A matched pair whose boxes both have zero area has IoU 0/0 = NaN, and the
+ * IoU-aware loss is then NaN, as the unfused formula gives (clamp keeps NaN).
+ * pred_boxes and tgt_boxes are read by the IoU-aware loss only (16-byte
+ * aligned).  rfm_label_loss_backward writes grad_loss[l] * d(loss)/dx into
+ * every element of grad_logits [L, B, Q, C] (torch's autograd of the same
+ * expressions, t constant).  No counterpart kernel in the reference.
+ */
+#define RFM_LABEL_LOSS_FOCAL 0
+#define RFM_LABEL_LOSS_IA_BCE 1
+#define RFM_LABEL_LOSS_PART_ELEMS 8192
+int64_t rfm_label_loss_parts(int num_layers, int num_images, int num_queries, int num_classes);
+int rfm_label_loss_forward(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+                           const float* tgt_boxes, const int32_t* tgt_offsets, const int64_t* query_idx,
+                           const int64_t* target_idx, const int32_t* pair_offsets, int num_layers,
+                           int num_images, int num_queries, int num_classes, int sum_targets, int mode,
+                           float focal_alpha, float* loss_part, int32_t* correct_part, void* stream);
+int rfm_label_loss_backward(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+                            const float* tgt_boxes, const int32_t* tgt_offsets, const int64_t* query_idx,
+                            const int64_t* target_idx, const int32_t* pair_offsets, int num_layers,
+                            int num_images, int num_queries, int num_classes, int sum_targets, int mode,
+                            float focal_alpha, const float* grad_loss, float* grad_logits, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

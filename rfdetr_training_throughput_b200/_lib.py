@@ -41,6 +41,9 @@ EXPORTS = (
     "rfm_lsap_dense_noalloc",
     "rfm_box_loss_forward",
     "rfm_box_loss_backward",
+    "rfm_label_loss_parts",
+    "rfm_label_loss_forward",
+    "rfm_label_loss_backward",
 )
 
 #: Size of the built-in scratch of rfm_lsap_dense_noalloc (RFM_NOALLOC_SCRATCH_BYTES).
@@ -62,6 +65,10 @@ assert PROBLEM_DTYPE.itemsize == 40
 
 
 PLAN_PERSISTENT = 1
+
+LABEL_LOSS_FOCAL = 0
+LABEL_LOSS_IA_BCE = 1
+LABEL_LOSS_PART_ELEMS = 8192
 
 LAYOUT_QUERY_MAJOR = 0
 LAYOUT_TARGET_MAJOR = 1
@@ -137,6 +144,14 @@ def load() -> ctypes.CDLL:
     lib.rfm_box_loss_forward.argtypes = [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _p, _p]
     lib.rfm_box_loss_backward.restype = _i32
     lib.rfm_box_loss_backward.argtypes = [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _p, _p, _p, _p]
+    lib.rfm_label_loss_parts.restype = _i64
+    lib.rfm_label_loss_parts.argtypes = [_i32, _i32, _i32, _i32]
+    lib.rfm_label_loss_forward.restype = _i32
+    lib.rfm_label_loss_forward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
+                                           _p, _p, _p]
+    lib.rfm_label_loss_backward.restype = _i32
+    lib.rfm_label_loss_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
+                                            _p, _p, _p]
     lib.rfm_lsap_dense_noalloc.restype = _i32
     lib.rfm_lsap_dense_noalloc.argtypes = [_p, _i32, _i32, _i32, _p, _p, _p]
     _lib = lib

@@ -6,8 +6,8 @@
 // written directly, so there is no padded intermediate and no copy.
 //
 // Two output layouts.  TARGET-MAJOR (the transpose, out[l][col][q]) is the one
-// the fused matcher step uses: one CTA covers 32 consecutive target rows (8 when
-// 32-row CTAs would not fill the GPU twice, as in the production step; runs
+// the fused matcher step uses: one CTA covers 64 consecutive target rows (8 when
+// 64-row CTAs would not fill the GPU twice, as in the production step; runs
 // of one image each) and a 256-query tile; each thread owns two consecutive
 // queries (one 8-byte vector of every output row), loads their boxes and logits
 // once per image run (the next run's while computing the current one),
@@ -266,8 +266,8 @@ __global__ void __launch_bounds__(kThreads) cost_qmajor_kernel(const CostArgs a)
 
 constexpr int kTmThreads = 128;  // 2 queries each: 256 queries per CTA
 constexpr int kQpt = 2;          // queries per thread (one f32x2 pair)
-constexpr int kTmCols = 32;      // target rows per CTA (may span several images)
-constexpr int kTmColsSmall = 8;  // ... for batches too small to fill the GPU twice with 32-row CTAs
+constexpr int kTmCols = 64;      // target rows per CTA (may span several images)
+constexpr int kTmColsSmall = 8;  // ... for batches too small to fill the GPU twice with 64-row CTAs
 constexpr int kSmallClasses = 4;
 
 // Packed float32 pairs: two queries per instruction (sm_100 f32x2 pipe), each
@@ -618,10 +618,10 @@ int cost_run(const float* pred_logits, const float* pred_boxes, const int64_t* t
 
   if (layout == RFM_LAYOUT_TARGET_MAJOR) {
     const int64_t gy = (ld / kQpt + kTmThreads - 1) / kTmThreads;
-    // 32 target rows per CTA, or 8 when that leaves fewer than two CTAs per SM
+    // 64 target rows per CTA, or 8 when that leaves fewer than two CTAs per SM
     // (the production step: a few hundred CTAs, each then a quarter as long)
-    const int64_t gx32 = (static_cast<int64_t>(sum_targets) + kTmCols - 1) / kTmCols;
-    const bool small = gx32 * gy * num_layers < 2 * static_cast<int64_t>(device_sm_count());
+    const int64_t gx_big = (static_cast<int64_t>(sum_targets) + kTmCols - 1) / kTmCols;
+    const bool small = gx_big * gy * num_layers < 2 * static_cast<int64_t>(device_sm_count());
     const int cols = small ? kTmColsSmall : kTmCols;
     const int64_t gx = (static_cast<int64_t>(sum_targets) + cols - 1) / cols;
     if (gy > 65535 || gx > 0x7fffffff) return RFM_ERR_UNSUPPORTED;

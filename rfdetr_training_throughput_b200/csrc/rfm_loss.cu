@@ -175,6 +175,273 @@ __global__ void __launch_bounds__(kLossThreads) box_loss_backward_kernel(const L
   }
 }
 
+// ---------------------------------------------------------------------------
+// Classification loss over all logits with the matched classes as positives
+// (SetCriterion.loss_labels, the criterion's other consumer of the indices:
+// criterion.py:562 as cited at patches.py:339-341).
+//
+// The criterion scatters target["labels"][J] into a [B, Q] class map at the
+// matched (image, query) slots and evaluates a sigmoid loss over every
+// [B, Q, C] logit, positive where (q, c) is a matched query and its target's
+// class.  Here one CTA covers a tile of queries of one (layer, image): it
+// streams the tile's logits once, coalesced, evaluating every element as a
+// negative, and corrects the matched (query, class) elements from the packed
+// pairs directly (no class map, no one-hot tensor).
+// Two losses, by `mode`, both summed (the caller divides by num_boxes):
+//
+//   FOCAL (Deformable-DETR's sigmoid_focal_loss on one-hot targets, gamma 2):
+//     y = 1: alpha (1-p)^2 softplus(-x)      y = 0: (1-alpha) p^2 softplus(x)
+//   IA_BCE (LW-DETR / RF-DETR IoU-aware BCE): with u = IoU(pred, target) of
+//   the matched pair (box_iou: inter / union, no clamp) and
+//   t = max(p^alpha u^(1-alpha), 0.01) held constant (detached):
+//     y = 1: (1-t) x + softplus(-x)          y = 0: p^2 softplus(x)
+//
+// p = sigmoid(x), softplus(x) = max(x, 0) + log1p(exp(-|x|)).  Gradients are
+// those of torch's autograd of the same expressions (t constant; the negative
+// weight p^2 differentiated).  Matched labels outside [0, C) make no positive.
+constexpr int kLabelThreads = 256;
+constexpr int kLabelMaxTile = 4096;  // queries per CTA at most
+
+// Queries per CTA (one partial sum each): about RFM_LABEL_LOSS_PART_ELEMS logits, a multiple of 32
+// between 64 and kLabelMaxTile, so that few-class and many-class batches both give CTAs of a few
+// thousand elements.
+__host__ __device__ inline int label_tile_queries(int num_classes) {
+  int t = RFM_LABEL_LOSS_PART_ELEMS / (num_classes > 0 ? num_classes : 1);
+  t = t < 64 ? 64 : (t > kLabelMaxTile ? kLabelMaxTile : t);
+  return t & ~31;
+}
+
+struct LabelArgs {
+  const float* logits;          // [L, B, Q, C]
+  const float4* pred;           // [L, B, Q] cxcywh (IA_BCE only)
+  const int64_t* labels;        // [S]
+  const float4* tgt;            // [S] cxcywh (IA_BCE only)
+  const int32_t* tgt_offsets;   // [B + 1]
+  const int64_t* query_idx;     // pairs
+  const int64_t* target_idx;
+  const int32_t* pair_offsets;  // [L * B + 1]
+  int L, B, Q, C, S, tiles, tile_q;
+  int mode;
+  float alpha;
+  float* loss_part;             // [L * B * tiles]
+  int32_t* correct_part;        // [L * B * tiles] or null
+  const float* grad_loss;       // [L]
+  float* grad_logits;           // [L, B, Q, C]
+};
+
+// sigmoid and softplus of x from one exponent, one logarithm and one
+// reciprocal: e = exp(-|x|), d = 1 + e, log1p(e) = log(d), sigmoid(x) =
+// (x >= 0 ? 1 : e) / d; softplus(+-x) = max(+-x, 0) + log1p(e).
+struct Sig {
+  float p, q, l;  // p = sigmoid(x), q = 1 - p = sigmoid(-x), l = log1p(exp(-|x|))
+};
+
+__device__ __forceinline__ Sig sig(float x) {
+  const float e = __expf(-fabsf(x));
+  const float d = 1.0f + e;
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  Sig s;
+  s.l = __logf(d);
+  s.p = x >= 0.0f ? r : e * r;
+  s.q = x >= 0.0f ? e * r : r;
+  return s;
+}
+
+// IoU of two cxcywh boxes as box_iou computes it (union not clamped).
+__device__ __forceinline__ float box_iou(float4 pb, float4 tb) {
+  const Xyxy p = xyxy(pb), t = xyxy(tb);
+  const float area_p = __fmul_rn(__fsub_rn(p.x1, p.x0), __fsub_rn(p.y1, p.y0));
+  const float area_t = __fmul_rn(__fsub_rn(t.x1, t.x0), __fsub_rn(t.y1, t.y0));
+  const float iw = fmaxf(__fsub_rn(fminf(p.x1, t.x1), fmaxf(p.x0, t.x0)), 0.0f);
+  const float ih = fmaxf(__fsub_rn(fminf(p.y1, t.y1), fmaxf(p.y0, t.y0)), 0.0f);
+  const float inter = __fmul_rn(iw, ih);
+  return __fdiv_rn(inter, __fsub_rn(__fadd_rn(area_p, area_t), inter));
+}
+
+// Loss term of one logit and its derivative; `pos` marks the matched class.
+__device__ __forceinline__ void label_term(const LabelArgs& a, float x, bool pos, float t, float& loss, float& grad) {
+  const Sig g = sig(x);
+  const float sp_pos = fmaxf(x, 0.0f) + g.l;   // softplus(x)
+  const float sp_neg = fmaxf(-x, 0.0f) + g.l;  // softplus(-x)
+  if (a.mode == RFM_LABEL_LOSS_FOCAL) {
+    if (pos) {
+      loss = a.alpha * g.q * g.q * sp_neg;
+      grad = -a.alpha * g.q * g.q * (2.0f * g.p * sp_neg + g.q);
+    } else {
+      loss = (1.0f - a.alpha) * g.p * g.p * sp_pos;
+      grad = (1.0f - a.alpha) * g.p * g.p * (2.0f * g.q * sp_pos + g.p);
+    }
+  } else {
+    if (pos) {
+      loss = (1.0f - t) * x + sp_neg;
+      grad = g.p - t;
+    } else {
+      loss = g.p * g.p * sp_pos;
+      grad = g.p * g.p * (2.0f * g.q * sp_pos + g.p);
+    }
+  }
+}
+
+// Matched pair k (query q) of CTA tile [q0, q0 + nq) of (layer, image) lb: its logit
+// offset within the tile, its class's logit x and, for the IoU-aware loss, its
+// soft target t; false when the pair is outside the tile or holds no valid
+// target.  `correct` counts it when its largest logit is its class.
+__device__ __forceinline__ bool load_match(const LabelArgs& a, int lb, int64_t k, int64_t q, int q0, int nq, int t0,
+                                           int nt, int64_t& elem, float& x, float& t, int& correct) {
+  const int64_t ti = a.target_idx[k];
+  if (q < q0 || q >= q0 + nq || ti < 0 || ti >= nt) return false;
+  const int64_t cls = a.labels[t0 + ti];
+  if (cls < 0 || cls >= a.C) return false;
+  const int64_t row_base = static_cast<int64_t>(lb) * a.Q;
+  const float* row = a.logits + (row_base + q) * a.C;
+  x = row[cls];
+  elem = (q - q0) * a.C + cls;
+  t = 0.0f;
+  if (a.mode == RFM_LABEL_LOSS_IA_BCE) {
+    const float p = 1.0f / (1.0f + expf(-x));
+    const float u = box_iou(__ldg(a.pred + row_base + q), __ldg(a.tgt + t0 + ti));
+    const float v = powf(p, a.alpha) * powf(u, 1.0f - a.alpha);
+    // clamp(min=0.01) that keeps a NaN (a matched pair of two zero-area boxes has IoU 0/0), as
+    // torch.clamp does: the loss is then NaN as in the unfused formula
+    t = v != v ? v : fmaxf(v, 0.01f);
+  }
+  if (a.correct_part != nullptr) {  // top-1 (the smallest index among equal maxima)
+    int best = 0;
+    float bv = row[0];
+    for (int c = 1; c < a.C; ++c) {
+      const float v = row[c];
+      if (v > bv) {
+        bv = v;
+        best = c;
+      }
+    }
+    correct += best == cls ? 1 : 0;
+  }
+  return true;
+}
+
+// One CTA per tile of a.tile_q queries of one (layer, image).  The dense pass
+// treats every logit as a negative; each matched pair then adds (forward) its
+// positive term minus its negative term, or (backward) overwrites its
+// gradient after the dense pass's stores.  The dense pass does not wait for the
+// pairs: the two run on independent loads, and only the backward overwrite
+// needs the barrier after the dense stores.
+template <bool kBackward>
+__global__ void __launch_bounds__(kLabelThreads) label_loss_kernel(const LabelArgs a) {
+  __shared__ float red[kLabelThreads / 32];
+  __shared__ int red_i[kLabelThreads / 32];
+  const int tile = blockIdx.x;
+  const int lb = blockIdx.y;
+  const int q0 = tile * a.tile_q;
+  const int nq = min(a.tile_q, a.Q - q0);
+  const int b = lb % a.B;
+  const int t0 = a.tgt_offsets[b];
+  const int nt = a.tgt_offsets[b + 1] - t0;
+  const int64_t k_begin = a.pair_offsets[lb];
+  const int64_t k_end = a.pair_offsets[lb + 1];
+  const int64_t base = (static_cast<int64_t>(lb) * a.Q + q0) * a.C;
+  const int n = nq * a.C;
+  const float g = kBackward ? a.grad_loss[lb / a.B] : 0.0f;
+  // this thread's first pair is requested before the dense pass
+  int64_t k = k_begin + threadIdx.x;
+  int64_t q_next = k < k_end ? a.query_idx[k] : -1;
+  float sum = 0.0f;
+  for (int e = threadIdx.x; e < n; e += kLabelThreads) {
+    const float x = a.logits[base + e];
+    float loss, grad;
+    label_term(a, x, false, 0.0f, loss, grad);
+    if (kBackward) {
+      a.grad_logits[base + e] = g * grad;
+    } else {
+      sum += loss;
+    }
+  }
+  // the pairs of (l, b), strided over the threads; only the tile's are used
+  int correct = 0;
+  if (kBackward) __syncthreads();  // every dense store of the tile precedes the overwrites
+  for (; k < k_end; k += kLabelThreads) {
+    const int64_t q = q_next;
+    q_next = k + kLabelThreads < k_end ? a.query_idx[k + kLabelThreads] : -1;
+    int64_t elem;
+    float x, t;
+    if (!load_match(a, lb, k, q, q0, nq, t0, nt, elem, x, t, correct)) continue;
+    float lp, gp, ln, gn;
+    label_term(a, x, true, t, lp, gp);
+    if (kBackward) {
+      a.grad_logits[base + elem] = g * gp;
+    } else {
+      label_term(a, x, false, 0.0f, ln, gn);
+      sum += lp - ln;
+    }
+  }
+  if (!kBackward) {
+    // fixed-order reduction: warp shuffles, then the warps' sums in order
+    float v = sum;
+    int c = correct;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      v += __shfl_xor_sync(kFullMask, v, o);
+      c += __shfl_xor_sync(kFullMask, c, o);
+    }
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+      red[warp] = v;
+      red_i[warp] = c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.0f;
+      int kk = 0;
+      for (int w = 0; w < kLabelThreads / 32; ++w) {
+        s += red[w];
+        kk += red_i[w];
+      }
+      const int64_t part = static_cast<int64_t>(lb) * a.tiles + tile;
+      a.loss_part[part] = s;
+      if (a.correct_part != nullptr) a.correct_part[part] = kk;
+    }
+  }
+}
+
+int label_args(LabelArgs& a, const float* logits, const float* pred_boxes, const int64_t* labels,
+               const float* tgt_boxes, const int32_t* tgt_offsets, const int64_t* query_idx,
+               const int64_t* target_idx, const int32_t* pair_offsets, int L, int B, int Q, int C, int S, int mode,
+               float alpha) {
+  if (L < 1 || B < 1 || Q < 1 || C < 1 || S < 0 || static_cast<int64_t>(L) * B > 65535 ||
+      (mode != RFM_LABEL_LOSS_FOCAL && mode != RFM_LABEL_LOSS_IA_BCE) || !(alpha >= 0.0f && alpha <= 1.0f)) {
+    return RFM_ERR_INVALID_ARGUMENT;
+  }
+  if (logits == nullptr || tgt_offsets == nullptr || pair_offsets == nullptr ||
+      (S > 0 && labels == nullptr) ||
+      (mode == RFM_LABEL_LOSS_IA_BCE && (pred_boxes == nullptr || !aligned16(pred_boxes) ||
+                                         (S > 0 && (tgt_boxes == nullptr || !aligned16(tgt_boxes)))))) {
+    return RFM_ERR_INVALID_ARGUMENT;
+  }
+  a.logits = logits;
+  a.pred = reinterpret_cast<const float4*>(pred_boxes);
+  a.labels = labels;
+  a.tgt = reinterpret_cast<const float4*>(tgt_boxes);
+  a.tgt_offsets = tgt_offsets;
+  a.query_idx = query_idx;
+  a.target_idx = target_idx;
+  a.pair_offsets = pair_offsets;
+  a.L = L;
+  a.B = B;
+  a.Q = Q;
+  a.C = C;
+  a.S = S;
+  a.tile_q = label_tile_queries(C);
+  a.tiles = (Q + a.tile_q - 1) / a.tile_q;
+  a.mode = mode;
+  a.alpha = alpha;
+  a.loss_part = nullptr;
+  a.correct_part = nullptr;
+  a.grad_loss = nullptr;
+  a.grad_logits = nullptr;
+  return RFM_OK;
+}
+
 int loss_args(LossArgs& a, const float* pred_boxes, const float* tgt_boxes, const int32_t* tgt_offsets,
               const int64_t* query_idx, const int64_t* target_idx, const int32_t* pair_offsets, int L, int B,
               int Q, int S) {
@@ -237,5 +504,51 @@ extern "C" int rfm_box_loss_backward(const float* pred_boxes, const float* tgt_b
   a.grad_giou = grad_giou;
   a.grad_pred = reinterpret_cast<float4*>(grad_pred);
   box_loss_backward_kernel<<<num_layers * num_images, kLossThreads, 0, as_stream(stream)>>>(a);
+  return launch_status();
+}
+
+extern "C" int64_t rfm_label_loss_parts(int num_layers, int num_images, int num_queries, int num_classes) {
+  if (num_layers < 1 || num_images < 1 || num_queries < 1 || num_classes < 1) {
+    return -static_cast<int64_t>(RFM_ERR_INVALID_ARGUMENT);
+  }
+  const int tile = rfm::label_tile_queries(num_classes);
+  return static_cast<int64_t>(num_layers) * num_images * ((num_queries + tile - 1) / tile);
+}
+
+extern "C" int rfm_label_loss_forward(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+                                     const float* tgt_boxes, const int32_t* tgt_offsets, const int64_t* query_idx,
+                                     const int64_t* target_idx, const int32_t* pair_offsets, int num_layers,
+                                     int num_images, int num_queries, int num_classes, int sum_targets, int mode,
+                                     float focal_alpha, float* loss_part, int32_t* correct_part, void* stream) {
+  using namespace rfm;
+  LabelArgs a;
+  const int rc = label_args(a, pred_logits, pred_boxes, tgt_labels, tgt_boxes, tgt_offsets, query_idx, target_idx,
+                            pair_offsets, num_layers, num_images, num_queries, num_classes, sum_targets, mode,
+                            focal_alpha);
+  if (rc != RFM_OK) return rc;
+  if (loss_part == nullptr) return RFM_ERR_INVALID_ARGUMENT;
+  a.loss_part = loss_part;
+  a.correct_part = correct_part;
+  const dim3 grid(static_cast<unsigned>(a.tiles), static_cast<unsigned>(num_layers * num_images));
+  label_loss_kernel<false><<<grid, kLabelThreads, 0, as_stream(stream)>>>(a);
+  return launch_status();
+}
+
+extern "C" int rfm_label_loss_backward(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+                                      const float* tgt_boxes, const int32_t* tgt_offsets, const int64_t* query_idx,
+                                      const int64_t* target_idx, const int32_t* pair_offsets, int num_layers,
+                                      int num_images, int num_queries, int num_classes, int sum_targets, int mode,
+                                      float focal_alpha, const float* grad_loss, float* grad_logits, void* stream) {
+  using namespace rfm;
+  LabelArgs a;
+  const int rc = label_args(a, pred_logits, pred_boxes, tgt_labels, tgt_boxes, tgt_offsets, query_idx, target_idx,
+                            pair_offsets, num_layers, num_images, num_queries, num_classes, sum_targets, mode,
+                            focal_alpha);
+  if (rc != RFM_OK) return rc;
+  if (grad_loss == nullptr || grad_logits == nullptr) return RFM_ERR_INVALID_ARGUMENT;
+  a.grad_loss = grad_loss;
+  a.grad_logits = grad_logits;
+  const dim3 grid(static_cast<unsigned>(a.tiles), static_cast<unsigned>(num_layers * num_images));
+  label_loss_kernel<true><<<grid, kLabelThreads, 0, as_stream(stream)>>>(a);
   return launch_status();
 }

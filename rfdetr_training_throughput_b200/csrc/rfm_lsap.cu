@@ -80,9 +80,15 @@ constexpr int kMaxWarpsPerCta = 4;
 // whose four warps share the load pass (a quarter of the rows each, so a
 // problem's rows cost a quarter of the round trips) before warp 0 solves it
 // alone: small batches, where every problem is resident at once and the
-// step's time is the slowest problem's latency.
-enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2, kVarCoop = 3 };
+// step's time is the slowest problem's latency.  STAGE is COOP for small batches
+// of long problems (searches of many steps): its CTA takes all the shared
+// memory an SM gives one or two CTAs, the load pass keeps as many of the
+// problem's rows there as fit, and warp 0's searches read those rows from shared
+// memory (the rest from L2), each scan's row requested early as in EARLY.
+enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2, kVarCoop = 3, kVarStage = 4 };
 constexpr int kEarlyMinRows = 64;
+// Batches of long problems (EARLY) with at most this many problems per SM run as STAGE.
+constexpr int kStageCtasPerSm = 2;
 // Batches with more than this many problems per SM use the wide layout.
 constexpr int kWideProblemsPerSm = 64;
 // Register budget.  The instantiations up to 320 columns run four CTAs of four
@@ -323,8 +329,9 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
                                              int lane) {
   constexpr int kCols = 32 * K;
   constexpr bool kWide = kVariant == kVarWide;
-  constexpr bool kEarly = kVariant == kVarEarly;
-  constexpr bool kCoop = kVariant == kVarCoop;
+  constexpr bool kStage = kVariant == kVarStage;
+  constexpr bool kEarly = kVariant == kVarEarly || kStage;
+  constexpr bool kCoop = kVariant == kVarCoop || kStage;
   constexpr int kLoadWarps = kCoop ? kMaxWarpsPerCta : 1;
   const int warp = kCoop ? static_cast<int>(threadIdx.x >> 5) : 0;
   int64_t cost_off, out_off, scratch_off;
@@ -410,6 +417,8 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   const int64_t fixed = fixed_warp_bytes(kCols, a.max_rows, kWide);
   float* tile = reinterpret_cast<float*>(base + fixed);
   const int mode = choose_mode(s, a.tile_cap, (slot - fixed) / 4);
+  // STAGE: solver rows [0, staged) are kept in shared memory (all of them when the tile fits)
+  const int staged = kStage ? min(nr, static_cast<int>((slot - fixed) / 4 / nc)) : 0;
   bool bad = false;
   const float* rows = src;  // solver row i starts at rows + i * row_pitch
   int64_t row_pitch = s.rs;
@@ -437,13 +446,14 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
         m[r] = lane_min<K>(x[r]);
         chk = min_nan(chk, m[r]);
       }
-      if (mode == kModeShared) {
+      if (kStage || mode == kModeShared) {
+        const int keep = kStage ? staged : nr;
 #pragma unroll
         for (int r = 0; r < kLoadRows; ++r) {
 #pragma unroll
           for (int k = 0; k < K; ++k) {
             const int j = lane + 32 * k;
-            if (j < nc && i + r < nr) tile[(i + r) * nc + j] = x[r][k];
+            if (j < nc && i + r < keep) tile[(i + r) * nc + j] = x[r][k];
           }
         }
       }
@@ -452,7 +462,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
         if (i + r < nr) record_first_pick<K>(x[r], m[r], lane, nc, i + r, pick_m_s, pick_w_s);
       }
     }
-    if (mode == kModeShared) {
+    if (!kStage && mode == kModeShared) {
       rows = tile;
       row_pitch = nc;
     }
@@ -545,6 +555,14 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
 
     float cf[K];
     const auto issue_row = [&](int r) {
+      if (kStage) {  // staged rows from shared memory, the rest from L2 / HBM
+        if (r < staged) {
+          load_row<K, kLoadShared>(tile + r * nc, lane, rem, cf);
+        } else {
+          load_row<K, kLoadGlobal>(src + r * s.rs, lane, rem, cf);
+        }
+        return;
+      }
       const float* row = rows + r * row_pitch;
       if (mode == kModeShared) {
         load_row<K, kLoadShared>(row, lane, rem, cf);
@@ -702,7 +720,7 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVari
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  if (kVariant == kVarCoop) {
+  if (kVariant == kVarCoop || kVariant == kVarStage) {
     // one problem per CTA, all four warps in its load pass
     solve_problem<K, kDense, kVariant>(a, blockIdx.x, smem_raw, a.slot, lane);
     return;
@@ -752,14 +770,16 @@ const void* pair_kernel(int cols_per_lane, int variant) {
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarWide>);
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarEarly>);
       if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarCoop>);
+      if (variant == kVarStage) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarStage>);
       return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarRegs>);
     case 10:
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarWide>);
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarEarly>);
       if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarCoop>);
+      if (variant == kVarStage) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarStage>);
       return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarRegs>);
     case 32:
-      if (variant == kVarWide || variant == kVarCoop) return nullptr;
+      if (variant == kVarWide || variant == kVarCoop || variant == kVarStage) return nullptr;
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarEarly>);
       return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarRegs>);
     default: return nullptr;
@@ -868,9 +888,10 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense, kVariant>); break;
     case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, kDense, kVariant>); break;
     case 32:
-      if (kVariant == kVarWide || kVariant == kVarCoop) return RFM_ERR_INVALID_ARGUMENT;
+      if (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage) return RFM_ERR_INVALID_ARGUMENT;
       fn = reinterpret_cast<const void*>(
-          &lsap_kernel<32, kDense, (kVariant == kVarWide || kVariant == kVarCoop) ? kVarRegs : kVariant>);
+          &lsap_kernel<32, kDense,
+                       (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage) ? kVarRegs : kVariant>);
       break;
     default: return RFM_ERR_INVALID_ARGUMENT;
   }
@@ -907,7 +928,8 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     case 4: lsap_kernel<4, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
     case 10: lsap_kernel<10, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
     default:
-      lsap_kernel<32, kDense, (kVariant == kVarWide || kVariant == kVarCoop) ? kVarRegs : kVariant>
+      lsap_kernel<32, kDense,
+                  (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage) ? kVarRegs : kVariant>
           <<<grid, block, smem, as_stream(stream)>>>(a);
       break;
   }
@@ -1086,6 +1108,18 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   // large batches (more problems than 64 per SM) take the wide layout, batches of
   // long problems the early-load variant.
   const int sms = device_sm_count();
+  if (early && plan->cols_per_lane <= 10 &&
+      static_cast<int64_t>(plan->num_problems) <= static_cast<int64_t>(kStageCtasPerSm) * sms) {
+    // a small batch of long problems: one problem per CTA, each CTA with the
+    // shared memory of an SM split kStageCtasPerSm ways (or all of it when the
+    // batch fits one CTA per SM), its rows staged there as far as they fit
+    const int per_sm = plan->num_problems <= sms ? 1 : kStageCtasPerSm;
+    const int64_t smem = kSmemPerSm / per_sm - kSmemPerCtaReserved;
+    a.slot = static_cast<int>(smem > kSmemPerBlockMax ? kSmemPerBlockMax : smem);
+    a.tile_cap = (a.slot - static_cast<int>(fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))) / 4;
+    return launch<false, kVarStage>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, a.slot, stream,
+                                    counter_zeroed);
+  }
   const bool wide = plan->cols_per_lane <= 10 &&
                     static_cast<int64_t>(plan->num_problems) > static_cast<int64_t>(kWideProblemsPerSm) * sms;
   const int variant = wide ? kVarWide : (early ? kVarEarly : kVarRegs);

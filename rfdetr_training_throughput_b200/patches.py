@@ -18,6 +18,10 @@ which applies them in order, returns one description per patch and raises
 ``box_loss``        ``SetCriterion.loss_boxes`` -> ``rfm_box_loss_forward/backward`` on the
                     matcher's index pairs (new: the criterion consumer of the indices,
                     DETR's loss_boxes contract)
+``label_loss``      ``SetCriterion.loss_labels`` -> ``rfm_label_loss_forward/backward`` on the
+                    index pairs (new: the criterion's classification loss, the IoU-aware
+                    BCE when the criterion has ``ia_bce_loss`` set, else the sigmoid focal
+                    loss; the varifocal and position-supervised variants raise)
 
 Unlike the reference there is no fallback to the original implementation for
 CPU tensors or out-of-envelope inputs: the patched functions raise instead.
@@ -96,6 +100,21 @@ def _apply_box_loss() -> str:
     return "box_loss: SetCriterion.loss_boxes computed from the index pairs by the sm_100a loss kernels"
 
 
+def _apply_label_loss() -> str:
+    cls = _module("rfdetr.models.criterion").SetCriterion
+    from .loss import criterion_loss_labels
+
+    def loss_labels(self, outputs, targets, indices, num_boxes, log=True):
+        if getattr(self, "use_varifocal_loss", False) or getattr(self, "use_position_supervised_loss", False):
+            raise NotImplementedError("only the IoU-aware BCE and the sigmoid focal classification losses run here")
+        mode = "ia_bce" if getattr(self, "ia_bce_loss", False) else "focal"
+        return criterion_loss_labels(outputs, targets, indices, num_boxes, log, mode=mode,
+                                     focal_alpha=getattr(self, "focal_alpha", 0.25))
+
+    cls.loss_labels = loss_labels
+    return "label_loss: SetCriterion.loss_labels computed from the index pairs by the sm_100a loss kernels"
+
+
 PATCHES: dict[str, Callable[[], str]] = {
     "triton_matcher": _apply_triton_matcher,
     "cuda_lap": _apply_cuda_lap,
@@ -103,6 +122,7 @@ PATCHES: dict[str, Callable[[], str]] = {
     "stacked_costs": _apply_stacked_costs,
     "matcher": _apply_matcher,
     "box_loss": _apply_box_loss,
+    "label_loss": _apply_label_loss,
 }
 
 

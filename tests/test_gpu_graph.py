@@ -1,9 +1,14 @@
 """MatchGraph: the captured step must return exactly what match_packed returns (index pairs:
 exact equality) for every batch of its shape, including the wide solver layout, and must
-refuse batches of another shape."""
+refuse batches of another shape.  The replayed pairs of the production step are also checked
+directly against SciPy on the device-computed cost matrix."""
 
+import numpy as np
 import pytest
 import torch
+from scipy.optimize import linear_sum_assignment
+
+from oracle.matcher import solve_blocks
 
 from rfdetr_training_throughput_b200 import MatchGraph, MatchGraphCache, matcher, workloads
 
@@ -43,6 +48,28 @@ def test_graph_replays_match_eager_steps(name, kw):
     torch.cuda.synchronize()
     assert torch.equal(res2.pairs, expect.pairs)
     assert res2.per_image == expect.per_image
+
+
+def scipy_pairs(wl, logits, boxes, packed) -> np.ndarray:
+    """SciPy's pairs for every (layer, image, group) block of the device-computed cost, in the packed
+    order of a MatchResult (layer-major, images in order, groups in order)."""
+    ex = {}
+    matcher.match_packed(logits, boxes, packed, wl.group_detr, weights=wl.weights, extras=ex)
+    cost = ex["cost"][:, :, : wl.queries].transpose(1, 2).cpu().numpy()  # compact [L, Q, S]
+    cols = []
+    for l in range(wl.layers):
+        for q, t in solve_blocks(cost[l], wl.sizes, wl.group_detr, solver=linear_sum_assignment):
+            cols.append(np.stack([q, t]))
+    return np.concatenate(cols, axis=1)
+
+
+def test_graph_replay_equals_scipy_on_the_device_cost():
+    wl = workloads.make("step")
+    g = MatchGraph(wl.sizes, wl.layers, wl.queries, wl.classes, wl.group_detr, weights=wl.weights)
+    logits, boxes, packed = _inputs(wl)
+    res = g(logits, boxes, packed.labels, packed.boxes)
+    torch.cuda.synchronize()
+    assert np.array_equal(res.pairs.cpu().numpy(), scipy_pairs(wl, logits, boxes, packed))
 
 
 def test_graph_refuses_other_shapes_and_cache_keys_by_shape():

@@ -1,8 +1,11 @@
 """PrefetchingMatcher: batches uploaded on a copy stream while the previous batch is matched give
-exactly the pairs match_packed gives for each batch (index pairs: exact equality)."""
+exactly the pairs match_packed gives for each batch (index pairs: exact equality), and the first
+batch's pairs are checked directly against SciPy on the device-computed cost matrix."""
 
+import numpy as np
 import pytest
 import torch
+from test_gpu_graph import scipy_pairs
 
 from rfdetr_training_throughput_b200 import matcher, workloads
 from rfdetr_training_throughput_b200.pipeline import PrefetchingMatcher
@@ -38,3 +41,7 @@ def test_prefetched_batches_match_like_match_packed():
     torch.cuda.synchronize()
     for b, got in zip(order, outs):
         assert torch.equal(got, expect[b])
+    wl0 = workloads.make("sweep", images=64, shard=0)
+    lg, bx, lb, tb, sz = batches[0]
+    packed = matcher.PackedTargets(lb.to(DEV), tb.to(DEV), sz)
+    assert np.array_equal(outs[0].cpu().numpy(), scipy_pairs(wl0, lg.to(DEV), bx.to(DEV), packed))

@@ -31,7 +31,9 @@ def fake_rfdetr(monkeypatch):
         "torch_linear_assignment.assignment": types.ModuleType("torch_linear_assignment.assignment"),
     }
     mods["rfdetr.models.matcher"].HungarianMatcher = HungarianMatcher
-    mods["rfdetr.models.criterion"].SetCriterion = type("SetCriterion", (), {"loss_boxes": lambda *a: "upstream"})
+    mods["rfdetr.models.criterion"].SetCriterion = type(
+        "SetCriterion", (), {"loss_boxes": lambda *a: "upstream", "loss_labels": lambda *a, **k: "upstream",
+                             "focal_alpha": 0.25, "ia_bce_loss": True})
     mods["rfdetr.models.matcher"]._STACKED_COST_ELEMENT_LIMIT = 350_000
     mods["rfdetr.models._assignment"]._assign_padded = lambda *a: "upstream"
     mods["torch_linear_assignment.assignment"].batch_linear_assignment = lambda c: "upstream"
@@ -42,8 +44,8 @@ def fake_rfdetr(monkeypatch):
 
 
 def test_apply_patches_rebinds_the_reference_names(fake_rfdetr):
-    done = patches.apply_patches("triton_matcher, cuda_lap,device_indices,stacked_costs,matcher,box_loss")
-    assert len(done) == 6 and all(":" in d for d in done)
+    done = patches.apply_patches("triton_matcher, cuda_lap,device_indices,stacked_costs,matcher,box_loss,label_loss")
+    assert len(done) == 7 and all(":" in d for d in done)
     cls = fake_rfdetr["rfdetr.models.matcher"].HungarianMatcher
     assert fake_rfdetr["torch_linear_assignment.assignment"].batch_linear_assignment is matcher.batch_linear_assignment
     assert fake_rfdetr["torch_linear_assignment"].batch_linear_assignment is matcher.batch_linear_assignment
@@ -61,6 +63,13 @@ def test_apply_patches_rebinds_the_reference_names(fake_rfdetr):
     with pytest.raises(ValueError, match="CUDA"):
         crit.loss_boxes({"pred_boxes": torch.zeros(1, 3, 4)}, targets,
                         [(torch.zeros(1, dtype=torch.int64), torch.zeros(1, dtype=torch.int64))], 1.0)
+    with pytest.raises(ValueError, match="CUDA"):
+        crit.loss_labels(outputs, targets, [(torch.zeros(1, dtype=torch.int64), torch.zeros(1, dtype=torch.int64))],
+                         1.0)
+    crit.use_varifocal_loss = True
+    with pytest.raises(NotImplementedError):
+        crit.loss_labels(outputs, targets, [(torch.zeros(1, dtype=torch.int64), torch.zeros(1, dtype=torch.int64))],
+                         1.0)
 
 
 def test_unknown_patch_name_raises_keyerror():

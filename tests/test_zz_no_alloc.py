@@ -5,7 +5,8 @@ not add a cudaMalloc/cudaFree beside the framework's caching allocator) call thi
 entry point instead of rfm_lsap_dense; it uses a scratch array built into the
 library.  The test calls both entry points through the C ABI on batches that need
 scratch, twice in a row with different data, and requires identical matchings
-(index outputs: the tolerance is exact equality, as for every solver test).
+(index outputs: the tolerance is exact equality, as for every solver test); the
+no-allocation results are also checked against SciPy itself, problem by problem.
 """
 
 import ctypes
@@ -13,6 +14,7 @@ import ctypes
 import numpy as np
 import pytest
 import torch
+from scipy.optimize import linear_sum_assignment
 
 from rfdetr_training_throughput_b200 import _lib
 
@@ -57,6 +59,12 @@ def test_noalloc_matches_the_workspace_entry_point_on_two_calls():
         torch.cuda.synchronize()
         assert torch.equal(got, ref), f"call {call}"
         assert bool((status == 0).all())
+        host = cost.cpu().numpy()
+        for p in range(shape[0]):
+            rows, cols = linear_sum_assignment(host[p])
+            expect = np.full(shape[1], -1, dtype=np.int64)
+            expect[rows] = cols
+            assert np.array_equal(got[p].cpu().numpy(), expect), f"call {call}, problem {p}"
 
 
 def test_noalloc_rejects_batches_beyond_its_scratch():

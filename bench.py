@@ -485,10 +485,12 @@ def run_rfm(args) -> None:
     box_loss = None
     configs = None
     label_loss = None
+    msda = None
     if world == 1 and not args.no_production_step:
         production = production_step_timing(device, max(args.warmup, 3))
         box_loss = box_loss_timing(device, max(args.warmup, 3))
         label_loss = label_loss_timing(device, max(args.warmup, 3), wl, logits, boxes, packed)
+        msda = msda_timing(device, max(args.warmup, 3))
     lsap_batches = None
     if world == 1 and not args.no_configs:
         configs = config_table(device, args, flush, wl)
@@ -541,7 +543,8 @@ def run_rfm(args) -> None:
             "graph_replay": {"ms_per_step": graph_max_ms / args.steps,
                              "problems_per_s": world * problems * args.steps / (graph_max_ms / 1e3),
                              "what": "the same step through a captured MatchGraph (one host call per step)"},
-            "production_step": production, "box_loss": box_loss, "label_loss": label_loss, "configs": configs,
+            "production_step": production, "box_loss": box_loss, "label_loss": label_loss, "msda": msda,
+            "configs": configs,
             "lsap_batches": lsap_batches,
             "library": _lib.version(), "step_ms": step_stats(step_ms), "per_rank_step_ms": per_rank,
         }
@@ -829,6 +832,65 @@ def label_loss_timing(device, warmup: int, sweep_wl, sweep_logits, sweep_boxes, 
                     "backward_gbs": 2 * nbytes / b_us / 1e3, "forward_frac_of_hbm": nbytes / f_us / 1e3 / peak,
                     "backward_frac_of_hbm": 2 * nbytes / b_us / 1e3 / peak,
                     "bytes": "forward reads the logits once; backward reads them and writes the gradient"}
+    return out
+
+
+def msda_timing(device, warmup: int, steps: int = 20) -> dict:
+    """Deformable attention (the MSDeformAttn core), forward + backward, fp32, at the reference's
+    production geometry (kernels_msda_cuda.py CASES / bench_msda.py: batch 8, 8 heads x 32 channels,
+    4 points, levels 36x36 / 18x18 / 9x9; decoder 300 queries, encoder 1701): ``ms_deform_attn``
+    (value in the kernel's [B, S, M, D] layout) against the grid_sample formulation rf-detr runs
+    when no fused kernel is installed, both on the GPU."""
+    import torch.nn.functional as F
+
+    from rfdetr_training_throughput_b200.msda import ms_deform_attn
+
+    shapes_l = [(36, 36), (18, 18), (9, 9)]
+    shapes = torch.tensor(shapes_l, device=device, dtype=torch.int64)
+    seq = sum(h * w for h, w in shapes_l)
+
+    def grid_sample_core(value_bsmd, loc, w):
+        b, _s, m, d = value_bsmd.shape
+        q, levels, points = loc.shape[1], loc.shape[3], loc.shape[4]
+        v = value_bsmd.permute(0, 2, 3, 1)  # [B, M, D, S], the fallback's layout
+        per_level = v.split([h * ww for h, ww in shapes_l], dim=3)
+        grids = 2 * loc - 1
+        sampled = [F.grid_sample(per_level[i].reshape(b * m, d, h, ww), grids[:, :, :, i].transpose(1, 2).flatten(0, 1),
+                                 mode="bilinear", padding_mode="zeros", align_corners=False)
+                   for i, (h, ww) in enumerate(shapes_l)]
+        wts = w.transpose(1, 2).reshape(b * m, 1, q, levels * points)
+        return (torch.stack(sampled, dim=-2).flatten(-2) * wts).sum(-1).view(b, m * d, q).transpose(1, 2)
+
+    out = {"geometry": "batch 8, 8 heads x 32 channels, 4 points, levels 36x36 / 18x18 / 9x9 (sequence 1701)",
+           "steps": steps}
+    for name, queries in (("decoder", 300), ("encoder", 1701)):
+        g = torch.Generator(device=device).manual_seed(7)
+        value = torch.randn((8, seq, 8, 32), device=device, generator=g)
+        loc = torch.rand((8, queries, 8, 3, 4, 2), device=device, generator=g)
+        w = torch.rand((8, queries, 8, 3, 4), device=device, generator=g)
+        w = w / w.sum(-1, keepdim=True)
+        seed = torch.randn((8, queries, 256), device=device, generator=g)
+        entry = {"queries": queries}
+        for impl, fn in (("rfm", lambda v, l, ww: ms_deform_attn(v, shapes, None, l, ww)),
+                         ("grid_sample", grid_sample_core)):
+            vv, ll, wwt = (t.clone().requires_grad_(True) for t in (value, loc, w))
+
+            def run():
+                vv.grad = ll.grad = wwt.grad = None
+                fn(vv, ll, wwt).backward(seed)
+
+            for _ in range(warmup):
+                run()
+            torch.cuda.synchronize(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                run()
+            e1.record()
+            torch.cuda.synchronize(device)
+            entry[f"{impl}_fwd_bwd_ms"] = e0.elapsed_time(e1) / steps
+        entry["speedup"] = entry["grid_sample_fwd_bwd_ms"] / entry["rfm_fwd_bwd_ms"]
+        out[name] = entry
     return out
 
 

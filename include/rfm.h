@@ -344,6 +344,38 @@ int rfm_label_loss_backward(const float* pred_logits, const float* pred_boxes, c
                             int num_images, int num_queries, int num_classes, int sum_targets, int mode,
                             float focal_alpha, const float* grad_loss, float* grad_logits, void* stream);
 
+/*
+ * Multi-scale deformable attention core (MSDeformAttn), fp32.  Replaces the
+ * prebuilt Deformable-DETR kernel the reference routes the decoder and encoder
+ * through (kernels_msda_cuda.py DeformableAttention.forward/backward: the
+ * ms_deform_attn_forward / _backward calls, patches fused_msda and
+ * fused_msda_native, patches.py:566-635); the arithmetic follows Deformable
+ * DETR's published sampling rule (F.grid_sample, bilinear, align_corners=False,
+ * zero padding, per level, then the attention-weighted sum):
+ *
+ *   out[b, q, m, :] = sum_{l, p} w[b, q, m, l, p] *
+ *                     bilinear(value[b, start[l] + (y, x), m, :] at
+ *                              x = loc[.., 0] * W_l - 0.5, y = loc[.., 1] * H_l - 0.5)
+ *
+ *   value               [B, S, M, D] float32 (sequence S = sum of H_l * W_l)
+ *   spatial_shapes      [L, 2] int64 (H_l, W_l), DEVICE; level_start [L] int64
+ *   sampling_locations  [B, Q, M, L, P, 2] float32 in [0, 1] (x, y)
+ *   attention_weights   [B, Q, M, L, P] float32
+ *   out                 [B, Q, M, D] float32 (= [B, Q, M * D])
+ *
+ * L <= 8, P <= 16.  rfm_msda_backward adds d out / d value (for grad_out) into
+ * grad_value (the caller zeroes it; atomic adds, so its last bits may vary
+ * between runs) and writes grad_locations [B, Q, M, L, P, 2] and grad_weights
+ * [B, Q, M, L, P].
+ */
+int rfm_msda_forward(const float* value, const int64_t* spatial_shapes, const int64_t* level_start,
+                     const float* sampling_locations, const float* attention_weights, int batch, int sequence,
+                     int heads, int head_dim, int queries, int levels, int points, float* out, void* stream);
+int rfm_msda_backward(const float* value, const int64_t* spatial_shapes, const int64_t* level_start,
+                      const float* sampling_locations, const float* attention_weights, const float* grad_out,
+                      int batch, int sequence, int heads, int head_dim, int queries, int levels, int points,
+                      float* grad_value, float* grad_locations, float* grad_weights, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,6 +44,8 @@ EXPORTS = (
     "rfm_label_loss_parts",
     "rfm_label_loss_forward",
     "rfm_label_loss_backward",
+    "rfm_msda_forward",
+    "rfm_msda_backward",
 )
 
 #: Size of the built-in scratch of rfm_lsap_dense_noalloc (RFM_NOALLOC_SCRATCH_BYTES).
@@ -152,6 +154,11 @@ def load() -> ctypes.CDLL:
     lib.rfm_label_loss_backward.restype = _i32
     lib.rfm_label_loss_backward.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
                                             _p, _p, _p]
+    lib.rfm_msda_forward.restype = _i32
+    lib.rfm_msda_forward.argtypes = [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p]
+    lib.rfm_msda_backward.restype = _i32
+    lib.rfm_msda_backward.argtypes = [_p, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _p, _p, _p,
+                                      _p]
     lib.rfm_lsap_dense_noalloc.restype = _i32
     lib.rfm_lsap_dense_noalloc.argtypes = [_p, _i32, _i32, _i32, _p, _p, _p]
     _lib = lib

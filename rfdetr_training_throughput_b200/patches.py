@@ -18,6 +18,11 @@ which applies them in order, returns one description per patch and raises
 ``box_loss``        ``SetCriterion.loss_boxes`` -> ``rfm_box_loss_forward/backward`` on the
                     matcher's index pairs (new: the criterion consumer of the indices,
                     DETR's loss_boxes contract)
+``fused_msda``      rf-detr's deformable-attention core ``ms_deform_attn_core_pytorch`` ->
+                    ``rfm_msda_forward/backward`` (patches.py:566-614); export-layout calls
+                    (rank-5 sampling locations) keep the original core
+``fused_msda_native`` ``MSDeformAttn.forward`` with the value kept in the kernel's layout, no
+                    copy (patches.py:617-635); export mode keeps the original forward
 ``label_loss``      ``SetCriterion.loss_labels`` -> ``rfm_label_loss_forward/backward`` on the
                     index pairs (new: the criterion's classification loss, the IoU-aware
                     BCE when the criterion has ``ia_bce_loss`` set, else the sigmoid focal
@@ -115,6 +120,37 @@ def _apply_label_loss() -> str:
     return "label_loss: SetCriterion.loss_labels computed from the index pairs by the sm_100a loss kernels"
 
 
+def _apply_fused_msda() -> str:
+    module = _module("rfdetr.models.ops.modules.ms_deform_attn")
+    from .msda import deformable_attention
+
+    original = module.ms_deform_attn_core_pytorch
+
+    def core(value, value_spatial_shapes, sampling_locations, attention_weights, value_spatial_shapes_hw=None):
+        if sampling_locations.dim() != 6:  # the export layout: not a training call
+            return original(value, value_spatial_shapes, sampling_locations, attention_weights,
+                            value_spatial_shapes_hw=value_spatial_shapes_hw)
+        return deformable_attention(value, value_spatial_shapes, sampling_locations, attention_weights)
+
+    module.ms_deform_attn_core_pytorch = core
+    return "fused_msda: deformable attention core on the sm_100a rfm_msda kernels"
+
+
+def _apply_fused_msda_native() -> str:
+    cls = _module("rfdetr.models.ops.modules.ms_deform_attn").MSDeformAttn
+    from .msda import module_forward
+
+    original = cls.forward
+
+    def forward(self, *args, **kwargs):
+        if getattr(self, "_export", False):
+            return original(self, *args, **kwargs)
+        return module_forward(self, *args, **kwargs)
+
+    cls.forward = forward
+    return "fused_msda_native: MSDeformAttn.forward reaches the rfm_msda kernels without a layout copy"
+
+
 PATCHES: dict[str, Callable[[], str]] = {
     "triton_matcher": _apply_triton_matcher,
     "cuda_lap": _apply_cuda_lap,
@@ -123,6 +159,8 @@ PATCHES: dict[str, Callable[[], str]] = {
     "matcher": _apply_matcher,
     "box_loss": _apply_box_loss,
     "label_loss": _apply_label_loss,
+    "fused_msda": _apply_fused_msda,
+    "fused_msda_native": _apply_fused_msda_native,
 }
 
 

@@ -27,6 +27,9 @@ def fake_rfdetr(monkeypatch):
         "rfdetr.models.matcher": types.ModuleType("rfdetr.models.matcher"),
         "rfdetr.models._assignment": types.ModuleType("rfdetr.models._assignment"),
         "rfdetr.models.criterion": types.ModuleType("rfdetr.models.criterion"),
+        "rfdetr.models.ops": types.ModuleType("rfdetr.models.ops"),
+        "rfdetr.models.ops.modules": types.ModuleType("rfdetr.models.ops.modules"),
+        "rfdetr.models.ops.modules.ms_deform_attn": types.ModuleType("rfdetr.models.ops.modules.ms_deform_attn"),
         "torch_linear_assignment": types.ModuleType("torch_linear_assignment"),
         "torch_linear_assignment.assignment": types.ModuleType("torch_linear_assignment.assignment"),
     }
@@ -35,6 +38,9 @@ def fake_rfdetr(monkeypatch):
         "SetCriterion", (), {"loss_boxes": lambda *a: "upstream", "loss_labels": lambda *a, **k: "upstream",
                              "focal_alpha": 0.25, "ia_bce_loss": True})
     mods["rfdetr.models.matcher"]._STACKED_COST_ELEMENT_LIMIT = 350_000
+    msda = mods["rfdetr.models.ops.modules.ms_deform_attn"]
+    msda.ms_deform_attn_core_pytorch = lambda *a, **k: "upstream"
+    msda.MSDeformAttn = type("MSDeformAttn", (), {"forward": lambda self, *a, **k: "upstream", "_export": False})
     mods["rfdetr.models._assignment"]._assign_padded = lambda *a: "upstream"
     mods["torch_linear_assignment.assignment"].batch_linear_assignment = lambda c: "upstream"
     mods["torch_linear_assignment"].batch_linear_assignment = lambda c: "upstream"
@@ -70,6 +76,21 @@ def test_apply_patches_rebinds_the_reference_names(fake_rfdetr):
     with pytest.raises(NotImplementedError):
         crit.loss_labels(outputs, targets, [(torch.zeros(1, dtype=torch.int64), torch.zeros(1, dtype=torch.int64))],
                          1.0)
+
+
+def test_msda_patches_rebind_core_and_forward(fake_rfdetr):
+    done = patches.apply_patches("fused_msda,fused_msda_native")
+    assert len(done) == 2
+    msda = fake_rfdetr["rfdetr.models.ops.modules.ms_deform_attn"]
+    value = torch.zeros(1, 2, 4, 5)  # [B, M, D, S] on the host: the patched core has no CPU path
+    locs6 = torch.zeros(1, 3, 2, 1, 2, 2)
+    with pytest.raises(ValueError, match="CUDA"):
+        msda.ms_deform_attn_core_pytorch(value, torch.tensor([[1, 5]]), locs6, torch.zeros(1, 3, 2, 1, 2))
+    # the export layout (rank-5 locations) keeps the original core, export mode the original forward
+    assert msda.ms_deform_attn_core_pytorch(value, None, torch.zeros(1, 3, 2, 2, 2), None) == "upstream"
+    mod = msda.MSDeformAttn()
+    mod._export = True
+    assert mod.forward() == "upstream"
 
 
 def test_unknown_patch_name_raises_keyerror():

@@ -83,6 +83,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration table (N = 1)")
     ap.add_argument("--config-cpu-seconds", type=float, default=2.0,
                     help="CPU time budget of each CPU leg of the per-configuration table")
+    ap.add_argument("--kernel", choices=["cost", "lsap", "label", "msda"], default=None,
+                    help="profiling mode: run only this kernel's workload a few times (for an ncu capture) and exit")
     return ap.parse_args()
 
 
@@ -1005,8 +1007,50 @@ def emit(line: dict) -> None:
         os.write(fd, text.encode())
 
 
+def run_kernel(name: str, workload: str = "sweep") -> None:
+    """A few launches of one kernel on its benchmark workload, for an ncu capture of that kernel:
+    cost / lsap (the workload's step, issued as two calls), label (the classification loss forward and
+    backward on the workload's pairs), msda (deformable attention forward and backward, decoder
+    geometry)."""
+    from rfdetr_training_throughput_b200 import matcher, workloads
+
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    if name in ("cost", "lsap", "label"):
+        wl = workloads.make(workload)
+        lg, bx = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)
+        pk = matcher.PackedTargets.from_list(wl.targets_on(dev), dev)
+        for _ in range(4):
+            res = matcher.match_packed(lg, bx, pk, wl.group_detr, weights=wl.weights, events={})
+            flush.zero_()
+        if name == "label":
+            from rfdetr_training_throughput_b200.loss import matched_label_losses
+
+            x = lg.clone().requires_grad_(True)
+            for _ in range(3):
+                x.grad = None
+                loss, _c = matched_label_losses(x, bx, pk, res, mode="ia_bce")
+                loss.sum().backward()
+                flush.zero_()
+    else:
+        from rfdetr_training_throughput_b200.msda import ms_deform_attn
+
+        g = torch.Generator(device="cuda").manual_seed(7)
+        shapes = torch.tensor([(36, 36), (18, 18), (9, 9)], device=dev)
+        v = torch.randn((8, 1701, 8, 32), device=dev, generator=g).requires_grad_(True)
+        loc = torch.rand((8, 300, 8, 3, 4, 2), device=dev, generator=g).requires_grad_(True)
+        w = torch.rand((8, 300, 8, 3, 4), device=dev, generator=g).requires_grad_(True)
+        for _ in range(3):
+            ms_deform_attn(v, shapes, None, loc, w).sum().backward()
+    torch.cuda.synchronize(dev)
+    print(f"kernel {name}: ok", file=sys.stderr)
+
+
 def main() -> None:
     args = parse()
+    if args.kernel is not None:
+        run_kernel(args.kernel, args.workload)
+        return
     # Everything else anything in the process writes to stdout (library banners such as NCCL's
     # version line under torchrun) goes to stderr, so stdout carries the JSON line alone.
     sys.stdout.flush()

@@ -363,7 +363,8 @@ int rfm_label_loss_backward(const float* pred_logits, const float* pred_boxes, c
  *   attention_weights   [B, Q, M, L, P] float32
  *   out                 [B, Q, M, D] float32 (= [B, Q, M * D])
  *
- * L <= 8, P <= 16.  rfm_msda_backward adds d out / d value (for grad_out) into
+ * L <= 8, P <= 16, D <= 128, S * M * D < 2^31.  rfm_msda_backward adds
+ * d out / d value (for grad_out) into
  * grad_value (the caller zeroes it; atomic adds, so its last bits may vary
  * between runs) and writes grad_locations [B, Q, M, L, P, 2] and grad_weights
  * [B, Q, M, L, P].

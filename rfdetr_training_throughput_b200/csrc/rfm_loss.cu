@@ -347,16 +347,60 @@ __global__ void __launch_bounds__(kLabelThreads) label_loss_kernel(const LabelAr
   int64_t k = k_begin + threadIdx.x;
   int64_t q_next = k < k_end ? a.query_idx[k] : -1;
   float sum = 0.0f;
-  for (int e = threadIdx.x; e < n; e += kLabelThreads) {
-    const float x = a.logits[base + e];
+  // the dense pass is elementwise over the tile's contiguous logits: a scalar
+  // head up to a 16-byte boundary, then 16-byte vectors, two in flight per
+  // thread, then a scalar tail (the gradient takes the vector path when its
+  // buffer has the logits' alignment)
+  const float* xs = a.logits + base;
+  float* gs = kBackward ? a.grad_logits + base : nullptr;
+  const auto term = [&](float x, int64_t e) {
     float loss, grad;
     label_term(a, x, false, 0.0f, loss, grad);
     if (kBackward) {
-      a.grad_logits[base + e] = g * grad;
+      gs[e] = g * grad;
     } else {
       sum += loss;
     }
+  };
+  int head = static_cast<int>((4 - ((reinterpret_cast<uintptr_t>(xs) >> 2) & 3)) & 3);
+  const bool vec = (reinterpret_cast<uintptr_t>(xs) & 3) == 0 &&
+                   (!kBackward || ((reinterpret_cast<uintptr_t>(gs) - reinterpret_cast<uintptr_t>(xs)) & 15) == 0);
+  if (!vec || head > n) head = n;
+  for (int e = threadIdx.x; e < head; e += kLabelThreads) term(xs[e], e);
+  const int n4 = (n - head) >> 2;
+  const float4* x4 = reinterpret_cast<const float4*>(xs + head);
+  for (int i = threadIdx.x; i < n4; i += 2 * kLabelThreads) {
+    const int i2 = i + kLabelThreads;
+    const float4 v0 = __ldg(x4 + i);
+    const float4 v1 = i2 < n4 ? __ldg(x4 + i2) : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (kBackward) {
+      float l, g0, g1, g2, g3;
+      label_term(a, v0.x, false, 0.0f, l, g0);
+      label_term(a, v0.y, false, 0.0f, l, g1);
+      label_term(a, v0.z, false, 0.0f, l, g2);
+      label_term(a, v0.w, false, 0.0f, l, g3);
+      reinterpret_cast<float4*>(gs + head)[i] = make_float4(g * g0, g * g1, g * g2, g * g3);
+      if (i2 < n4) {
+        label_term(a, v1.x, false, 0.0f, l, g0);
+        label_term(a, v1.y, false, 0.0f, l, g1);
+        label_term(a, v1.z, false, 0.0f, l, g2);
+        label_term(a, v1.w, false, 0.0f, l, g3);
+        reinterpret_cast<float4*>(gs + head)[i2] = make_float4(g * g0, g * g1, g * g2, g * g3);
+      }
+    } else {
+      term(v0.x, 0);
+      term(v0.y, 0);
+      term(v0.z, 0);
+      term(v0.w, 0);
+      if (i2 < n4) {
+        term(v1.x, 0);
+        term(v1.y, 0);
+        term(v1.z, 0);
+        term(v1.w, 0);
+      }
+    }
   }
+  for (int e = head + 4 * n4 + threadIdx.x; e < n; e += kLabelThreads) term(xs[e], e);
   // the pairs of (l, b), strided over the threads; only the tile's are used
   int correct = 0;
   if (kBackward) __syncthreads();  // every dense store of the tile precedes the overwrites

@@ -18,7 +18,9 @@
 //
 // Layout.  One warp computes one (b, q, m): lane d holds channel d (channels
 // beyond 32 in further passes), so each neighbour is one coalesced 128-byte row
-// of value, and the D outputs are one coalesced store.  The backward warp
+// of value, and the D outputs are one coalesced store.  The samples' neighbour
+// rows and weights are worked out once per warp, lane j for sample j, and
+// read by every lane from shared memory as broadcasts.  The backward warp
 // recomputes the samples, reduces the gradients of the sampling location and of
 // the attention weight over the channels with warp shuffles, and adds the
 // value gradient into the four neighbours with atomic adds, each lane its own
@@ -34,6 +36,7 @@ namespace {
 constexpr int kMsdaWarps = 8;
 constexpr int kMsdaMaxLevels = 8;
 constexpr int kMsdaMaxPoints = 16;
+constexpr int kMsdaMaxPasses = 4;  // head_dim <= 128: up to four channel passes of 32 lanes
 
 struct MsdaArgs {
   const float* value;    // [B, S, M, D]
@@ -86,10 +89,22 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// One sample's neighbours as the warp's lanes read them (64 bytes, four
+// 16-byte broadcasts): value rows (within the (b, m) plane, -1 outside) and
+// bilinear weights, and for the backward pass the attention weight, the
+// fractional position and the map size.
+struct SampleSlot {
+  int4 idx;
+  float4 wt;     // forward: attention weight x bilinear weight; backward: bilinear weight
+  float4 extra;  // ws, fx, fy, W
+  float4 extra2; // H
+};
+
 template <bool kBackward>
 __global__ void __launch_bounds__(32 * kMsdaWarps) msda_kernel(const MsdaArgs a) {
   __shared__ int s_h[kMsdaMaxLevels], s_w[kMsdaMaxLevels];
   __shared__ int64_t s_start[kMsdaMaxLevels];
+  __shared__ SampleSlot s_slot[kMsdaWarps][32];
   if (threadIdx.x < a.L) {
     // a level whose rows do not lie inside [0, S) is sampled as empty (every
     // neighbour outside the map), so no access leaves the value tensor
@@ -102,75 +117,114 @@ __global__ void __launch_bounds__(32 * kMsdaWarps) msda_kernel(const MsdaArgs a)
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int64_t task = static_cast<int64_t>(blockIdx.x) * kMsdaWarps + (threadIdx.x >> 5);
+  const int warp = threadIdx.x >> 5;
+  const int64_t task = static_cast<int64_t>(blockIdx.x) * kMsdaWarps + warp;
   const int64_t tasks = static_cast<int64_t>(a.B) * a.Q * a.M;
   if (task >= tasks) return;
   const int m = static_cast<int>(task % a.M);
-  const int64_t bq = task / a.M;
-  const int b = static_cast<int>(bq / a.Q);
+  const int b = static_cast<int>(task / a.M / a.Q);
   const int LP = a.L * a.P;
-  const float* loc = a.loc + task * LP * 2;
-  const float* wts = a.w + task * LP;
-  // value row (s) of head m of image b starts at ((b * S + s) * M + m) * D
+  const int passes = (a.D + 31) >> 5;  // <= kMsdaMaxPasses channel passes of 32
+  // value row s of head m of image b: value + ((b * S + s) * M + m) * D
   const int64_t row_stride = static_cast<int64_t>(a.M) * a.D;
   const float* vb = a.value + (static_cast<int64_t>(b) * a.S * a.M + m) * a.D;
-  for (int d0 = 0; d0 < a.D; d0 += 32) {
-    const int d = d0 + lane;
-    const bool on = d < a.D;
-    float acc = 0.0f;
-    const float g = (kBackward && on) ? a.grad_out[task * a.D + d] : 0.0f;
-    for (int l = 0; l < a.L; ++l) {
+  float* gvb = kBackward ? a.grad_value + (static_cast<int64_t>(b) * a.S * a.M + m) * a.D : nullptr;
+  float acc[kMsdaMaxPasses], g[kMsdaMaxPasses];
+#pragma unroll
+  for (int c = 0; c < kMsdaMaxPasses; ++c) {
+    acc[c] = 0.0f;
+    const int d = 32 * c + lane;
+    g[c] = (kBackward && c < passes && d < a.D) ? a.grad_out[task * a.D + d] : 0.0f;
+  }
+  SampleSlot* slot = s_slot[warp];
+  for (int c0 = 0; c0 < LP; c0 += 32) {
+    // lane j prepares sample c0 + j
+    const int sp = c0 + lane;
+    if (sp < LP) {
+      const int l = sp / a.P;
       const int H = s_h[l], W = s_w[l];
-      const float* vl = vb + s_start[l] * row_stride;
-      for (int p = 0; p < a.P; ++p) {
-        const int sp = l * a.P + p;
-        const float lx = __ldg(loc + 2 * sp), ly = __ldg(loc + 2 * sp + 1);
-        const float ws = __ldg(wts + sp);
-        const Corners4 c = corners_of(lx, ly, H, W);
-        float v[4];
+      const float lx = __ldg(a.loc + 2 * (task * LP + sp)), ly = __ldg(a.loc + 2 * (task * LP + sp) + 1);
+      const float ws = __ldg(a.w + task * LP + sp);
+      const Corners4 c = corners_of(lx, ly, H, W);
+      SampleSlot sl;
+      const int64_t st = s_start[l];
+      sl.idx = make_int4(c.idx[0] < 0 ? -1 : static_cast<int>(st + c.idx[0]),
+                         c.idx[1] < 0 ? -1 : static_cast<int>(st + c.idx[1]),
+                         c.idx[2] < 0 ? -1 : static_cast<int>(st + c.idx[2]),
+                         c.idx[3] < 0 ? -1 : static_cast<int>(st + c.idx[3]));
+      const float f = kBackward ? 1.0f : ws;
+      sl.wt = make_float4(f * c.wt[0], f * c.wt[1], f * c.wt[2], f * c.wt[3]);
+      sl.extra = make_float4(ws, c.fx, c.fy, static_cast<float>(W));
+      sl.extra2 = make_float4(static_cast<float>(H), 0.f, 0.f, 0.f);
+      slot[lane] = sl;
+    }
+    __syncwarp();
+    const int n = min(32, LP - c0);
+    for (int j = 0; j < n; ++j) {
+      const int4 ix = slot[j].idx;
+      const float4 wt = slot[j].wt;
+      float gw = 0.f, gx = 0.f, gy = 0.f;  // backward: this lane's channels' shares
+      float ws = 0.f, fx = 0.f, fy = 0.f;
+      if (kBackward) {
+        const float4 e = slot[j].extra;
+        ws = e.x;
+        fx = e.y;
+        fy = e.z;
+      }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[k] = (on && c.idx[k] >= 0) ? __ldg(vl + c.idx[k] * row_stride + d) : 0.0f;
-        const float sample = ((c.wt[0] * v[0] + c.wt[1] * v[1]) + c.wt[2] * v[2]) + c.wt[3] * v[3];
+      for (int c = 0; c < kMsdaMaxPasses; ++c) {
+        const int d = 32 * c + lane;
+        if (c >= passes) break;
+        const bool on = d < a.D;
+        const float v0 = (on && ix.x >= 0) ? __ldg(vb + ix.x * row_stride + d) : 0.0f;
+        const float v1 = (on && ix.y >= 0) ? __ldg(vb + ix.y * row_stride + d) : 0.0f;
+        const float v2 = (on && ix.z >= 0) ? __ldg(vb + ix.z * row_stride + d) : 0.0f;
+        const float v3 = (on && ix.w >= 0) ? __ldg(vb + ix.w * row_stride + d) : 0.0f;
+        const float sample = ((wt.x * v0 + wt.y * v1) + wt.z * v2) + wt.w * v3;
         if (!kBackward) {
-          acc += ws * sample;
+          acc[c] += sample;
         } else {
-          // d sample / dx and / dy (pixel units), then / dloc = * W and * H
-          const float gx = 1.0f - c.fx, gy = 1.0f - c.fy;
-          const float dsx = gy * (v[1] - v[0]) + c.fy * (v[3] - v[2]);
-          const float dsy = gx * (v[2] - v[0]) + c.fx * (v[3] - v[1]);
-          const float gw = warp_sum(g * sample);
-          const float glx = warp_sum(g * dsx) * ws * static_cast<float>(W);
-          const float gly = warp_sum(g * dsy) * ws * static_cast<float>(H);
-          if (lane == 0) {
-            // channel passes (D > 32) accumulate into the same slots
-            if (d0 == 0) {
-              a.grad_w[task * LP + sp] = gw;
-              a.grad_loc[(task * LP + sp) * 2] = glx;
-              a.grad_loc[(task * LP + sp) * 2 + 1] = gly;
-            } else {
-              a.grad_w[task * LP + sp] += gw;
-              a.grad_loc[(task * LP + sp) * 2] += glx;
-              a.grad_loc[(task * LP + sp) * 2 + 1] += gly;
-            }
-          }
+          const float hx = 1.0f - fx, hy = 1.0f - fy;
+          gw += g[c] * sample;
+          gx += g[c] * (hy * (v1 - v0) + fy * (v3 - v2));
+          gy += g[c] * (hx * (v2 - v0) + fx * (v3 - v1));
           if (on) {
-            const float gs = ws * g;
-            float* gvl = a.grad_value + (static_cast<int64_t>(b) * a.S * a.M + m) * a.D + s_start[l] * row_stride;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              if (c.idx[k] >= 0) atomicAdd(gvl + c.idx[k] * row_stride + d, gs * c.wt[k]);
-            }
+            const float gs = ws * g[c];
+            if (ix.x >= 0) atomicAdd(gvb + ix.x * row_stride + d, gs * wt.x);
+            if (ix.y >= 0) atomicAdd(gvb + ix.y * row_stride + d, gs * wt.y);
+            if (ix.z >= 0) atomicAdd(gvb + ix.z * row_stride + d, gs * wt.z);
+            if (ix.w >= 0) atomicAdd(gvb + ix.w * row_stride + d, gs * wt.w);
           }
         }
       }
+      if (kBackward) {
+        // sums over the channels: d out / d w, and d out / d loc = w * d sample / d (x, y) * (W, H)
+        gw = warp_sum(gw);
+        gx = warp_sum(gx);
+        gy = warp_sum(gy);
+        if (lane == 0) {
+          const int64_t k = task * LP + c0 + j;
+          a.grad_w[k] = gw;
+          a.grad_loc[2 * k] = gx * ws * slot[j].extra.w;
+          a.grad_loc[2 * k + 1] = gy * ws * slot[j].extra2.x;
+        }
+      }
     }
-    if (!kBackward && on) a.out[task * a.D + d] = acc;
+    __syncwarp();  // every lane is done with the slots before the next chunk rewrites them
+  }
+  if (!kBackward) {
+#pragma unroll
+    for (int c = 0; c < kMsdaMaxPasses; ++c) {
+      const int d = 32 * c + lane;
+      if (c < passes && d < a.D) a.out[task * a.D + d] = acc[c];
+    }
   }
 }
 
 int msda_args(MsdaArgs& a, const float* value, const int64_t* shapes, const int64_t* start, const float* loc,
               const float* w, int B, int S, int M, int D, int Q, int L, int P) {
-  if (B < 1 || S < 1 || M < 1 || D < 1 || Q < 0 || L < 1 || L > kMsdaMaxLevels || P < 1 || P > kMsdaMaxPoints ||
+  if (B < 1 || S < 1 || M < 1 || D < 1 || D > 32 * kMsdaMaxPasses || Q < 0 || L < 1 || L > kMsdaMaxLevels ||
+      P < 1 || P > kMsdaMaxPoints || static_cast<int64_t>(S) * M * D > 0x7fffffff ||
       value == nullptr || shapes == nullptr || start == nullptr ||
       (Q > 0 && (loc == nullptr || w == nullptr))) {
     return RFM_ERR_INVALID_ARGUMENT;

@@ -27,9 +27,10 @@ Keys beyond the base contract:
   per_rank_step_ms  min / median / max / mean device ms of the timed steps on
                 every rank.
 
-Timed regions start behind a short device-side delay (``torch.cuda._sleep``,
-outside the events), so the host has enqueued the first steps before the GPU
-reaches them and a late host launch cannot leave the GPU idle inside a step.
+Timed regions start behind about a millisecond of device-side work outside the
+events (writes of the L2-flush buffer, which keep the GPU busy rather than idle),
+so the host has enqueued the first steps before the GPU reaches them and a late
+host launch cannot leave the GPU idle inside a step.
 
 ``--impl reference`` times that CPU path alone, with the same thread setting as
 ``cpu_baseline``.
@@ -57,7 +58,18 @@ METRIC = "matched problems/s (cost+LSAP) at 1/2/4/8 B200; cost-kernel HBM GB/s v
 UNIT = "problems/s"
 FALLBACK_HBM_GBS = 6650.0
 L2_FLUSH_BYTES = 256 << 20
-LEAD_CYCLES = 2_000_000  # ~1 ms at 1.9 GHz of device-side delay before each timed region
+LEAD_FILLS = 25  # writes of a 256 MiB buffer (~1 ms of device-side work) before each timed region
+_LEAD_BUF: dict = {}
+
+
+def device_lead(device) -> None:
+    """About a millisecond of memory-bound device work, enqueued before a timed region: the host gets
+    ahead of the GPU, and the GPU stays busy (an idle spin before the region left its next step slow)."""
+    key = str(device)
+    if key not in _LEAD_BUF:
+        _LEAD_BUF[key] = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+    for _ in range(LEAD_FILLS):
+        _LEAD_BUF[key].zero_()
 CONFIG_NAMES = ("step", "crowd", "ties", "sweep")
 REFERENCE_POOL_THREADS = 8  # LAP_THREADS default of the parallel_lap patch (patches.py:210)
 
@@ -354,7 +366,7 @@ def time_device_steps(fn, steps: int, warmup: int, flush: torch.Tensor, device, 
     if barrier is not None:
         barrier()
     torch.cuda.synchronize(device)
-    torch.cuda._sleep(LEAD_CYCLES)
+    device_lead(device)
     for k in range(steps):
         starts[k].record()
         fn()
@@ -493,6 +505,9 @@ def run_rfm(args) -> None:
         box_loss = box_loss_timing(device, max(args.warmup, 3))
         label_loss = label_loss_timing(device, max(args.warmup, 3), wl, logits, boxes, packed)
         msda = msda_timing(device, max(args.warmup, 3))
+    cost_qmajor = None
+    if world == 1:
+        cost_qmajor = cost_query_major_timing(device, wl, logits, boxes, packed)
     lsap_batches = None
     if world == 1 and not args.no_configs:
         configs = config_table(device, args, flush, wl)
@@ -549,6 +564,7 @@ def run_rfm(args) -> None:
             "configs": configs,
             "lsap_batches": lsap_batches,
             "library": _lib.version(), "step_ms": step_stats(step_ms), "per_rank_step_ms": per_rank,
+            "step_ms_all": [round(x, 5) for x in step_ms], "cost_query_major": cost_qmajor,
         }
         emit(line)
     if world > 1:
@@ -611,6 +627,45 @@ def e2e_timing(args, wl, plan, device, barrier, world: int, problems: int) -> di
             "path": "PrefetchingMatcher: pinned H2D of step k+1 on a copy stream overlapping match + D2H of step k",
             "host_buffers": (f"pinned by a thread on the {len(local_cpus)} GPU-local CPUs NVML reports"
                              if local_cpus else "pinned without NUMA placement (NVML gave no CPU set)")}
+
+
+def cost_query_major_timing(device, wl, logits, boxes, packed, reps: int = 20) -> dict:
+    """The drop-in cost call (``compute_compact_detection_cost_matrix``, the ``triton_matcher`` patch's
+    contract: the compact ``[Q, sum T]`` query-major matrix) on the sweep, the kernel alone (C-ABI
+    calls back to back between events, behind a device-side delay), and its HBM figure."""
+    import ctypes
+
+    from rfdetr_training_throughput_b200 import _lib
+
+    L, B, Q, C = logits.shape
+    S = packed.total
+    out = torch.empty((L, Q, S), dtype=torch.float32, device=device)
+    offs = torch.tensor(np.concatenate([[0], np.cumsum(packed.sizes)]).astype(np.int32), device=device)
+    P = ctypes.c_void_p
+    stream = P(torch.cuda.current_stream(device).cuda_stream)
+    lib = _lib.load()
+    w = wl.weights
+    args = [P(logits.data_ptr()), P(boxes.data_ptr()), P(packed.labels.data_ptr()), P(packed.boxes.data_ptr()),
+            P(offs.data_ptr()), L, B, Q, C, S, S, _lib.LAYOUT_QUERY_MAJOR, float(w["cost_class"]),
+            float(w["cost_bbox"]), float(w["cost_giou"]), float(w["focal_alpha"]), P(out.data_ptr()), stream]
+    samples = []
+    for _ in range(5):
+        _lib.check("rfm_cost", lib.rfm_cost(*args))
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        device_lead(device)
+        e0.record()
+        for _ in range(reps):
+            lib.rfm_cost(*args)
+        e1.record()
+        torch.cuda.synchronize(device)
+        samples.append(e0.elapsed_time(e1) * 1e3 / reps)
+    us = statistics.median(samples)
+    peak, _kind = peak_hbm()
+    cb = cost_bytes(wl)
+    return {"what": "rfm_cost query-major (the compact [Q, sum T] matrix of the triton_matcher patch), sweep",
+            "us_per_launch": us, "achieved_gbs": cb / us / 1e3, "frac_of_hbm": cb / us / 1e3 / peak,
+            "timing": f"{reps} launches back to back per sample, median of 5 (no L2 flush between launches)"}
 
 
 def production_step_timing(device, warmup: int, steps: int = 200) -> dict:
@@ -817,7 +872,7 @@ def label_loss_timing(device, warmup: int, sweep_wl, sweep_logits, sweep_boxes, 
             fn()
             torch.cuda.synchronize(device)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda._sleep(LEAD_CYCLES)
+            device_lead(device)
             e0.record()
             for _ in range(rep):
                 fn()
@@ -915,7 +970,7 @@ def time_solver(fn, cost: torch.Tensor, device, rep: int = 5) -> float:
     ms = []
     for _ in range(rep):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda._sleep(LEAD_CYCLES // 4)
+        device_lead(device)
         e0.record()
         fn(cost)
         e1.record()

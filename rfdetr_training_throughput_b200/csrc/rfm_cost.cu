@@ -19,15 +19,10 @@
 // per-thread tiles do.
 //
 // QUERY-MAJOR (the compact matrix itself, out[l][q][col]) serves the drop-in
-// cost-matrix call.  Each thread owns four consecutive columns of the output (one
-// 16-byte vector) and walks a strip of rows.  The target data of its columns
-// (box, xyxy corners, area, clamped label, owning image) is loaded once into
-// registers and reused for every row; the per-(image, query) prediction data
-// (box and the logit at the target's class) comes through L1, where the
-// neighbouring columns of the same image hit it again.  Stores are 128-bit,
-// coalesced along the row when the row stride ld is a multiple of 4 (every
-// row then starts 16-byte aligned; the caller pads ld and the pad columns are
-// written with 0); any other ld takes a scalar-store variant.
+// cost-matrix call.  The same kernel computes the same tiles (32 target rows x
+// 256 queries) into shared memory instead, query-major, and then writes each
+// query row's 32 columns out as one coalesced store; any ld >= S is accepted
+// and the pad columns are written with 0.
 //
 // Arithmetic.  Every operation is explicitly rounded: scalar add/sub/mul.rn,
 // packed f32x2 ops (same per-lane rounding) and explicit FMAs.  ptxas contracts
@@ -38,15 +33,13 @@
 // reference chain (kernels_matcher.py:98-120); the hull extents use the interval
 // identity max(a1,b1) - min(a0,b0) = (a1-a0) + (b1-b0) - (min(a1,b1) -
 // max(a0,b0)); quotients are a * rcp(b); the focal term uses fast exp/log.  All
-// of it is well inside the 1e-5 relative bar, and both layouts evaluate the same
-// operations, so they produce bit-identical matrices.
+// of it is well inside the 1e-5 relative bar, and both layouts come out of the
+// same code, so they hold bit-identical matrices.
 #include "rfm_common.cuh"
 
 namespace rfm {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kRowsPerThread = 8;
 constexpr float kBoxEps = 1e-7f;  // kernels_matcher.py:53
 
 struct CostArgs {
@@ -57,7 +50,6 @@ struct CostArgs {
   const int32_t* offsets;  // [B + 1]
   int B, Q, C, S;
   int64_t ld;
-  int rows_per_cta;
   float w_class, w_bbox, w_giou, alpha, alpha_m1;
   float* out;            // [L, Q, ld]
   int* reset_word;       // target-major only: set to 0 by one thread (a solver counter), or null
@@ -111,36 +103,6 @@ __device__ __forceinline__ float focal_cost(float x, float alpha, float alpha_m1
   const float mneg = __fsub_rn(l, fminf(-x, 0.0f));
   const float nneg = __fmul_rn(__fmul_rn(alpha_m1, __fmul_rn(p, p)), mneg);
   return __fmaf_rn(__fmul_rn(alpha, __fmul_rn(q, q)), mpos, nneg);
-}
-
-// cost_bbox * l1 + w_class_cost + cost_giou * (-giou), evaluated as
-// fma(-cost_giou, giou, fma(cost_bbox, l1, w_class_cost)) in every kernel.
-__device__ __forceinline__ float combine(float l1, float giou, float wcls, const CostArgs& a) {
-  return __fmaf_rn(-a.w_giou, giou, __fmaf_rn(a.w_bbox, l1, wcls));
-}
-
-__device__ __forceinline__ float pair_cost(const float4 pb, const Corners& pc, const float4 tb,
-                                           const Corners& tc, float wcls, const CostArgs& a) {
-  // torch.cdist(p=1) over the four cxcywh coordinates (kernels_matcher.py:98-103)
-  const float l1 = __fadd_rn(
-      __fadd_rn(__fadd_rn(fabsf(__fsub_rn(pb.x, tb.x)), fabsf(__fsub_rn(pb.y, tb.y))),
-                fabsf(__fsub_rn(pb.z, tb.z))),
-      fabsf(__fsub_rn(pb.w, tb.w)));
-  // GIoU with clamped union and hull (kernels_matcher.py:118-127)
-  const float iw = __fsub_rn(fminf(pc.x1, tc.x1), fmaxf(pc.x0, tc.x0));
-  const float ih = __fsub_rn(fminf(pc.y1, tc.y1), fmaxf(pc.y0, tc.y0));
-  const float iwc = fmaxf(iw, 0.0f);
-  const float ihc = fmaxf(ih, 0.0f);
-  const float inter = __fmul_rn(iwc, ihc);
-  const float uni = __fmaf_rn(-iwc, ihc, __fadd_rn(pc.area, tc.area));
-  // hull extent = width_p + width_t - intersection extent (an identity for intervals)
-  const float ewc = fmaxf(__fsub_rn(__fadd_rn(__fsub_rn(pc.x1, pc.x0), __fsub_rn(tc.x1, tc.x0)), iw), 0.0f);
-  const float ehc = fmaxf(__fsub_rn(__fadd_rn(__fsub_rn(pc.y1, pc.y0), __fsub_rn(tc.y1, tc.y0)), ih), 0.0f);
-  const float hull = __fmul_rn(ewc, ehc);
-  const float gap = __fmaf_rn(ewc, ehc, -uni);
-  const float iou = __fmul_rn(inter, rcp_approx(fmaxf(uni, kBoxEps)));
-  const float giou = __fmaf_rn(-gap, rcp_approx(fmaxf(hull, kBoxEps)), iou);
-  return combine(l1, giou, wcls, a);
 }
 
 // Largest image b in [lo, hi) with offsets[b] <= col, given offsets[lo] <= col
@@ -200,74 +162,11 @@ __device__ __forceinline__ int image_in_window(const int* s_off, int lo, const i
   return lo + l;
 }
 
-template <bool kVec>
-__global__ void __launch_bounds__(kThreads) cost_qmajor_kernel(const CostArgs a) {
-  __shared__ int s_off[kImageWindow + 1];
-  const int64_t col0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
-  const int64_t cta_col = static_cast<int64_t>(blockIdx.x) * blockDim.x * 4;
-  const int tid = threadIdx.y * blockDim.x + threadIdx.x;
-  int win_lo = 0;
-  if (cta_col < a.S) {  // uniform across the CTA
-    win_lo = stage_image_window(a.offsets, a.B, static_cast<int>(cta_col), s_off, tid, kThreads);
-  }
-  if (col0 >= a.ld) return;
-  const int layer = blockIdx.z;
-  const int q_begin = blockIdx.y * a.rows_per_cta;
-  const int q_end = min(a.Q, q_begin + a.rows_per_cta);
-
-  float4 tb[4];
-  Corners tc[4];
-  int label[4], image[4];
-  bool valid[4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int64_t col = col0 + c;
-    valid[c] = col < a.S;
-    if (valid[c]) {
-      image[c] = image_in_window(s_off, win_lo, a.offsets, a.B, static_cast<int>(col));
-      tb[c] = __ldg(a.tboxes + col);
-      const int64_t raw = __ldg(a.labels + col);
-      label[c] = static_cast<int>(raw < 0 ? 0 : (raw >= a.C ? a.C - 1 : raw));
-      tc[c] = corners(tb[c]);
-    } else {
-      image[c] = 0;
-      label[c] = 0;
-      tb[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-      tc[c] = Corners{0.f, 0.f, 0.f, 0.f, 0.f};
-    }
-  }
-  const int64_t layer_base = static_cast<int64_t>(layer) * a.B;
-
-  for (int q = q_begin + threadIdx.y; q < q_end; q += blockDim.y) {
-    float r[4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      r[c] = 0.0f;
-      if (valid[c]) {
-        const int64_t pq = (layer_base + image[c]) * a.Q + q;
-        const float4 pb = __ldg(a.pboxes + pq);
-        const float x = __ldg(a.logits + pq * a.C + label[c]);
-        r[c] = pair_cost(pb, corners(pb), tb[c], tc[c],
-                         __fmul_rn(a.w_class, focal_cost(x, a.alpha, a.alpha_m1)), a);
-      }
-    }
-    float* dst = a.out + (static_cast<int64_t>(layer) * a.Q + q) * a.ld + col0;
-    if (kVec) {
-      *reinterpret_cast<float4*>(dst) = make_float4(r[0], r[1], r[2], r[3]);
-    } else {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (col0 + c < a.ld) dst[c] = r[c];
-      }
-    }
-  }
-}
-
-
 constexpr int kTmThreads = 128;  // 2 queries each: 256 queries per CTA
 constexpr int kQpt = 2;          // queries per thread (one f32x2 pair)
 constexpr int kTmCols = 64;      // target rows per CTA (may span several images)
 constexpr int kTmColsSmall = 8;  // ... for batches too small to fill the GPU twice with 64-row CTAs
+constexpr int kQmCols = 32;      // target rows per CTA in the query-major layout (its tile is in shared memory)
 constexpr int kSmallClasses = 4;
 
 // Packed float32 pairs: two queries per instruction (sm_100 f32x2 pipe), each
@@ -417,14 +316,16 @@ __device__ __forceinline__ void load_raw(PredRaw<NCLS>& r, const CostArgs& a, in
 }
 
 // Costs of targets [c_begin, c_end) of one image run against the thread's two
-// queries, one 8-byte store per target row.
-template <int NCLS, bool kUnclamped, bool kTail>
+// queries: one 8-byte store per target row of the target-major matrix, or
+// (kQM) two 4-byte stores into the CTA's query-major shared-memory tile.
+template <int NCLS, bool kUnclamped, bool kTail, bool kQM>
 __device__ __forceinline__ void cost_targets(const TargetRow* s_t, int c_begin, int c_end, float* out_row,
                                              const PredPair& p01, const float2 (&wcls01)[kSmallClasses],
-                                             int q0, int64_t pbase, const CostArgs& a) {
-  float* dst = out_row + static_cast<int64_t>(c_begin) * a.ld;
+                                             int q0, int64_t pbase, const CostArgs& a, float* tile, int pitch) {
+  float* dst = kQM ? tile + c_begin : out_row + static_cast<int64_t>(c_begin) * a.ld;
+  const int64_t step = kQM ? 1 : a.ld;
 #pragma unroll 2
-  for (int c = c_begin; c < c_end; ++c, dst += a.ld) {
+  for (int c = c_begin; c < c_end; ++c, dst += step) {
     const TargetRow t = s_t[c];
     float2 w01;
     if (NCLS > 0) {
@@ -442,21 +343,49 @@ __device__ __forceinline__ void cost_targets(const TargetRow* s_t, int c_begin, 
       w01 = make_float2(f[0], f[1]);
     }
     float2 r01 = pair_cost2<kUnclamped>(p01, t, w01, a);
-    if (kTail && q0 + 2 > a.Q) {  // zero the pad queries (q >= Q, up to ld) of the last tile
-      if (q0 >= a.Q) r01.x = 0.f;
-      r01.y = 0.f;
+    if (kQM) {  // rows of queries q0 and q0 + 1 of the tile (a query past Q is never written out)
+      dst[0] = r01.x;
+      dst[pitch] = r01.y;
+    } else {
+      if (kTail && q0 + 2 > a.Q) {  // zero the pad queries (q >= Q, up to ld) of the last tile
+        if (q0 >= a.Q) r01.x = 0.f;
+        r01.y = 0.f;
+      }
+      *reinterpret_cast<float2*>(dst) = r01;
     }
-    *reinterpret_cast<float2*>(dst) = r01;
   }
 }
 
-template <int NCLS, int kCols>
+// One CTA: kCols consecutive target rows x 256 queries.  Target-major: every
+// cost goes straight to its row.  Query-major (kQM, the compact [Q, ld] matrix):
+// the tile is built in shared memory, query-major with a pitch of kCols + 1
+// floats, then each query row's kCols costs leave as one coalesced store of
+// consecutive columns; a CTA past the last target only zeroes its pad columns.
+// The arithmetic is the same in both, so the two layouts hold identical bits.
+template <int NCLS, int kCols, bool kQM>
 __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs a) {
   // A solver launched after this kernel with programmatic stream serialization
   // may start its prologue now; it waits for this grid's completion (and its
   // stores) before it reads the matrix.
   asm volatile("griddepcontrol.launch_dependents;");
-  if (a.reset_word != nullptr && (blockIdx.x | blockIdx.y | blockIdx.z | threadIdx.x) == 0) *a.reset_word = 0;
+  if (!kQM && a.reset_word != nullptr && (blockIdx.x | blockIdx.y | blockIdx.z | threadIdx.x) == 0) {
+    *a.reset_word = 0;
+  }
+  constexpr int kPitch = kCols + 1;
+  __shared__ float s_tile[kQM ? kQpt * kTmThreads * kPitch : 1];
+  if (kQM && static_cast<int64_t>(blockIdx.x) * kCols >= a.S) {
+    // pad columns only: zero [c_begin, min(c_begin + kCols, ld)) of every query row of the tile
+    const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kCols;
+    const int width = static_cast<int>(min(static_cast<int64_t>(kCols), a.ld - c0));
+    const int qt0 = blockIdx.y * kTmThreads * kQpt;
+    for (int e = threadIdx.x; e < kTmThreads * kQpt * kCols; e += kTmThreads) {
+      const int ql = e / kCols, c = e - ql * kCols;
+      if (c < width && qt0 + ql < a.Q) {
+        a.out[(static_cast<int64_t>(blockIdx.z) * a.Q + qt0 + ql) * a.ld + c0 + c] = 0.0f;
+      }
+    }
+    return;
+  }
   __shared__ TargetRow s_t[kCols];
   __shared__ int s_seg[kCols + 1];
   __shared__ int s_nseg;
@@ -520,10 +449,11 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
     }
   }
   __syncthreads();
-  if (q0 >= a.ld) return;
-  const int nseg = s_nseg;
+  if (!kQM && q0 >= a.ld) return;
+  const int nseg = (kQM && q0 >= a.Q) ? 0 : s_nseg;  // query-major: queries past Q are not computed
   const bool all_plain = s_all_plain != 0;
-  float* out_row = a.out + (static_cast<int64_t>(layer) * a.S + c_begin) * a.ld + q0;
+  float* out_row = kQM ? nullptr : a.out + (static_cast<int64_t>(layer) * a.S + c_begin) * a.ld + q0;
+  float* tile_row = s_tile + (kQM ? tid * kQpt * kPitch : 0);
   for (int sg = 0; sg < nseg; ++sg) {
     const int img = s_t[s_seg[sg]].image;
     const int64_t pbase = (layer_base + img) * a.Q;
@@ -544,21 +474,35 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
     // one uniform choice per image run: clamp-free when every box of the run is
     // plain, pad-query zeroing only in the last query tile
     if (preds_plain && all_plain && q0 + 2 <= a.Q) {
-      cost_targets<NCLS, true, false>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, wcls01, q0, pbase, a);
+      cost_targets<NCLS, true, false, kQM>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, wcls01, q0, pbase, a,
+                                          tile_row, kPitch);
     } else {
-      cost_targets<NCLS, false, true>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, wcls01, q0, pbase, a);
+      cost_targets<NCLS, false, true, kQM>(s_t, s_seg[sg], s_seg[sg + 1], out_row, p01, wcls01, q0, pbase, a,
+                                          tile_row, kPitch);
+    }
+  }
+  if (kQM) {
+    // the tile out, query-major: warp w writes query rows w, w + 4, ...; lane c
+    // column c_begin + c (the row's real columns, then its pad columns with 0)
+    __syncthreads();
+    const int width = static_cast<int>(min(static_cast<int64_t>(kCols), a.ld - c_begin));
+    const int qt0 = blockIdx.y * kTmThreads * kQpt;
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int ql = warp; ql < kTmThreads * kQpt && qt0 + ql < a.Q; ql += kTmThreads / 32) {
+      float* dst = a.out + (static_cast<int64_t>(layer) * a.Q + qt0 + ql) * a.ld + c_begin;
+      for (int c = lane; c < width; c += 32) dst[c] = c < n ? s_tile[ql * kPitch + c] : 0.0f;
     }
   }
 }
 
-template <int kCols>
+template <int kCols, bool kQM>
 void launch_tmajor(const CostArgs& a, dim3 grid, int num_classes, cudaStream_t stream) {
   switch (num_classes) {
-    case 1: cost_tmajor_kernel<1, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
-    case 2: cost_tmajor_kernel<2, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
-    case 3: cost_tmajor_kernel<3, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
-    case 4: cost_tmajor_kernel<4, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
-    default: cost_tmajor_kernel<0, kCols><<<grid, kTmThreads, 0, stream>>>(a); break;
+    case 1: cost_tmajor_kernel<1, kCols, kQM><<<grid, kTmThreads, 0, stream>>>(a); break;
+    case 2: cost_tmajor_kernel<2, kCols, kQM><<<grid, kTmThreads, 0, stream>>>(a); break;
+    case 3: cost_tmajor_kernel<3, kCols, kQM><<<grid, kTmThreads, 0, stream>>>(a); break;
+    case 4: cost_tmajor_kernel<4, kCols, kQM><<<grid, kTmThreads, 0, stream>>>(a); break;
+    default: cost_tmajor_kernel<0, kCols, kQM><<<grid, kTmThreads, 0, stream>>>(a); break;
   }
 }
 
@@ -628,28 +572,27 @@ int cost_run(const float* pred_logits, const float* pred_boxes, const int64_t* t
     const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy),
                     static_cast<unsigned>(num_layers));
     if (small) {
-      launch_tmajor<kTmColsSmall>(a, grid, num_classes, as_stream(stream));
+      launch_tmajor<kTmColsSmall, false>(a, grid, num_classes, as_stream(stream));
     } else {
-      launch_tmajor<kTmCols>(a, grid, num_classes, as_stream(stream));
+      launch_tmajor<kTmCols, false>(a, grid, num_classes, as_stream(stream));
     }
     return launch_status();
   }
 
-  const int64_t chunks = (ld + 3) / 4;
-  int tx = 1;
-  while (tx < chunks && tx < 64) tx <<= 1;
-  const int ty = kThreads / tx;
-  a.rows_per_cta = ty * kRowsPerThread;
-  const int64_t gx = (chunks + tx - 1) / tx;
-  const int64_t gy = (num_queries + a.rows_per_cta - 1) / a.rows_per_cta;
-  if (gx > 0x7fffffff || gy > 65535) return RFM_ERR_UNSUPPORTED;
-  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy),
-                  static_cast<unsigned>(num_layers));
-  const dim3 block(tx, ty, 1);
-  if ((ld & 3) == 0 && aligned16(out)) {
-    cost_qmajor_kernel<true><<<grid, block, 0, as_stream(stream)>>>(a);
+  // query-major: the same tiles (32 target rows, or 8 for small batches) computed
+  // into shared memory and written out transposed; the grid covers every column
+  // up to ld so the pad columns are zeroed
+  const int64_t gy = (static_cast<int64_t>(num_queries) + kQpt * kTmThreads - 1) / (kQpt * kTmThreads);
+  const int64_t gx_big = (static_cast<int64_t>(sum_targets) + kQmCols - 1) / kQmCols;
+  const bool small = gx_big * gy * num_layers < 2 * static_cast<int64_t>(device_sm_count());
+  const int cols = small ? kTmColsSmall : kQmCols;
+  const int64_t gx = (ld + cols - 1) / cols;
+  if (gy > 65535 || gx > 0x7fffffff) return RFM_ERR_UNSUPPORTED;
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(num_layers));
+  if (small) {
+    launch_tmajor<kTmColsSmall, true>(a, grid, num_classes, as_stream(stream));
   } else {
-    cost_qmajor_kernel<false><<<grid, block, 0, as_stream(stream)>>>(a);
+    launch_tmajor<kQmCols, true>(a, grid, num_classes, as_stream(stream));
   }
   return launch_status();
 }

@@ -85,7 +85,8 @@ constexpr int kMaxWarpsPerCta = 4;
 // memory an SM gives one or two CTAs, the load pass keeps as many of the
 // problem's rows there as fit, and warp 0's searches read those rows from shared
 // memory (the rest from L2), each scan's row requested early as in EARLY.
-enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2, kVarCoop = 3, kVarStage = 4 };
+// MULTI is STAGE with the searches spread over the CTA's four warps.
+enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2, kVarCoop = 3, kVarStage = 4, kVarMulti = 5 };
 constexpr int kEarlyMinRows = 64;
 // Batches of long problems (EARLY) with at most this many problems per SM run as STAGE.
 constexpr int kStageCtasPerSm = 2;
@@ -105,6 +106,10 @@ constexpr int kCtaBudget = kSmemPerSm / 4 - kSmemPerCtaReserved;
 // kKeyBase + pos, so the smallest key is SciPy's pick among equal path costs.
 constexpr unsigned kKeyBase = 1024u;
 constexpr unsigned kNoKey = 0xffffffffu;
+// In the search's registers a key is (tie key << kColBits) | column, so the
+// warp's argmin names the column without a lookup in `remaining`.
+constexpr int kColBits = 10;
+constexpr unsigned kColMask = (1u << kColBits) - 1u;
 // Persistent launches keep their problem counter at the start of the workspace.
 constexpr int64_t kQueueBytes = 256;
 
@@ -240,32 +245,64 @@ __device__ __forceinline__ void load_row(const float* row, int lane, unsigned ma
 // trip, not one per column).  Column duals and tie keys come from registers,
 // or in the wide layout from shared memory (every remaining column's key is
 // read, so the (cost, key) comparison compiles to selects, not branches).
+//
+// The step is branch-free: every column's reduced cost is computed (removed
+// columns are masked out afterwards), so the K chains of float64 arithmetic
+// overlap, and the lane's lexicographic (path cost, key) minimum is a tree of
+// depth log2(K) instead of a chain of K compares.  Keys are unique, so any
+// reduction order gives the same minimum.  The key carries the column in its
+// low kColBits bits (tie order is decided by the position bits above them).
 template <int K, bool kWide>
 __device__ __forceinline__ void scan_row(const float (&cf)[K], int lane, int i, double minv, double ui,
                                          const double (&v)[K], const double* v_s, double (&spc)[K],
                                          const unsigned (&key)[K], const uint16_t* key_s, unsigned rem,
                                          int16_t* path_s, double& bv, unsigned& bk) {
+  if constexpr (K > 10) {  // 1024 columns: the per-lane arrays leave no registers for the tree
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    if (rem & (1u << k)) {
-      const int j = lane + 32 * k;
-      const double r = ((minv + static_cast<double>(cf[k])) - ui) - (kWide ? v_s[j] : v[k]);
-      if (r < spc[k]) {
-        spc[k] = r;
-        path_s[j] = static_cast<int16_t>(i);
-      }
-      const unsigned kj = kWide ? static_cast<unsigned>(key_s[j]) : key[k];
-      if (spc[k] < bv || (spc[k] == bv && kj < bk)) {
-        bv = spc[k];
-        bk = kj;
+    for (int k = 0; k < K; ++k) {
+      if (rem & (1u << k)) {
+        const int j = lane + 32 * k;
+        const double r = ((minv + static_cast<double>(cf[k])) - ui) - (kWide ? v_s[j] : v[k]);
+        if (r < spc[k]) {
+          spc[k] = r;
+          path_s[j] = static_cast<int16_t>(i);
+        }
+        const unsigned kj =
+            kWide ? (static_cast<unsigned>(key_s[j]) << kColBits) | static_cast<unsigned>(j) : key[k];
+        if (spc[k] < bv || (spc[k] == bv && kj < bk)) {
+          bv = spc[k];
+          bk = kj;
+        }
       }
     }
+  } else {
+    double rv[K];
+    unsigned rk[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int j = lane + 32 * k;
+      const bool live = (rem >> k) & 1u;
+      const double r = ((minv + static_cast<double>(cf[k])) - ui) - (kWide ? v_s[j] : v[k]);
+      const bool better = live && r < spc[k];
+      if (better) path_s[j] = static_cast<int16_t>(i);
+      spc[k] = better ? r : spc[k];
+      rv[k] = live ? spc[k] : CUDART_INF;
+      rk[k] = live ? (kWide ? (static_cast<unsigned>(key_s[j]) << kColBits) | static_cast<unsigned>(j) : key[k])
+                   : kNoKey;
+    }
+#pragma unroll
+    for (int stride = 1; stride < K; stride *= 2) {
+#pragma unroll
+      for (int k = 0; k + stride < K; k += 2 * stride) {
+        const bool take = rv[k + stride] < rv[k] || (rv[k + stride] == rv[k] && rk[k + stride] < rk[k]);
+        rv[k] = take ? rv[k + stride] : rv[k];
+        rk[k] = take ? rk[k + stride] : rk[k];
+      }
+    }
+    bv = rv[0];
+    bk = rk[0];
   }
 }
-
-
-
-
 
 // Order-preserving map of a float (NaN excluded) onto uint32.
 __device__ __forceinline__ unsigned ordered32(float x) {
@@ -322,6 +359,240 @@ __device__ __forceinline__ int claim_next(const LsapArgs& a, int lane) {
   return (a.queue != nullptr && lane == 0) ? atomicAdd(a.queue, 1) + a.claim_base : 0;
 }
 
+// MULTI: the searches of one problem run on all four warps of its CTA.  Thread
+// t owns columns t, t + 128, t + 256 (K3 of them), so a scan step is K3
+// columns per thread instead of up to ten per lane; each warp reduces its
+// (path cost, key) minimum with redux.sync, lane 0 posts it to a shared slot
+// (double-buffered by step parity, so one barrier per step suffices: a warp
+// can only overwrite a slot after every warp has passed the next barrier, which
+// it reaches after reading the slot), and every thread combines the four posts.
+// Every thread then holds the same argmin, so the rest of the step (next row,
+// swap-with-last removal of `remaining`, the tie key of the moved column) runs
+// without further exchange.  Same arithmetic and tie rule as the one-warp
+// search: the result is identical.
+struct MultiShared {
+  double* u;
+  double* pick_m;
+  int16_t* col4row;
+  int16_t* pick_w;
+  int16_t* row4col;
+  int16_t* path;
+  int16_t* rem;
+  unsigned* vis;   // visited-column bitmap of the last search (bit j & 31 of word j >> 5)
+  double* post_v;  // [2][4] step posts
+  unsigned* post_k;
+  int* flag;
+};
+constexpr int kMultiPostBytes = 128;
+
+template <int K3>
+__device__ __forceinline__ void multi_row(const float* row, int t, unsigned mask, float (&cf)[K3]) {
+#pragma unroll
+  for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? row[t + 128 * k] : 0.0f;
+}
+
+template <int K3>
+__device__ __forceinline__ void multi_row_global(const float* row, int t, unsigned mask, float (&cf)[K3]) {
+#pragma unroll
+  for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? __ldg(row + t + 128 * k) : 0.0f;
+}
+
+// Searches and commits every row of a problem whose costs are staged (rows
+// [0, staged) at `tile`, pitch nc) or read from `src` (row pitch rs).  Called by
+// all 128 threads after the load pass; returns the problem's status.
+template <int K3>
+__device__ int multi_search(const MultiShared& m, const float* tile, const float* src, int64_t rs, int staged,
+                            int nr, int nc, bool bad) {
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int warp = t >> 5;
+  unsigned valid = 0;
+#pragma unroll
+  for (int k = 0; k < K3; ++k) {
+    if (t + 128 * k < nc) valid |= 1u << k;
+  }
+  unsigned freem = valid;
+  double v[K3];
+#pragma unroll
+  for (int k = 0; k < K3; ++k) v[k] = 0.0;
+  int code = bad ? RFM_STATUS_INVALID : RFM_STATUS_OK;
+  int parity = 0;
+
+  for (int cur = 0; cur < nr && code == RFM_STATUS_OK; ++cur) {
+    const int w = m.pick_w[cur];
+    if (w >= 0 && m.row4col[w] < 0) {  // still valid: commit the trivial augmentation
+      const double mv = m.pick_m[cur];
+      __syncthreads();  // every thread has read row4col[w] before it changes
+      if (t == 0) {
+        m.u[cur] += mv;
+        m.row4col[w] = static_cast<int16_t>(cur);
+        m.col4row[cur] = static_cast<int16_t>(w);
+      }
+      if ((w & 127) == t) freem &= ~(1u << (w >> 7));
+      __syncthreads();
+      continue;
+    }
+
+    double spc[K3];
+    unsigned key[K3];
+#pragma unroll
+    for (int k = 0; k < K3; ++k) {
+      const int j = t + 128 * k;
+      const unsigned pos = static_cast<unsigned>(nc - 1 - j);
+      spc[k] = CUDART_INF;
+      const unsigned kv = (freem & (1u << k)) ? kKeyBase - 1u - pos : kKeyBase + pos;
+      key[k] = (kv << kColBits) | static_cast<unsigned>(j);
+      if (j < nc) m.rem[nc - 1 - j] = static_cast<int16_t>(j);
+    }
+    unsigned rem = valid;
+    int i = cur;
+    int nrem = nc;
+    int sink = -1;
+    double minv = 0.0;
+    float cf[K3];
+    const auto issue_row = [&](int r) {
+      if (r < staged) {
+        multi_row<K3>(tile + r * nc, t, rem, cf);
+      } else {
+        multi_row_global<K3>(src + r * rs, t, rem, cf);
+      }
+    };
+    issue_row(cur);
+    __syncthreads();  // `remaining` is initialised
+    for (int it = 0; it < nc; ++it) {
+      const double ui = m.u[i];
+      double bv = CUDART_INF;
+      unsigned bk = kNoKey;
+      {
+        double rv[K3];
+        unsigned rk[K3];
+#pragma unroll
+        for (int k = 0; k < K3; ++k) {
+          const int j = t + 128 * k;
+          const bool live = (rem >> k) & 1u;
+          const double r = ((minv + static_cast<double>(cf[k])) - ui) - v[k];
+          const bool better = live && r < spc[k];
+          if (better) m.path[j] = static_cast<int16_t>(i);
+          spc[k] = better ? r : spc[k];
+          rv[k] = live ? spc[k] : CUDART_INF;
+          rk[k] = live ? key[k] : kNoKey;
+        }
+#pragma unroll
+        for (int stride = 1; stride < K3; stride *= 2) {
+#pragma unroll
+          for (int k = 0; k + stride < K3; k += 2 * stride) {
+            const bool take = rv[k + stride] < rv[k] || (rv[k + stride] == rv[k] && rk[k + stride] < rk[k]);
+            rv[k] = take ? rv[k + stride] : rv[k];
+            rk[k] = take ? rk[k + stride] : rk[k];
+          }
+        }
+        bv = rv[0];
+        bk = rk[0];
+      }
+      warp_argmin(bv, bk);
+      if (lane == 0) {
+        m.post_v[parity * 4 + warp] = bv;
+        m.post_k[parity * 4 + warp] = bk;
+      }
+      __syncthreads();
+      bv = m.post_v[parity * 4];
+      bk = m.post_k[parity * 4];
+#pragma unroll
+      for (int q = 1; q < kMaxWarpsPerCta; ++q) {
+        const double ov = m.post_v[parity * 4 + q];
+        const unsigned ok = m.post_k[parity * 4 + q];
+        const bool take = ov < bv || (ov == bv && ok < bk);
+        bv = take ? ov : bv;
+        bk = take ? ok : bk;
+      }
+      parity ^= 1;
+      if (bv == CUDART_INF) {
+        code = RFM_STATUS_INFEASIBLE;
+        break;
+      }
+      const int js = static_cast<int>(bk & kColMask);
+      const int rj = m.row4col[js];
+      if (rj >= 0) issue_row(rj);  // the next scan's row, before this step's bookkeeping
+      const unsigned tk = bk >> kColBits;
+      const int ps = static_cast<int>(tk < kKeyBase ? kKeyBase - 1u - tk : tk - kKeyBase);
+      // swap-with-last removal; the write is read after the next step's barrier
+      const int jl = m.rem[nrem - 1];
+      if (t == 0) m.rem[ps] = static_cast<int16_t>(jl);
+      if ((jl & 127) == t) {
+        const int kl = jl >> 7;
+        const unsigned kv = ((freem >> kl) & 1u) ? kKeyBase - 1u - ps : kKeyBase + ps;
+#pragma unroll
+        for (int k = 0; k < K3; ++k) {
+          if (k == kl) key[k] = (kv << kColBits) | static_cast<unsigned>(jl);
+        }
+      }
+      if ((js & 127) == t) rem &= ~(1u << (js >> 7));
+      --nrem;
+      minv = bv;
+      if (rj < 0) {
+        sink = js;
+        break;
+      }
+      i = rj;
+    }
+    if (code != RFM_STATUS_OK) break;
+    if (sink < 0) {
+      code = RFM_STATUS_NO_SINK;
+      break;
+    }
+
+    // dual update over the tree: every read of u in the search came before the
+    // last step's barrier, and each visited column's row is updated by its owner
+    const unsigned visited = valid & ~rem;
+    bool raised = false;
+#pragma unroll
+    for (int k = 0; k < K3; ++k) {
+      if (visited & (1u << k)) {
+        const int j = t + 128 * k;
+        const double d = minv - spc[k];
+        raised |= d < 0.0;
+        if (j != sink) m.u[m.row4col[j]] += d;
+        v[k] -= d;
+      }
+    }
+    if (t == 0) m.u[cur] += minv;
+    raised = __syncthreads_or(raised) != 0;  // also publishes path, u and v
+
+    if (t == 0) {
+      int flipped = 0;
+      int j = sink;
+      for (int step = 0; step <= nr; ++step) {
+        const int ii = m.path[j];
+        m.row4col[j] = static_cast<int16_t>(ii);
+        const int prev = m.col4row[ii];
+        m.col4row[ii] = static_cast<int16_t>(j);
+        j = prev;
+        if (ii == cur) {
+          flipped = 1;
+          break;
+        }
+      }
+      *m.flag = flipped;
+    }
+    if ((sink & 127) == t) freem &= ~(1u << (sink >> 7));
+#pragma unroll
+    for (int k = 0; k < K3; ++k) {
+      const unsigned b = __ballot_sync(kFullMask, (visited >> k) & 1u);
+      if (lane == 0) m.vis[warp + 4 * k] = raised ? 0xffffffffu : b;
+    }
+    __syncthreads();
+    if (*m.flag == 0) code = RFM_STATUS_NO_SINK;
+    // drop the pending picks this search visited (all of them if a dual went down)
+    for (int r = cur + 1 + t; r < nr; r += 32 * kMaxWarpsPerCta) {
+      const int pw = m.pick_w[r];
+      if (pw >= 0 && ((m.vis[pw >> 5] >> (pw & 31)) & 1u)) m.pick_w[r] = -1;
+    }
+    __syncthreads();
+  }
+  __syncthreads();
+  return code;
+}
+
 // Solves problem p with the warp's shared-memory slot at `base` (`slot` bytes).
 // Returns, in lane 0, the next problem a persistent warp claimed.
 template <int K, bool kDense, int kVariant>
@@ -329,7 +600,8 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
                                              int lane) {
   constexpr int kCols = 32 * K;
   constexpr bool kWide = kVariant == kVarWide;
-  constexpr bool kStage = kVariant == kVarStage;
+  constexpr bool kMulti = kVariant == kVarMulti;
+  constexpr bool kStage = kVariant == kVarStage || kMulti;
   constexpr bool kEarly = kVariant == kVarEarly || kStage;
   constexpr bool kCoop = kVariant == kVarCoop || kStage;
   constexpr int kLoadWarps = kCoop ? kMaxWarpsPerCta : 1;
@@ -418,7 +690,8 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   float* tile = reinterpret_cast<float*>(base + fixed);
   const int mode = choose_mode(s, a.tile_cap, (slot - fixed) / 4);
   // STAGE: solver rows [0, staged) are kept in shared memory (all of them when the tile fits)
-  const int staged = kStage ? min(nr, static_cast<int>((slot - fixed) / 4 / nc)) : 0;
+  const int staged =
+      kStage ? min(nr, static_cast<int>((slot - fixed - (kMulti ? kMultiPostBytes : 0)) / 4 / nc)) : 0;
   bool bad = false;
   const float* rows = src;  // solver row i starts at rows + i * row_pitch
   int64_t row_pitch = s.rs;
@@ -504,169 +777,186 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   bad = !(chk > -CUDART_INF_F);
   bad = __any_sync(kFullMask, bad);
   if (kCoop) {
-    // every warp's first picks and checks are in; warp 0 solves the problem alone
+    // every warp's first picks and checks are in; warp 0 solves the problem
+    // alone (MULTI: all four warps)
     bad = __syncthreads_or(bad) != 0;
-    if (warp != 0) return 0;
+    if (!kMulti && warp != 0) return 0;
   }
 
   unsigned freem = valid;
-  double v[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) v[k] = 0.0;
-  __syncwarp();
   int code = bad ? RFM_STATUS_INVALID : RFM_STATUS_OK;
-
-  for (int cur = 0; cur < nr && code == RFM_STATUS_OK; ++cur) {
-    const int w = pick_w_s[cur];
-    if (w >= 0 && row4col_s[w] < 0) {  // still valid: commit the trivial augmentation
-      const double m = pick_m_s[cur];
-      __syncwarp();
-      if (lane == 0) {
-        u_s[cur] += m;
-        row4col_s[w] = static_cast<int16_t>(cur);
-        col4row_s[cur] = static_cast<int16_t>(w);
-      }
-      if ((w & 31) == lane) freem &= ~(1u << (w >> 5));
-      __syncwarp();
-      continue;
-    }
-
-    // ---- full shortest-augmenting-path search for row `cur` ---------------
-    double spc[K];
-    unsigned key[K];
+  if constexpr (kMulti) {
+    constexpr int K3 = (32 * K + 127) / 128;
+    unsigned char* post = base + slot - kMultiPostBytes;
+    const MultiShared ms{u_s, pick_m_s, col4row_s, pick_w_s, row4col_s, path_s, rem_s, vis_s,
+                         reinterpret_cast<double*>(post), reinterpret_cast<unsigned*>(post + 64),
+                         reinterpret_cast<int*>(post + 96)};
+    code = multi_search<K3>(ms, tile, src, s.rs, staged, nr, nc, bad);
+    if (warp != 0) return 0;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const int j = lane + 32 * k;
-      const unsigned pos = static_cast<unsigned>(nc - 1 - j);  // remaining[it] = nc-1-it (reverse fill)
-      spc[k] = CUDART_INF;
-      const unsigned kv = (freem & (1u << k)) ? kKeyBase - 1u - pos : kKeyBase + pos;
-      if (!kWide) key[k] = kv;
-      if (j < nc) {
-        if (kWide) key_s[j] = static_cast<uint16_t>(kv);
-        rem_s[nc - 1 - j] = static_cast<int16_t>(j);
-      }
+      if (j < nc && row4col_s[j] >= 0) freem &= ~(1u << k);
     }
-    unsigned rem = valid;
-    int i = cur;
-    int nrem = nc;
-    int sink = -1;
-    double minv = 0.0;
-    __syncwarp();
-
-    float cf[K];
-    const auto issue_row = [&](int r) {
-      if (kStage) {  // staged rows from shared memory, the rest from L2 / HBM
-        if (r < staged) {
-          load_row<K, kLoadShared>(tile + r * nc, lane, rem, cf);
-        } else {
-          load_row<K, kLoadGlobal>(src + r * s.rs, lane, rem, cf);
-        }
-        return;
-      }
-      const float* row = rows + r * row_pitch;
-      if (mode == kModeShared) {
-        load_row<K, kLoadShared>(row, lane, rem, cf);
-      } else if (mode == kModeDirect) {
-        load_row<K, kLoadGlobal>(row, lane, rem, cf);
-      } else {
-        load_row<K, kLoadScratch>(row, lane, rem, cf);
-      }
-    };
-    if (kEarly) issue_row(cur);
-    for (int it = 0; it < nc; ++it) {
-      if (!kEarly) issue_row(i);
-      const double ui = u_s[i];
-      double bv = CUDART_INF;
-      unsigned bk = kNoKey;
-      scan_row<K, kWide>(cf, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv, bk);
-      warp_argmin(bv, bk);
-      if (bv == CUDART_INF) {
-        code = RFM_STATUS_INFEASIBLE;
-        break;
-      }
-      const int ps = static_cast<int>(bk < kKeyBase ? kKeyBase - 1u - bk : bk - kKeyBase);
-      const int js = rem_s[ps];
-      const int rj = row4col_s[js];
-      if (kEarly && rj >= 0) issue_row(rj);  // the next scan's row, before this step's bookkeeping
-      const int last = nrem - 1;
-      const int jl = rem_s[last];
-      __syncwarp();
-      if (lane == 0) rem_s[ps] = static_cast<int16_t>(jl);  // swap-with-last removal
-      if ((jl & 31) == lane) {
-        const int kl = jl >> 5;
-        const unsigned kv = ((freem >> kl) & 1u) ? kKeyBase - 1u - ps : kKeyBase + ps;
-        if (kWide) {
-          key_s[jl] = static_cast<uint16_t>(kv);
-        } else {
-          set_key<K>(key, kl, kv);
-        }
-      }
-      if ((js & 31) == lane) rem &= ~(1u << (js >> 5));
-      nrem = last;
-      minv = bv;
-      __syncwarp();
-      if (rj < 0) {
-        sink = js;
-        break;
-      }
-      i = rj;
-    }
-    if (code != RFM_STATUS_OK) break;
-    if (sink < 0) {
-      code = RFM_STATUS_NO_SINK;
-      break;
-    }
-
-    // ---- dual update over the tree (lane-local, see header comment) -------
-    const unsigned visited = valid & ~rem;
-    bool raised = false;  // a visited column's v went up: rounding broke minv >= spc
+  } else {
+    double v[K];
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      if (visited & (1u << k)) {
-        const int j = lane + 32 * k;
-        const double d = minv - spc[k];
-        raised |= d < 0.0;
-        if (j != sink) u_s[row4col_s[j]] += d;
-        if (kWide) {
-          v_s[j] -= d;
-        } else {
-          v[k] -= d;
-        }
-      }
-    }
-    raised = __any_sync(kFullMask, raised);
-    if (lane == 0) u_s[cur] += minv;
+    for (int k = 0; k < K; ++k) v[k] = 0.0;
     __syncwarp();
 
-    // ---- flip the alternating path ----------------------------------------
-    int flipped = 1;
-    if (lane == 0) {
-      flipped = 0;
-      int j = sink;
-      for (int step = 0; step <= nr; ++step) {
-        const int ii = path_s[j];
-        row4col_s[j] = static_cast<int16_t>(ii);
-        const int prev = col4row_s[ii];
-        col4row_s[ii] = static_cast<int16_t>(j);
-        j = prev;
-        if (ii == cur) {
-          flipped = 1;
+    for (int cur = 0; cur < nr && code == RFM_STATUS_OK; ++cur) {
+      const int w = pick_w_s[cur];
+      if (w >= 0 && row4col_s[w] < 0) {  // still valid: commit the trivial augmentation
+        const double m = pick_m_s[cur];
+        __syncwarp();
+        if (lane == 0) {
+          u_s[cur] += m;
+          row4col_s[w] = static_cast<int16_t>(cur);
+          col4row_s[cur] = static_cast<int16_t>(w);
+        }
+        if ((w & 31) == lane) freem &= ~(1u << (w >> 5));
+        __syncwarp();
+        continue;
+      }
+
+      // ---- full shortest-augmenting-path search for row `cur` ---------------
+      double spc[K];
+      unsigned key[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int j = lane + 32 * k;
+        const unsigned pos = static_cast<unsigned>(nc - 1 - j);  // remaining[it] = nc-1-it (reverse fill)
+        spc[k] = CUDART_INF;
+        const unsigned kv = (freem & (1u << k)) ? kKeyBase - 1u - pos : kKeyBase + pos;
+        if (!kWide) key[k] = (kv << kColBits) | static_cast<unsigned>(j);
+        if (j < nc) {
+          if (kWide) key_s[j] = static_cast<uint16_t>(kv);
+          rem_s[nc - 1 - j] = static_cast<int16_t>(j);
+        }
+      }
+      unsigned rem = valid;
+      int i = cur;
+      int nrem = nc;
+      int sink = -1;
+      double minv = 0.0;
+      __syncwarp();
+
+      float cf[K];
+      const auto issue_row = [&](int r) {
+        if (kStage) {  // staged rows from shared memory, the rest from L2 / HBM
+          if (r < staged) {
+            load_row<K, kLoadShared>(tile + r * nc, lane, rem, cf);
+          } else {
+            load_row<K, kLoadGlobal>(src + r * s.rs, lane, rem, cf);
+          }
+          return;
+        }
+        const float* row = rows + r * row_pitch;
+        if (mode == kModeShared) {
+          load_row<K, kLoadShared>(row, lane, rem, cf);
+        } else if (mode == kModeDirect) {
+          load_row<K, kLoadGlobal>(row, lane, rem, cf);
+        } else {
+          load_row<K, kLoadScratch>(row, lane, rem, cf);
+        }
+      };
+      if (kEarly) issue_row(cur);
+      for (int it = 0; it < nc; ++it) {
+        if (!kEarly) issue_row(i);
+        const double ui = u_s[i];
+        const int last = nrem - 1;
+        const int jl = rem_s[last];
+        double bv = CUDART_INF;
+        unsigned bk = kNoKey;
+        scan_row<K, kWide>(cf, lane, i, minv, ui, v, v_s, spc, key, key_s, rem, path_s, bv, bk);
+        warp_argmin(bv, bk);
+        if (bv == CUDART_INF) {
+          code = RFM_STATUS_INFEASIBLE;
           break;
         }
+        const int js = static_cast<int>(bk & kColMask);
+        const int rj = row4col_s[js];
+        if (kEarly && rj >= 0) issue_row(rj);  // the next scan's row, before this step's bookkeeping
+        const unsigned tk = bk >> kColBits;
+        const int ps = static_cast<int>(tk < kKeyBase ? kKeyBase - 1u - tk : tk - kKeyBase);
+        __syncwarp();
+        if (lane == 0) rem_s[ps] = static_cast<int16_t>(jl);  // swap-with-last removal
+        if ((jl & 31) == lane) {
+          const int kl = jl >> 5;
+          const unsigned kv = ((freem >> kl) & 1u) ? kKeyBase - 1u - ps : kKeyBase + ps;
+          if (kWide) {
+            key_s[jl] = static_cast<uint16_t>(kv);
+          } else {
+            set_key<K>(key, kl, (kv << kColBits) | static_cast<unsigned>(jl));
+          }
+        }
+        if ((js & 31) == lane) rem &= ~(1u << (js >> 5));
+        nrem = last;
+        minv = bv;
+        __syncwarp();
+        if (rj < 0) {
+          sink = js;
+          break;
+        }
+        i = rj;
       }
-    }
-    if ((sink & 31) == lane) freem &= ~(1u << (sink >> 5));
-    if (!__shfl_sync(kFullMask, flipped, 0)) code = RFM_STATUS_NO_SINK;
+      if (code != RFM_STATUS_OK) break;
+      if (sink < 0) {
+        code = RFM_STATUS_NO_SINK;
+        break;
+      }
 
-    // ---- drop the pending picks this search visited (all of them if some
-    // column's reduced costs went down) ------------------------------------
-    vis_s[lane] = raised ? 0xffffffffu : visited;
-    __syncwarp();
-    for (int r = cur + 1 + lane; r < nr; r += 32) {
-      const int pw = pick_w_s[r];
-      if (pw >= 0 && ((vis_s[pw & 31] >> (pw >> 5)) & 1u)) pick_w_s[r] = -1;
+      // ---- dual update over the tree (lane-local, see header comment) -------
+      const unsigned visited = valid & ~rem;
+      bool raised = false;  // a visited column's v went up: rounding broke minv >= spc
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        if (visited & (1u << k)) {
+          const int j = lane + 32 * k;
+          const double d = minv - spc[k];
+          raised |= d < 0.0;
+          if (j != sink) u_s[row4col_s[j]] += d;
+          if (kWide) {
+            v_s[j] -= d;
+          } else {
+            v[k] -= d;
+          }
+        }
+      }
+      raised = __any_sync(kFullMask, raised);
+      if (lane == 0) u_s[cur] += minv;
+      __syncwarp();
+
+      // ---- flip the alternating path ----------------------------------------
+      int flipped = 1;
+      if (lane == 0) {
+        flipped = 0;
+        int j = sink;
+        for (int step = 0; step <= nr; ++step) {
+          const int ii = path_s[j];
+          row4col_s[j] = static_cast<int16_t>(ii);
+          const int prev = col4row_s[ii];
+          col4row_s[ii] = static_cast<int16_t>(j);
+          j = prev;
+          if (ii == cur) {
+            flipped = 1;
+            break;
+          }
+        }
+      }
+      if ((sink & 31) == lane) freem &= ~(1u << (sink >> 5));
+      if (!__shfl_sync(kFullMask, flipped, 0)) code = RFM_STATUS_NO_SINK;
+
+      // ---- drop the pending picks this search visited (all of them if some
+      // column's reduced costs went down) ------------------------------------
+      vis_s[lane] = raised ? 0xffffffffu : visited;
+      __syncwarp();
+      for (int r = cur + 1 + lane; r < nr; r += 32) {
+        const int pw = pick_w_s[r];
+        if (pw >= 0 && ((vis_s[pw & 31] >> (pw >> 5)) & 1u)) pick_w_s[r] = -1;
+      }
+      __syncwarp();
     }
-    __syncwarp();
   }
 
   // ---- epilogue: write the result in SciPy's order -------------------------
@@ -720,7 +1010,7 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVari
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  if (kVariant == kVarCoop || kVariant == kVarStage) {
+  if (kVariant == kVarCoop || kVariant == kVarStage || kVariant == kVarMulti) {
     // one problem per CTA, all four warps in its load pass
     solve_problem<K, kDense, kVariant>(a, blockIdx.x, smem_raw, a.slot, lane);
     return;
@@ -771,15 +1061,17 @@ const void* pair_kernel(int cols_per_lane, int variant) {
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarEarly>);
       if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarCoop>);
       if (variant == kVarStage) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarStage>);
+      if (variant == kVarMulti) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMulti>);
       return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarRegs>);
     case 10:
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarWide>);
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarEarly>);
       if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarCoop>);
       if (variant == kVarStage) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarStage>);
+      if (variant == kVarMulti) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMulti>);
       return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarRegs>);
     case 32:
-      if (variant == kVarWide || variant == kVarCoop || variant == kVarStage) return nullptr;
+      if (variant == kVarWide || variant == kVarCoop || variant == kVarStage || variant == kVarMulti) return nullptr;
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarEarly>);
       return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarRegs>);
     default: return nullptr;
@@ -888,10 +1180,14 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense, kVariant>); break;
     case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, kDense, kVariant>); break;
     case 32:
-      if (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage) return RFM_ERR_INVALID_ARGUMENT;
+      if (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage || kVariant == kVarMulti) {
+        return RFM_ERR_INVALID_ARGUMENT;
+      }
       fn = reinterpret_cast<const void*>(
           &lsap_kernel<32, kDense,
-                       (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage) ? kVarRegs : kVariant>);
+                       (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage || kVariant == kVarMulti)
+                           ? kVarRegs
+                           : kVariant>);
       break;
     default: return RFM_ERR_INVALID_ARGUMENT;
   }
@@ -929,7 +1225,9 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     case 10: lsap_kernel<10, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
     default:
       lsap_kernel<32, kDense,
-                  (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage) ? kVarRegs : kVariant>
+                  (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage || kVariant == kVarMulti)
+                           ? kVarRegs
+                           : kVariant>
           <<<grid, block, smem, as_stream(stream)>>>(a);
       break;
   }
@@ -1117,7 +1415,7 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
     const int64_t smem = kSmemPerSm / per_sm - kSmemPerCtaReserved;
     a.slot = static_cast<int>(smem > kSmemPerBlockMax ? kSmemPerBlockMax : smem);
     a.tile_cap = (a.slot - static_cast<int>(fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))) / 4;
-    return launch<false, kVarStage>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, a.slot, stream,
+    return launch<false, kVarMulti>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, a.slot, stream,
                                     counter_zeroed);
   }
   const bool wide = plan->cols_per_lane <= 10 &&

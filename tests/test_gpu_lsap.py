@@ -7,7 +7,7 @@ from scipy.optimize import linear_sum_assignment as scipy_lsa
 
 from golden_io import lsap_case, names
 from oracle.lsap import linear_sum_assignment as oracle_lsa
-from rfdetr_training_throughput_b200 import matcher
+from rfdetr_training_throughput_b200 import _lib, matcher
 
 pytestmark = pytest.mark.gpu
 
@@ -102,3 +102,57 @@ def test_repeat_calls_are_deterministic():
     a = matcher.batch_linear_assignment(cost)
     b = matcher.batch_linear_assignment(cost)
     assert torch.equal(a, b)
+
+
+def _target_major_matrix(sizes, width, groups, kind, rng):
+    """A target-major compact matrix [sum T, groups * width] of the given value kind."""
+    shape = (sum(sizes), groups * width)
+    if kind == "uniform":
+        m = rng.random(shape, dtype=np.float32) * 10 - 5
+    elif kind.startswith("ties"):
+        q = int(kind[4:])
+        m = (rng.integers(0, q, shape) / q).astype(np.float32)
+    else:  # "inf": a third of the entries +inf, and one target of image 1 unmatchable in group 0
+        m = rng.random(shape, dtype=np.float32)
+        m[rng.random(shape) < 0.3] = np.inf
+        m[sizes[0], :width] = np.inf
+    return np.ascontiguousarray(m.astype(np.float32))
+
+
+@pytest.mark.parametrize("sizes,width,groups,kind", [
+    ((297, 250, 180, 120, 64), 300, 2, "uniform"),  # 297 x 300 floats exceed an SM's shared memory
+    ((260, 200, 100, 70), 300, 3, "ties4"),
+    ((99, 80, 64, 70), 100, 4, "ties2"),  # at most 128 columns
+    ((220, 150, 90), 300, 2, "inf"),
+    (tuple(range(64, 124, 3)), 300, 13, "ties8"),  # 260 problems: two per SM
+])
+def test_long_problems_on_target_major_blocks(sizes, width, groups, kind):
+    """Small batches of long, row-contiguous problems (a target-major matrix, 64+ targets each): the
+    launch that gives every problem a CTA and stages its rows in shared memory.  Indices and statuses
+    are compared with SciPy problem by problem."""
+    rng = np.random.default_rng(sum(sizes) + width + groups)
+    m = _target_major_matrix(sizes, width, groups, kind, rng)
+    dev = torch.device("cuda")
+    cost = torch.as_tensor(m, device=dev)
+    plan = matcher.plan_step(sizes, 1, groups * width, groups, m.shape[1], dev, _lib.LAYOUT_TARGET_MAJOR)
+    pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=dev)
+    status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=dev)
+    matcher.launch_lsap(cost, plan, pairs, status)
+    per_image = matcher.MatchResult(pairs, plan.per_image, 1, len(sizes)).layer(0)
+    status_of = {int(plan.order[i]): int(s) for i, s in enumerate(status.cpu().numpy())}
+    off = np.concatenate([[0], np.cumsum(sizes)])
+    for b, t in enumerate(sizes):
+        qs, ts = (x.cpu().numpy() for x in per_image[b])
+        n = min(width, t)
+        for g in range(groups):
+            block = m[off[b]:off[b + 1], g * width:(g + 1) * width].T  # [queries, targets]
+            chunk = slice(g * n, (g + 1) * n)
+            try:
+                r, c = scipy_lsa(block)
+            except ValueError:
+                assert status_of[b * groups + g] == _lib.STATUS_INFEASIBLE
+                assert (qs[chunk] == -1).all() and (ts[chunk] == -1).all()
+                continue
+            assert status_of[b * groups + g] == _lib.STATUS_OK
+            assert np.array_equal(qs[chunk], r + g * width)
+            assert np.array_equal(ts[chunk], c)

@@ -379,11 +379,27 @@ struct MultiShared {
   int16_t* path;
   int16_t* rem;
   unsigned* vis;   // visited-column bitmap of the last search (bit j & 31 of word j >> 5)
-  double* post_v;  // [2][4] step posts
-  unsigned* post_k;
+  double2* post;  // [2][4] step posts: (path cost, key)
   int* flag;
 };
-constexpr int kMultiPostBytes = 128;
+constexpr int kMultiPostBytes = 144;
+// A MULTI key also carries the column's matched row plus one (0 when free) in
+// its low kRowBits bits, so the step's argmin names the next row directly.
+// Columns are at most 320 here, and rows at most columns.
+constexpr int kRowBits = 9;
+constexpr unsigned kRowMask = (1u << kRowBits) - 1u;
+constexpr int kTieShift = kColBits + kRowBits;
+
+// A post is (path cost, key) with the key in the low word of .y.
+__device__ __forceinline__ double key_as_double(unsigned k) {
+  return __longlong_as_double(static_cast<long long>(k));
+}
+
+__device__ __forceinline__ bool post_less(const double2& x, const double2& y) {
+  const unsigned kx = static_cast<unsigned>(__double_as_longlong(x.y));
+  const unsigned ky = static_cast<unsigned>(__double_as_longlong(y.y));
+  return x.x < y.x || (x.x == y.x && kx < ky);
+}
 
 template <int K3>
 __device__ __forceinline__ void multi_row(const float* row, int t, unsigned mask, float (&cf)[K3]) {
@@ -441,7 +457,8 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
       const unsigned pos = static_cast<unsigned>(nc - 1 - j);
       spc[k] = CUDART_INF;
       const unsigned kv = (freem & (1u << k)) ? kKeyBase - 1u - pos : kKeyBase + pos;
-      key[k] = (kv << kColBits) | static_cast<unsigned>(j);
+      const unsigned row1 = j < nc ? static_cast<unsigned>(m.row4col[j] + 1) : 0u;
+      key[k] = (kv << kTieShift) | (static_cast<unsigned>(j) << kRowBits) | row1;
       if (j < nc) m.rem[nc - 1 - j] = static_cast<int16_t>(j);
     }
     unsigned rem = valid;
@@ -489,31 +506,44 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
         bv = rv[0];
         bk = rk[0];
       }
-      warp_argmin(bv, bk);
-      if (lane == 0) {
-        m.post_v[parity * 4 + warp] = bv;
-        m.post_k[parity * 4 + warp] = bk;
+      // the warp's minimum: one redux.sync on the high word of the ordered
+      // path cost; only when several lanes share that word do the low word and
+      // the key decide (two more).  The lane holding the minimum posts it.
+      {
+        const unsigned long long o = ordered_bits(bv);
+        const unsigned hi = static_cast<unsigned>(o >> 32);
+        const unsigned mhi = __reduce_min_sync(kFullMask, hi);
+        const unsigned tied = __ballot_sync(kFullMask, hi == mhi);
+        bool mine = hi == mhi;
+        if (__popc(tied) > 1) {
+          const unsigned lo = static_cast<unsigned>(o);
+          const unsigned mlo = __reduce_min_sync(kFullMask, mine ? lo : 0xffffffffu);
+          mine = mine && lo == mlo;
+          const unsigned mk = __reduce_min_sync(kFullMask, mine ? bk : kNoKey);
+          mine = mine && bk == mk;
+        }
+        if (mine) m.post[parity * 4 + warp] = make_double2(bv, key_as_double(bk));
       }
       __syncthreads();
-      bv = m.post_v[parity * 4];
-      bk = m.post_k[parity * 4];
-#pragma unroll
-      for (int q = 1; q < kMaxWarpsPerCta; ++q) {
-        const double ov = m.post_v[parity * 4 + q];
-        const unsigned ok = m.post_k[parity * 4 + q];
-        const bool take = ov < bv || (ov == bv && ok < bk);
-        bv = take ? ov : bv;
-        bk = take ? ok : bk;
+      {
+        // fixed-shape tree over the four posts (keys are unique: any order agrees)
+        const double2 p0 = m.post[parity * 4 + 0], p1 = m.post[parity * 4 + 1];
+        const double2 p2 = m.post[parity * 4 + 2], p3 = m.post[parity * 4 + 3];
+        const double2 a = post_less(p1, p0) ? p1 : p0;
+        const double2 b = post_less(p3, p2) ? p3 : p2;
+        const double2 w = post_less(b, a) ? b : a;
+        bv = w.x;
+        bk = static_cast<unsigned>(__double_as_longlong(w.y));
       }
       parity ^= 1;
       if (bv == CUDART_INF) {
         code = RFM_STATUS_INFEASIBLE;
         break;
       }
-      const int js = static_cast<int>(bk & kColMask);
-      const int rj = m.row4col[js];
+      const int js = static_cast<int>((bk >> kRowBits) & kColMask);
+      const int rj = static_cast<int>(bk & kRowMask) - 1;
       if (rj >= 0) issue_row(rj);  // the next scan's row, before this step's bookkeeping
-      const unsigned tk = bk >> kColBits;
+      const unsigned tk = bk >> kTieShift;
       const int ps = static_cast<int>(tk < kKeyBase ? kKeyBase - 1u - tk : tk - kKeyBase);
       // swap-with-last removal; the write is read after the next step's barrier
       const int jl = m.rem[nrem - 1];
@@ -523,7 +553,7 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
         const unsigned kv = ((freem >> kl) & 1u) ? kKeyBase - 1u - ps : kKeyBase + ps;
 #pragma unroll
         for (int k = 0; k < K3; ++k) {
-          if (k == kl) key[k] = (kv << kColBits) | static_cast<unsigned>(jl);
+          if (k == kl) key[k] = (kv << kTieShift) | (key[k] & ((1u << kTieShift) - 1u));
         }
       }
       if ((js & 127) == t) rem &= ~(1u << (js >> 7));
@@ -789,8 +819,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
     constexpr int K3 = (32 * K + 127) / 128;
     unsigned char* post = base + slot - kMultiPostBytes;
     const MultiShared ms{u_s, pick_m_s, col4row_s, pick_w_s, row4col_s, path_s, rem_s, vis_s,
-                         reinterpret_cast<double*>(post), reinterpret_cast<unsigned*>(post + 64),
-                         reinterpret_cast<int*>(post + 96)};
+                         reinterpret_cast<double2*>(post), reinterpret_cast<int*>(post + 128)};
     code = multi_search<K3>(ms, tile, src, s.rs, staged, nr, nc, bad);
     if (warp != 0) return 0;
 #pragma unroll

@@ -80,23 +80,36 @@ constexpr int kMaxWarpsPerCta = 4;
 // whose four warps share the load pass (a quarter of the rows each, so a
 // problem's rows cost a quarter of the round trips) before warp 0 solves it
 // alone: small batches, where every problem is resident at once and the
-// step's time is the slowest problem's latency.  STAGE is COOP for small batches
-// of long problems (searches of many steps): its CTA takes all the shared
-// memory an SM gives one or two CTAs, the load pass keeps as many of the
-// problem's rows there as fit, and warp 0's searches read those rows from shared
-// memory (the rest from L2), each scan's row requested early as in EARLY.
-// MULTI is STAGE with the searches spread over the CTA's four warps.
-enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2, kVarCoop = 3, kVarStage = 4, kVarMulti = 5 };
+// step's time is the slowest problem's latency.  MULTI is for batches of long
+// problems (searches of many steps) small enough to run in one wave of
+// four-warp CTAs: one problem per CTA, whose shared memory is the SM's divided
+// by the CTAs the SM holds; the load pass keeps as many of the problem's rows
+// there as fit (the rest are read from L2), and every step of a search is spread
+// over the four warps.  MULTI_COPY is MULTI for batches whose solver rows are
+// not all contiguous in the source: those problems are staged as a transposed
+// copy, partly in scratch.
+enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2, kVarCoop = 3, kVarMulti = 5, kVarMultiCopy = 6 };
+// Variants with one problem per CTA; none exists for the 1024-column layout,
+// and neither does WIDE.
+__host__ __device__ constexpr bool cta_variant(int v) {
+  return v == kVarCoop || v == kVarMulti || v == kVarMultiCopy;
+}
+__host__ __device__ constexpr bool narrow_only(int v) { return v == kVarWide || cta_variant(v); }
 constexpr int kEarlyMinRows = 64;
-// Batches of long problems (EARLY) with at most this many problems per SM run as STAGE.
-constexpr int kStageCtasPerSm = 2;
+// Batches of long problems (EARLY) with at most this many problems per SM run as
+// MULTI, when that many of its CTAs fit an SM (registers; the shared memory is
+// divided among them).  Beyond about eight, four warps per problem issue more
+// than one warp per problem would.
+constexpr int kMultiCtasPerSm = 8;
 // Batches with more than this many problems per SM use the wide layout.
 constexpr int kWideProblemsPerSm = 64;
 // Register budget.  The instantiations up to 320 columns run four CTAs of four
 // warps per SM (at most 128 registers a thread), or six in the wide layout,
 // which keeps the column duals and tie keys in shared memory (at most 85): more
 // resident warps for large batches at a longer chain per problem.  The
-// 1024-column one keeps its per-lane arrays in registers.
+// 1024-column one keeps its per-lane arrays in registers.  (MULTI compiles to
+// 96 registers, five CTAs per SM; capped at 80 or 64 for six or eight CTAs its
+// searches ran 9 % and 22 % longer.)
 __host__ __device__ constexpr int min_ctas_per_sm(int cols_per_lane, int variant) {
   return cols_per_lane > 10 ? 1 : (variant == kVarWide ? 6 : 4);
 }
@@ -407,16 +420,19 @@ __device__ __forceinline__ void multi_row(const float* row, int t, unsigned mask
   for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? row[t + 128 * k] : 0.0f;
 }
 
-template <int K3>
+// Rows in global memory: the read-only source (kLoadGlobal) or the scratch copy
+// this kernel wrote (kLoadScratch, read through L2).
+template <int K3, int L>
 __device__ __forceinline__ void multi_row_global(const float* row, int t, unsigned mask, float (&cf)[K3]) {
 #pragma unroll
-  for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? __ldg(row + t + 128 * k) : 0.0f;
+  for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? load_cost<L>(row + t + 128 * k) : 0.0f;
 }
 
 // Searches and commits every row of a problem whose costs are staged (rows
-// [0, staged) at `tile`, pitch nc) or read from `src` (row pitch rs).  Called by
-// all 128 threads after the load pass; returns the problem's status.
-template <int K3>
+// [0, staged) at `tile`, pitch nc) or read from `src` (row pitch rs; kWritten
+// when the rows are the scratch copy of this launch).  Called by all 128
+// threads after the load pass; returns the problem's status.
+template <int K3, bool kWritten>
 __device__ int multi_search(const MultiShared& m, const float* tile, const float* src, int64_t rs, int staged,
                             int nr, int nc, bool bad) {
   const int t = threadIdx.x;
@@ -471,7 +487,7 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
       if (r < staged) {
         multi_row<K3>(tile + r * nc, t, rem, cf);
       } else {
-        multi_row_global<K3>(src + r * rs, t, rem, cf);
+        multi_row_global<K3, kWritten ? kLoadScratch : kLoadGlobal>(src + r * rs, t, rem, cf);
       }
     };
     issue_row(cur);
@@ -630,8 +646,9 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
                                              int lane) {
   constexpr int kCols = 32 * K;
   constexpr bool kWide = kVariant == kVarWide;
-  constexpr bool kMulti = kVariant == kVarMulti;
-  constexpr bool kStage = kVariant == kVarStage || kMulti;
+  constexpr bool kCopy = kVariant == kVarMultiCopy;
+  constexpr bool kMulti = kVariant == kVarMulti || kCopy;
+  constexpr bool kStage = kMulti;  // rows [0, staged) kept in shared memory
   constexpr bool kEarly = kVariant == kVarEarly || kStage;
   constexpr bool kCoop = kVariant == kVarCoop || kStage;
   constexpr int kLoadWarps = kCoop ? kMaxWarpsPerCta : 1;
@@ -769,6 +786,40 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
       rows = tile;
       row_pitch = nc;
     }
+  } else if (kCopy) {
+    // the source runs along solver rows: the four warps stage a transposed
+    // copy, rows [0, staged) in shared memory and the rest in the problem's
+    // scratch (the launch only runs MULTI when every tile that does not fit
+    // has scratch).  Consecutive lanes read consecutive solver rows, which are
+    // consecutive in the source.
+    float* scratch = a.workspace + (scratch_off < 0 ? 0 : scratch_off);
+    // (the launch never leaves an unstaged tile without scratch; should it, the
+    // problem is reported invalid and no memory outside it is touched)
+    const bool scratch_ok = staged == nr || (scratch_off >= 0 && a.workspace != nullptr);
+    const int copied = scratch_ok ? nr : staged;
+    bad = !scratch_ok;
+    for (int j = warp; j < nc; j += kMaxWarpsPerCta) {
+      for (int i = lane; i < copied; i += 32) {
+        const float x = __ldg(src + i * s.rs + j * s.cs);
+        if (i < staged) {
+          tile[i * nc + j] = x;
+        } else {
+          scratch[static_cast<int64_t>(i) * nc + j] = x;
+        }
+      }
+    }
+    __syncthreads();
+    for (int i = warp; i < copied; i += kMaxWarpsPerCta) {
+      float x[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int j = lane + 32 * k;
+        x[k] = j >= nc ? CUDART_INF_F : (i < staged ? tile[i * nc + j] : __ldcg(scratch + static_cast<int64_t>(i) * nc + j));
+      }
+      const float m = lane_min<K>(x);
+      chk = min_nan(chk, m);
+      record_first_pick<K>(x, m, lane, nc, i, pick_m_s, pick_w_s);
+    }
   } else if (warp == 0) {
     // the source runs along solver rows: stage a transposed copy first
     const int total = nr * nc;
@@ -804,7 +855,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
       record_first_pick<K>(x, m, lane, nc, i, pick_m_s, pick_w_s);
     }
   }
-  bad = !(chk > -CUDART_INF_F);
+  bad = bad || !(chk > -CUDART_INF_F);
   bad = __any_sync(kFullMask, bad);
   if (kCoop) {
     // every warp's first picks and checks are in; warp 0 solves the problem
@@ -820,7 +871,15 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
     unsigned char* post = base + slot - kMultiPostBytes;
     const MultiShared ms{u_s, pick_m_s, col4row_s, pick_w_s, row4col_s, path_s, rem_s, vis_s,
                          reinterpret_cast<double2*>(post), reinterpret_cast<int*>(post + 128)};
-    code = multi_search<K3>(ms, tile, src, s.rs, staged, nr, nc, bad);
+    if constexpr (kCopy) {
+      if (s.cs == 1) {
+        code = multi_search<K3, false>(ms, tile, src, s.rs, staged, nr, nc, bad);
+      } else {
+        code = multi_search<K3, true>(ms, tile, a.workspace + scratch_off, nc, staged, nr, nc, bad);
+      }
+    } else {
+      code = multi_search<K3, false>(ms, tile, src, s.rs, staged, nr, nc, bad);
+    }
     if (warp != 0) return 0;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -872,14 +931,6 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
 
       float cf[K];
       const auto issue_row = [&](int r) {
-        if (kStage) {  // staged rows from shared memory, the rest from L2 / HBM
-          if (r < staged) {
-            load_row<K, kLoadShared>(tile + r * nc, lane, rem, cf);
-          } else {
-            load_row<K, kLoadGlobal>(src + r * s.rs, lane, rem, cf);
-          }
-          return;
-        }
         const float* row = rows + r * row_pitch;
         if (mode == kModeShared) {
           load_row<K, kLoadShared>(row, lane, rem, cf);
@@ -1039,7 +1090,7 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVari
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  if (kVariant == kVarCoop || kVariant == kVarStage || kVariant == kVarMulti) {
+  if (cta_variant(kVariant)) {
     // one problem per CTA, all four warps in its load pass
     solve_problem<K, kDense, kVariant>(a, blockIdx.x, smem_raw, a.slot, lane);
     return;
@@ -1089,18 +1140,18 @@ const void* pair_kernel(int cols_per_lane, int variant) {
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarWide>);
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarEarly>);
       if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarCoop>);
-      if (variant == kVarStage) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarStage>);
       if (variant == kVarMulti) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMulti>);
+      if (variant == kVarMultiCopy) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMultiCopy>);
       return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarRegs>);
     case 10:
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarWide>);
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarEarly>);
       if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarCoop>);
-      if (variant == kVarStage) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarStage>);
       if (variant == kVarMulti) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMulti>);
+      if (variant == kVarMultiCopy) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMultiCopy>);
       return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarRegs>);
     case 32:
-      if (variant == kVarWide || variant == kVarCoop || variant == kVarStage || variant == kVarMulti) return nullptr;
+      if (narrow_only(variant)) return nullptr;
       if (variant == kVarEarly) return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarEarly>);
       return reinterpret_cast<const void*>(&lsap_kernel<32, false, kVarRegs>);
     default: return nullptr;
@@ -1148,9 +1199,8 @@ bool ensure_dynamic_smem(const void* fn, int64_t smem) {
   return true;
 }
 
-// CTAs of a pair-mode kernel that fit on one SM at this shared-memory size.
-int query_resident_ctas(int cols_per_lane, int variant, int64_t smem) {
-  const void* fn = pair_kernel(cols_per_lane, variant);
+// CTAs of a solver kernel that fit on one SM at this shared-memory size.
+int query_resident_ctas(const void* fn, int64_t smem) {
   if (fn == nullptr) return 0;
   if (!ensure_dynamic_smem(fn, smem)) {
     cudaGetLastError();
@@ -1170,15 +1220,16 @@ int query_resident_ctas(int cols_per_lane, int variant, int64_t smem) {
 // Occupancy is a property of the device and the kernel, so the memo stays
 // valid across contexts; the launch itself raises the attribute per context.
 struct OccupancyEntry {
-  int device, cols_per_lane;
-  int variant;
+  int device;
+  const void* fn;
   int64_t smem;
   int ctas;
 };
 std::mutex g_occupancy_mutex;
 std::vector<OccupancyEntry> g_occupancy;
 
-int resident_ctas(int cols_per_lane, int variant, int64_t smem) {
+int resident_ctas(const void* fn, int64_t smem) {
+  if (fn == nullptr) return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
@@ -1187,15 +1238,15 @@ int resident_ctas(int cols_per_lane, int variant, int64_t smem) {
   {
     std::lock_guard<std::mutex> lock(g_occupancy_mutex);
     for (const OccupancyEntry& e : g_occupancy) {
-      if (e.device == dev && e.cols_per_lane == cols_per_lane && e.variant == variant && e.smem == smem) {
+      if (e.device == dev && e.fn == fn && e.smem == smem) {
         return e.ctas;
       }
     }
   }
-  const int n = query_resident_ctas(cols_per_lane, variant, smem);
+  const int n = query_resident_ctas(fn, smem);
   if (n > 0) {
     std::lock_guard<std::mutex> lock(g_occupancy_mutex);
-    g_occupancy.push_back({dev, cols_per_lane, variant, smem, n});
+    g_occupancy.push_back({dev, fn, smem, n});
   }
   return n;
 }
@@ -1209,14 +1260,8 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     case 4: fn = reinterpret_cast<const void*>(&lsap_kernel<4, kDense, kVariant>); break;
     case 10: fn = reinterpret_cast<const void*>(&lsap_kernel<10, kDense, kVariant>); break;
     case 32:
-      if (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage || kVariant == kVarMulti) {
-        return RFM_ERR_INVALID_ARGUMENT;
-      }
-      fn = reinterpret_cast<const void*>(
-          &lsap_kernel<32, kDense,
-                       (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage || kVariant == kVarMulti)
-                           ? kVarRegs
-                           : kVariant>);
+      if (narrow_only(kVariant)) return RFM_ERR_INVALID_ARGUMENT;
+      fn = reinterpret_cast<const void*>(&lsap_kernel<32, kDense, narrow_only(kVariant) ? kVarRegs : kVariant>);
       break;
     default: return RFM_ERR_INVALID_ARGUMENT;
   }
@@ -1253,11 +1298,7 @@ int launch(const LsapArgs& a, int cols_per_lane, int num_ctas, int warps_per_cta
     case 4: lsap_kernel<4, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
     case 10: lsap_kernel<10, kDense, kVariant><<<grid, block, smem, as_stream(stream)>>>(a); break;
     default:
-      lsap_kernel<32, kDense,
-                  (kVariant == kVarWide || kVariant == kVarCoop || kVariant == kVarStage || kVariant == kVarMulti)
-                           ? kVarRegs
-                           : kVariant>
-          <<<grid, block, smem, as_stream(stream)>>>(a);
+      lsap_kernel<32, kDense, narrow_only(kVariant) ? kVarRegs : kVariant><<<grid, block, smem, as_stream(stream)>>>(a);
       break;
   }
   return launch_status();
@@ -1382,6 +1423,31 @@ extern "C" int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, 
 
 namespace rfm {
 namespace {
+// Shared memory of one CTA of the MULTI kernel `fn` when a batch of
+// `num_problems` runs as one wave of them: ceil(P / SMs) CTAs per SM, each
+// taking that share of the SM.  0 when the batch is larger than
+// kMultiCtasPerSm per SM, when that many CTAs do not fit (registers), or when
+// the share does not hold the problem's `fixed` arrays and the step posts.
+int multi_slot_bytes(int num_problems, const void* fn, int64_t fixed) {
+  const int sms = device_sm_count();
+  if (fn == nullptr || sms < 1 || num_problems < 1 ||
+      static_cast<int64_t>(num_problems) > static_cast<int64_t>(kMultiCtasPerSm) * sms) {
+    return 0;
+  }
+  const int per_sm = (num_problems + sms - 1) / sms;
+  // whole KB, so that per_sm shares plus their reservations fit the SM
+  int smem = (kSmemPerSm / per_sm - kSmemPerCtaReserved) / 1024 * 1024;
+  if (smem > kSmemPerBlockMax) smem = kSmemPerBlockMax;
+  if (fixed + kMultiPostBytes > smem) return 0;
+  return resident_ctas(fn, smem) >= per_sm ? smem : 0;
+}
+
+const void* dense_multi_kernel(int cols_per_lane) {
+  if (cols_per_lane == 4) return reinterpret_cast<const void*>(&lsap_kernel<4, true, kVarMultiCopy>);
+  if (cols_per_lane == 10) return reinterpret_cast<const void*>(&lsap_kernel<10, true, kVarMultiCopy>);
+  return nullptr;
+}
+
 // rfm_lsap; with `counter_zeroed` the persistent counter was reset by the cost
 // kernel that runs just before on the stream, so there is no memset and the
 // persistent launch overlaps that kernel's end.
@@ -1424,6 +1490,23 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   a.status = status;
   const bool early = plan->max_rows >= kEarlyMinRows;
   if (!persistent) {
+    const int slot = early && plan->cols_per_lane <= 10
+                         ? multi_slot_bytes(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMultiCopy),
+                                            fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
+                         : 0;
+    if (slot > 0) {
+      // a one-wave batch of long problems, some not row-contiguous: MULTI_COPY.
+      // Every tile above the plan's cap has scratch, so it runs when its shared
+      // memory holds that cap.
+      const int64_t room =
+          (slot - fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows) - kMultiPostBytes) / 4;
+      if (plan->tile_cap_floats <= room) {
+        a.slot = slot;
+        a.tile_cap = static_cast<int>(room);
+        return launch<false, kVarMultiCopy>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, slot,
+                                            stream);
+      }
+    }
     if (early) {
       return launch<false, kVarEarly>(a, plan->cols_per_lane, plan->num_ctas, kMaxWarpsPerCta,
                                       plan->cta_smem_bytes, stream);
@@ -1435,14 +1518,13 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   // large batches (more problems than 64 per SM) take the wide layout, batches of
   // long problems the early-load variant.
   const int sms = device_sm_count();
-  if (early && plan->cols_per_lane <= 10 &&
-      static_cast<int64_t>(plan->num_problems) <= static_cast<int64_t>(kStageCtasPerSm) * sms) {
-    // a small batch of long problems: one problem per CTA, each CTA with the
-    // shared memory of an SM split kStageCtasPerSm ways (or all of it when the
-    // batch fits one CTA per SM), its rows staged there as far as they fit
-    const int per_sm = plan->num_problems <= sms ? 1 : kStageCtasPerSm;
-    const int64_t smem = kSmemPerSm / per_sm - kSmemPerCtaReserved;
-    a.slot = static_cast<int>(smem > kSmemPerBlockMax ? kSmemPerBlockMax : smem);
+  const int multi_slot = early && plan->cols_per_lane <= 10
+                             ? multi_slot_bytes(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMulti),
+                                                fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
+                             : 0;
+  if (multi_slot > 0) {
+    // a one-wave batch of long problems: MULTI, its rows staged as far as they fit
+    a.slot = multi_slot;
     a.tile_cap = (a.slot - static_cast<int>(fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))) / 4;
     return launch<false, kVarMulti>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, a.slot, stream,
                                     counter_zeroed);
@@ -1454,7 +1536,7 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
     // a small batch whose problems are all resident at once: one problem per
     // CTA, the CTA's four warps sharing its load pass (no counter, no memset)
     const int64_t coop_smem = fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows);
-    const int coop_ctas = resident_ctas(plan->cols_per_lane, kVarCoop, coop_smem);
+    const int coop_ctas = resident_ctas(pair_kernel(plan->cols_per_lane, kVarCoop), coop_smem);
     if (coop_ctas > 0 && static_cast<int64_t>(plan->num_problems) <= static_cast<int64_t>(coop_ctas) * sms) {
       a.slot = static_cast<int>(coop_smem);
       return launch<false, kVarCoop>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, coop_smem,
@@ -1469,7 +1551,7 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   if (!counter_zeroed && cudaMemsetAsync(a.queue, 0, sizeof(int), as_stream(stream)) != cudaSuccess) {
     return launch_status();
   }
-  const int ctas_per_sm = resident_ctas(plan->cols_per_lane, variant, smem);
+  const int ctas_per_sm = resident_ctas(pair_kernel(plan->cols_per_lane, variant), smem);
   if (ctas_per_sm < 1) return launch_status() != RFM_OK ? RFM_ERR_LAUNCH : RFM_ERR_UNSUPPORTED;
   const int grid = ctas_per_sm * sms;
   const int needed = (plan->num_problems + kMaxWarpsPerCta - 1) / kMaxWarpsPerCta;
@@ -1586,6 +1668,20 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.q_out = matching;
   a.t_out = nullptr;
   a.status = status;
+  if (dp.max_rows >= kEarlyMinRows && dp.cpl <= 10) {
+    // a one-wave batch of long problems: MULTI_COPY when every tile either fits
+    // its CTA's shared memory or has scratch
+    const int slot =
+        multi_slot_bytes(num_problems, dense_multi_kernel(dp.cpl), fixed_warp_bytes(32 * dp.cpl, dp.max_rows));
+    const Shape s = solver_shape(num_workers, num_tasks, num_tasks, 1);
+    const int64_t room = slot > 0 ? (slot - fixed_warp_bytes(32 * dp.cpl, dp.max_rows) - kMultiPostBytes) / 4 : 0;
+    // (row-contiguous problems read their unstaged rows from the source)
+    if (slot > 0 && (static_cast<int64_t>(s.nr) * s.nc <= room || s.cs == 1 || dp.scratch_bytes > 0)) {
+      a.slot = slot;
+      a.tile_cap = static_cast<int>(room);
+      return launch<true, kVarMultiCopy>(a, dp.cpl, num_problems, kMaxWarpsPerCta, slot, stream);
+    }
+  }
   const int ctas = (num_problems + dp.warps - 1) / dp.warps;
   if (dp.max_rows >= kEarlyMinRows) return launch<true, kVarEarly>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);
   return launch<true, kVarRegs>(a, dp.cpl, ctas, dp.warps, dp.warps * dp.slot, stream);

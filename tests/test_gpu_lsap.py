@@ -125,16 +125,24 @@ def _target_major_matrix(sizes, width, groups, kind, rng):
     ((99, 80, 64, 70), 100, 4, "ties2"),  # at most 128 columns
     ((220, 150, 90), 300, 2, "inf"),
     (tuple(range(64, 124, 3)), 300, 13, "ties8"),  # 260 problems: two per SM
+    ((300, 180, 90), 300, 2, "ties4"),  # square problems: solver rows run across the target-major rows
 ])
-def test_long_problems_on_target_major_blocks(sizes, width, groups, kind):
-    """Small batches of long, row-contiguous problems (a target-major matrix, 64+ targets each): the
-    launch that gives every problem a CTA and stages its rows in shared memory.  Indices and statuses
-    are compared with SciPy problem by problem."""
+@pytest.mark.parametrize("layout", ["target_major", "query_major"])
+def test_long_problems_one_cta_each(sizes, width, groups, kind, layout):
+    """Small batches of long problems (64+ solver rows): the launch that gives every problem a CTA,
+    stages its rows in shared memory (row-contiguous blocks directly, the others as a transposed copy,
+    partly in scratch when it does not fit) and runs its searches on all four warps.  Indices and
+    statuses are compared with SciPy problem by problem."""
     rng = np.random.default_rng(sum(sizes) + width + groups)
     m = _target_major_matrix(sizes, width, groups, kind, rng)
     dev = torch.device("cuda")
-    cost = torch.as_tensor(m, device=dev)
-    plan = matcher.plan_step(sizes, 1, groups * width, groups, m.shape[1], dev, _lib.LAYOUT_TARGET_MAJOR)
+    if layout == "target_major":
+        cost = torch.as_tensor(m, device=dev)
+        code = _lib.LAYOUT_TARGET_MAJOR
+    else:
+        cost = torch.as_tensor(np.ascontiguousarray(m.T), device=dev)
+        code = _lib.LAYOUT_QUERY_MAJOR
+    plan = matcher.plan_step(sizes, 1, groups * width, groups, cost.shape[1], dev, code)
     pairs = torch.empty((2, plan.total_pairs), dtype=torch.int64, device=dev)
     status = torch.empty(plan.problems.shape[0], dtype=torch.int32, device=dev)
     matcher.launch_lsap(cost, plan, pairs, status)

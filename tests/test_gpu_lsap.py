@@ -30,7 +30,10 @@ def _solve_dense(cost: np.ndarray, **kw) -> np.ndarray:
 
 @pytest.mark.parametrize("shape", [(520, 300, 1), (520, 300, 12), (520, 300, 37), (104, 300, 60),
                                    (8, 300, 300), (1, 16, 16), (3, 64, 0), (6, 300, 333), (4, 64, 16),
-                                   (3, 600, 40), (5, 40, 1000)])
+                                   (3, 600, 40), (5, 40, 1000),
+                                   # long problems: one four-warp CTA each at 1, 5 and 3 per SM (the
+                                   # last square, rows read in place), then too many for one wave
+                                   (140, 300, 90), (700, 300, 70), (300, 200, 200), (1300, 300, 66)])
 def test_dense_random(shape):
     rng = np.random.default_rng(sum(shape))
     cost = (rng.random(shape, dtype=np.float32) * 10 - 5).astype(np.float32)

@@ -95,7 +95,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration table (N = 1)")
     ap.add_argument("--config-cpu-seconds", type=float, default=2.0,
                     help="CPU time budget of each CPU leg of the per-configuration table")
-    ap.add_argument("--kernel", choices=["cost", "lsap", "label", "msda"], default=None,
+    ap.add_argument("--kernel", choices=["cost", "cost_qm", "lsap", "label", "msda"], default=None,
                     help="profiling mode: run only this kernel's workload a few times (for an ncu capture) and exit")
     return ap.parse_args()
 
@@ -1064,14 +1064,23 @@ def emit(line: dict) -> None:
 
 def run_kernel(name: str, workload: str = "sweep") -> None:
     """A few launches of one kernel on its benchmark workload, for an ncu capture of that kernel:
-    cost / lsap (the workload's step, issued as two calls), label (the classification loss forward and
+    cost / lsap (the workload's step, issued as two calls), cost_qm (the drop-in query-major cost
+    matrix, ``compute_compact_detection_cost_matrix``), label (the classification loss forward and
     backward on the workload's pairs), msda (deformable attention forward and backward, decoder
     geometry)."""
     from rfdetr_training_throughput_b200 import matcher, workloads
 
     dev = torch.device("cuda", 0)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
-    if name in ("cost", "lsap", "label"):
+    if name == "cost_qm":
+        wl = workloads.make(workload)
+        lg, bx = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)
+        tg = wl.targets_on(dev)
+        for _ in range(4):
+            matcher.compute_compact_detection_cost_matrix({"pred_logits": lg, "pred_boxes": bx}, tg,
+                                                         weights=wl.weights)
+            flush.zero_()
+    elif name in ("cost", "lsap", "label"):
         wl = workloads.make(workload)
         lg, bx = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)
         pk = matcher.PackedTargets.from_list(wl.targets_on(dev), dev)

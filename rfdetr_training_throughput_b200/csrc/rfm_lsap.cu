@@ -72,6 +72,7 @@ constexpr int kSmemPerCtaReserved = 1024;
 constexpr int kSmemPerBlockMax = 227 * 1024;
 constexpr int64_t kTileCapDefault = 16384;  // floats: 64 KB of staged cost per warp
 constexpr int kMaxWarpsPerCta = 4;
+
 // Solver variants: REGS keeps column duals and tie keys in registers; WIDE keeps
 // them in shared memory (large batches); EARLY is REGS with each scan's row
 // requested as soon as the row is known, before the previous step's
@@ -88,19 +89,35 @@ constexpr int kMaxWarpsPerCta = 4;
 // over the four warps.  MULTI_COPY is MULTI for batches whose solver rows are
 // not all contiguous in the source: those problems are staged as a transposed
 // copy, partly in scratch.
-enum Variant : int { kVarRegs = 0, kVarWide = 1, kVarEarly = 2, kVarCoop = 3, kVarMulti = 5, kVarMultiCopy = 6 };
+// MULTI_TWO and MULTI_COPY_TWO are the same with two warps per problem, for
+// waves of more than kMultiFourPerSm problems per SM.
+enum Variant : int {
+  kVarRegs = 0,
+  kVarWide = 1,
+  kVarEarly = 2,
+  kVarCoop = 3,
+  kVarMulti = 5,
+  kVarMultiCopy = 6,
+  kVarMultiTwo = 7,
+  kVarMultiCopyTwo = 8
+};
+__host__ __device__ constexpr bool multi_variant(int v) { return v >= kVarMulti && v <= kVarMultiCopyTwo; }
+__host__ __device__ constexpr bool copy_variant(int v) { return v == kVarMultiCopy || v == kVarMultiCopyTwo; }
+// Warps that share one problem's searches in a MULTI variant.
+__host__ __device__ constexpr int multi_warps(int v) { return (v == kVarMultiTwo || v == kVarMultiCopyTwo) ? 2 : 4; }
 // Variants with one problem per CTA; none exists for the 1024-column layout,
 // and neither does WIDE.
-__host__ __device__ constexpr bool cta_variant(int v) {
-  return v == kVarCoop || v == kVarMulti || v == kVarMultiCopy;
-}
+__host__ __device__ constexpr bool cta_variant(int v) { return v == kVarCoop || multi_variant(v); }
 __host__ __device__ constexpr bool narrow_only(int v) { return v == kVarWide || cta_variant(v); }
 constexpr int kEarlyMinRows = 64;
-// Batches of long problems (EARLY) with at most this many problems per SM run as
-// MULTI, when that many of its CTAs fit an SM (registers; the shared memory is
-// divided among them).  Beyond about eight, four warps per problem issue more
-// than one warp per problem would.
-constexpr int kMultiCtasPerSm = 8;
+// Batches of long problems (EARLY) that run in one wave of MULTI CTAs (their
+// shared memory divided among the CTAs an SM holds): four warps per problem up
+// to kMultiFourPerSm CTAs per SM, two warps up to kMultiTwoPerSm (or the CTAs
+// that fit, registers permitting).  Past four per SM four-warp problems issue
+// too much to share an SM well; two warps per problem then run their steps
+// faster than one warp does, up to the register file's limit.
+constexpr int kMultiFourPerSm = 4;
+constexpr int kMultiTwoPerSm = 16;
 // Batches with more than this many problems per SM use the wide layout.
 constexpr int kWideProblemsPerSm = 64;
 // Register budget.  The instantiations up to 320 columns run four CTAs of four
@@ -372,13 +389,14 @@ __device__ __forceinline__ int claim_next(const LsapArgs& a, int lane) {
   return (a.queue != nullptr && lane == 0) ? atomicAdd(a.queue, 1) + a.claim_base : 0;
 }
 
-// MULTI: the searches of one problem run on all four warps of its CTA.  Thread
-// t owns columns t, t + 128, t + 256 (K3 of them), so a scan step is K3
-// columns per thread instead of up to ten per lane; each warp reduces its
-// (path cost, key) minimum with redux.sync, lane 0 posts it to a shared slot
-// (double-buffered by step parity, so one barrier per step suffices: a warp
-// can only overwrite a slot after every warp has passed the next barrier, which
-// it reaches after reading the slot), and every thread combines the four posts.
+// MULTI: the searches of one problem run on all the warps of its CTA (four, or
+// two in the _TWO variants).  Thread t owns columns t, t + 32W, ... (K3 of
+// them), so a scan step is K3 columns per thread instead of up to ten per lane;
+// each warp reduces its (path cost, key) minimum with redux.sync, the lane
+// holding it posts it to a shared slot (double-buffered by step parity, so one
+// barrier per step suffices: a warp can only overwrite a slot after every warp
+// has passed the next barrier, which it reaches after reading the slot), and
+// every thread combines the W posts.
 // Every thread then holds the same argmin, so the rest of the step (next row,
 // swap-with-last removal of `remaining`, the tie key of the moved column) runs
 // without further exchange.  Same arithmetic and tie rule as the one-warp
@@ -414,34 +432,38 @@ __device__ __forceinline__ bool post_less(const double2& x, const double2& y) {
   return x.x < y.x || (x.x == y.x && kx < ky);
 }
 
-template <int K3>
+template <int K3, int kThreads>
 __device__ __forceinline__ void multi_row(const float* row, int t, unsigned mask, float (&cf)[K3]) {
 #pragma unroll
-  for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? row[t + 128 * k] : 0.0f;
+  for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? row[t + kThreads * k] : 0.0f;
 }
 
 // Rows in global memory: the read-only source (kLoadGlobal) or the scratch copy
 // this kernel wrote (kLoadScratch, read through L2).
-template <int K3, int L>
+template <int K3, int L, int kThreads>
 __device__ __forceinline__ void multi_row_global(const float* row, int t, unsigned mask, float (&cf)[K3]) {
 #pragma unroll
-  for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? load_cost<L>(row + t + 128 * k) : 0.0f;
+  for (int k = 0; k < K3; ++k) cf[k] = (mask & (1u << k)) ? load_cost<L>(row + t + kThreads * k) : 0.0f;
 }
 
 // Searches and commits every row of a problem whose costs are staged (rows
 // [0, staged) at `tile`, pitch nc) or read from `src` (row pitch rs; kWritten
-// when the rows are the scratch copy of this launch).  Called by all 128
+// when the rows are the scratch copy of this launch).  Called by all
 // threads after the load pass; returns the problem's status.
-template <int K3, bool kWritten>
+template <int K3, bool kWritten, int kWarps>
 __device__ int multi_search(const MultiShared& m, const float* tile, const float* src, int64_t rs, int staged,
                             int nr, int nc, bool bad) {
+  constexpr int kMultiWarps = kWarps;
+  constexpr int kMultiThreads = 32 * kWarps;
+  constexpr int kMultiShift = kWarps == 2 ? 6 : 7;
+  static_assert(kWarps == 2 || kWarps == 4, "two or four warps per problem");
   const int t = threadIdx.x;
   const int lane = t & 31;
   const int warp = t >> 5;
   unsigned valid = 0;
 #pragma unroll
   for (int k = 0; k < K3; ++k) {
-    if (t + 128 * k < nc) valid |= 1u << k;
+    if (t + kMultiThreads * k < nc) valid |= 1u << k;
   }
   unsigned freem = valid;
   double v[K3];
@@ -460,7 +482,7 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
         m.row4col[w] = static_cast<int16_t>(cur);
         m.col4row[cur] = static_cast<int16_t>(w);
       }
-      if ((w & 127) == t) freem &= ~(1u << (w >> 7));
+      if ((w & (kMultiThreads - 1)) == t) freem &= ~(1u << (w >> kMultiShift));
       __syncthreads();
       continue;
     }
@@ -469,7 +491,7 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
     unsigned key[K3];
 #pragma unroll
     for (int k = 0; k < K3; ++k) {
-      const int j = t + 128 * k;
+      const int j = t + kMultiThreads * k;
       const unsigned pos = static_cast<unsigned>(nc - 1 - j);
       spc[k] = CUDART_INF;
       const unsigned kv = (freem & (1u << k)) ? kKeyBase - 1u - pos : kKeyBase + pos;
@@ -485,9 +507,9 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
     float cf[K3];
     const auto issue_row = [&](int r) {
       if (r < staged) {
-        multi_row<K3>(tile + r * nc, t, rem, cf);
+        multi_row<K3, kMultiThreads>(tile + r * nc, t, rem, cf);
       } else {
-        multi_row_global<K3, kWritten ? kLoadScratch : kLoadGlobal>(src + r * rs, t, rem, cf);
+        multi_row_global<K3, kWritten ? kLoadScratch : kLoadGlobal, kMultiThreads>(src + r * rs, t, rem, cf);
       }
     };
     issue_row(cur);
@@ -501,7 +523,7 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
         unsigned rk[K3];
 #pragma unroll
         for (int k = 0; k < K3; ++k) {
-          const int j = t + 128 * k;
+          const int j = t + kMultiThreads * k;
           const bool live = (rem >> k) & 1u;
           const double r = ((minv + static_cast<double>(cf[k])) - ui) - v[k];
           const bool better = live && r < spc[k];
@@ -538,18 +560,23 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
           const unsigned mk = __reduce_min_sync(kFullMask, mine ? bk : kNoKey);
           mine = mine && bk == mk;
         }
-        if (mine) m.post[parity * 4 + warp] = make_double2(bv, key_as_double(bk));
+        if (mine) m.post[parity * kMultiWarps + warp] = make_double2(bv, key_as_double(bk));
       }
       __syncthreads();
       {
-        // fixed-shape tree over the four posts (keys are unique: any order agrees)
-        const double2 p0 = m.post[parity * 4 + 0], p1 = m.post[parity * 4 + 1];
-        const double2 p2 = m.post[parity * 4 + 2], p3 = m.post[parity * 4 + 3];
-        const double2 a = post_less(p1, p0) ? p1 : p0;
-        const double2 b = post_less(p3, p2) ? p3 : p2;
-        const double2 w = post_less(b, a) ? b : a;
-        bv = w.x;
-        bk = static_cast<unsigned>(__double_as_longlong(w.y));
+        // fixed-shape tree over the warps' posts (keys are unique: any order agrees)
+        double2 pw[kMultiWarps];
+#pragma unroll
+        for (int q = 0; q < kMultiWarps; ++q) pw[q] = m.post[parity * kMultiWarps + q];
+#pragma unroll
+        for (int stride = 1; stride < kMultiWarps; stride *= 2) {
+#pragma unroll
+          for (int q = 0; q + stride < kMultiWarps; q += 2 * stride) {
+            pw[q] = post_less(pw[q + stride], pw[q]) ? pw[q + stride] : pw[q];
+          }
+        }
+        bv = pw[0].x;
+        bk = static_cast<unsigned>(__double_as_longlong(pw[0].y));
       }
       parity ^= 1;
       if (bv == CUDART_INF) {
@@ -564,15 +591,15 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
       // swap-with-last removal; the write is read after the next step's barrier
       const int jl = m.rem[nrem - 1];
       if (t == 0) m.rem[ps] = static_cast<int16_t>(jl);
-      if ((jl & 127) == t) {
-        const int kl = jl >> 7;
+      if ((jl & (kMultiThreads - 1)) == t) {
+        const int kl = jl >> kMultiShift;
         const unsigned kv = ((freem >> kl) & 1u) ? kKeyBase - 1u - ps : kKeyBase + ps;
 #pragma unroll
         for (int k = 0; k < K3; ++k) {
           if (k == kl) key[k] = (kv << kTieShift) | (key[k] & ((1u << kTieShift) - 1u));
         }
       }
-      if ((js & 127) == t) rem &= ~(1u << (js >> 7));
+      if ((js & (kMultiThreads - 1)) == t) rem &= ~(1u << (js >> kMultiShift));
       --nrem;
       minv = bv;
       if (rj < 0) {
@@ -594,7 +621,7 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
 #pragma unroll
     for (int k = 0; k < K3; ++k) {
       if (visited & (1u << k)) {
-        const int j = t + 128 * k;
+        const int j = t + kMultiThreads * k;
         const double d = minv - spc[k];
         raised |= d < 0.0;
         if (j != sink) m.u[m.row4col[j]] += d;
@@ -620,16 +647,16 @@ __device__ int multi_search(const MultiShared& m, const float* tile, const float
       }
       *m.flag = flipped;
     }
-    if ((sink & 127) == t) freem &= ~(1u << (sink >> 7));
+    if ((sink & (kMultiThreads - 1)) == t) freem &= ~(1u << (sink >> kMultiShift));
 #pragma unroll
     for (int k = 0; k < K3; ++k) {
       const unsigned b = __ballot_sync(kFullMask, (visited >> k) & 1u);
-      if (lane == 0) m.vis[warp + 4 * k] = raised ? 0xffffffffu : b;
+      if (lane == 0) m.vis[warp + kMultiWarps * k] = raised ? 0xffffffffu : b;
     }
     __syncthreads();
     if (*m.flag == 0) code = RFM_STATUS_NO_SINK;
     // drop the pending picks this search visited (all of them if a dual went down)
-    for (int r = cur + 1 + t; r < nr; r += 32 * kMaxWarpsPerCta) {
+    for (int r = cur + 1 + t; r < nr; r += kMultiThreads) {
       const int pw = m.pick_w[r];
       if (pw >= 0 && ((m.vis[pw >> 5] >> (pw & 31)) & 1u)) m.pick_w[r] = -1;
     }
@@ -646,12 +673,13 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
                                              int lane) {
   constexpr int kCols = 32 * K;
   constexpr bool kWide = kVariant == kVarWide;
-  constexpr bool kCopy = kVariant == kVarMultiCopy;
-  constexpr bool kMulti = kVariant == kVarMulti || kCopy;
+  constexpr bool kCopy = copy_variant(kVariant);
+  constexpr bool kMulti = multi_variant(kVariant);
+  constexpr int kMultiWarps = multi_warps(kVariant);
   constexpr bool kStage = kMulti;  // rows [0, staged) kept in shared memory
   constexpr bool kEarly = kVariant == kVarEarly || kStage;
   constexpr bool kCoop = kVariant == kVarCoop || kStage;
-  constexpr int kLoadWarps = kCoop ? kMaxWarpsPerCta : 1;
+  constexpr int kLoadWarps = kMulti ? kMultiWarps : (kCoop ? kMaxWarpsPerCta : 1);
   const int warp = kCoop ? static_cast<int>(threadIdx.x >> 5) : 0;
   int64_t cost_off, out_off, scratch_off;
   int nq, nt, qbase;
@@ -798,7 +826,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
     const bool scratch_ok = staged == nr || (scratch_off >= 0 && a.workspace != nullptr);
     const int copied = scratch_ok ? nr : staged;
     bad = !scratch_ok;
-    for (int j = warp; j < nc; j += kMaxWarpsPerCta) {
+    for (int j = warp; j < nc; j += kMultiWarps) {
       for (int i = lane; i < copied; i += 32) {
         const float x = __ldg(src + i * s.rs + j * s.cs);
         if (i < staged) {
@@ -809,7 +837,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
       }
     }
     __syncthreads();
-    for (int i = warp; i < copied; i += kMaxWarpsPerCta) {
+    for (int i = warp; i < copied; i += kMultiWarps) {
       float x[K];
 #pragma unroll
       for (int k = 0; k < K; ++k) {
@@ -867,18 +895,18 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   unsigned freem = valid;
   int code = bad ? RFM_STATUS_INVALID : RFM_STATUS_OK;
   if constexpr (kMulti) {
-    constexpr int K3 = (32 * K + 127) / 128;
+    constexpr int K3 = (K + kMultiWarps - 1) / kMultiWarps;
     unsigned char* post = base + slot - kMultiPostBytes;
     const MultiShared ms{u_s, pick_m_s, col4row_s, pick_w_s, row4col_s, path_s, rem_s, vis_s,
                          reinterpret_cast<double2*>(post), reinterpret_cast<int*>(post + 128)};
     if constexpr (kCopy) {
       if (s.cs == 1) {
-        code = multi_search<K3, false>(ms, tile, src, s.rs, staged, nr, nc, bad);
+        code = multi_search<K3, false, kMultiWarps>(ms, tile, src, s.rs, staged, nr, nc, bad);
       } else {
-        code = multi_search<K3, true>(ms, tile, a.workspace + scratch_off, nc, staged, nr, nc, bad);
+        code = multi_search<K3, true, kMultiWarps>(ms, tile, a.workspace + scratch_off, nc, staged, nr, nc, bad);
       }
     } else {
-      code = multi_search<K3, false>(ms, tile, src, s.rs, staged, nr, nc, bad);
+      code = multi_search<K3, false, kMultiWarps>(ms, tile, src, s.rs, staged, nr, nc, bad);
     }
     if (warp != 0) return 0;
 #pragma unroll
@@ -1142,6 +1170,8 @@ const void* pair_kernel(int cols_per_lane, int variant) {
       if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarCoop>);
       if (variant == kVarMulti) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMulti>);
       if (variant == kVarMultiCopy) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMultiCopy>);
+      if (variant == kVarMultiTwo) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMultiTwo>);
+      if (variant == kVarMultiCopyTwo) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMultiCopyTwo>);
       return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarRegs>);
     case 10:
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarWide>);
@@ -1149,6 +1179,8 @@ const void* pair_kernel(int cols_per_lane, int variant) {
       if (variant == kVarCoop) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarCoop>);
       if (variant == kVarMulti) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMulti>);
       if (variant == kVarMultiCopy) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMultiCopy>);
+      if (variant == kVarMultiTwo) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMultiTwo>);
+      if (variant == kVarMultiCopyTwo) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMultiCopyTwo>);
       return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarRegs>);
     case 32:
       if (narrow_only(variant)) return nullptr;
@@ -1199,15 +1231,16 @@ bool ensure_dynamic_smem(const void* fn, int64_t smem) {
   return true;
 }
 
-// CTAs of a solver kernel that fit on one SM at this shared-memory size.
-int query_resident_ctas(const void* fn, int64_t smem) {
+// CTAs of a solver kernel (CTAs of `threads`) that fit on one SM at this
+// shared-memory size.
+int query_resident_ctas(const void* fn, int64_t smem, int threads) {
   if (fn == nullptr) return 0;
   if (!ensure_dynamic_smem(fn, smem)) {
     cudaGetLastError();
     return 0;
   }
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, 32 * kMaxWarpsPerCta,
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads,
                                                     static_cast<size_t>(smem)) != cudaSuccess) {
     cudaGetLastError();
     return 0;
@@ -1228,7 +1261,7 @@ struct OccupancyEntry {
 std::mutex g_occupancy_mutex;
 std::vector<OccupancyEntry> g_occupancy;
 
-int resident_ctas(const void* fn, int64_t smem) {
+int resident_ctas(const void* fn, int64_t smem, int threads = 32 * kMaxWarpsPerCta) {
   if (fn == nullptr) return 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -1243,7 +1276,7 @@ int resident_ctas(const void* fn, int64_t smem) {
       }
     }
   }
-  const int n = query_resident_ctas(fn, smem);
+  const int n = query_resident_ctas(fn, smem, threads);
   if (n > 0) {
     std::lock_guard<std::mutex> lock(g_occupancy_mutex);
     g_occupancy.push_back({dev, fn, smem, n});
@@ -1423,28 +1456,42 @@ extern "C" int rfm_lsap_make_plan(rfm_problem* host_problems, int num_problems, 
 
 namespace rfm {
 namespace {
-// Shared memory of one CTA of the MULTI kernel `fn` when a batch of
-// `num_problems` runs as one wave of them: ceil(P / SMs) CTAs per SM, each
-// taking that share of the SM.  0 when the batch is larger than
-// kMultiCtasPerSm per SM, when that many CTAs do not fit (registers), or when
-// the share does not hold the problem's `fixed` arrays and the step posts.
-int multi_slot_bytes(int num_problems, const void* fn, int64_t fixed) {
+// A MULTI launch for a batch of `num_problems` as one wave: ceil(P / SMs) CTAs
+// per SM, each taking that share of the SM's shared memory (`slot` bytes),
+// with four warps per problem (`fn4`) up to kMultiFourPerSm per SM and two
+// (`fn2`) beyond.  `slot` is 0 when the batch is larger than kMultiTwoPerSm per
+// SM, when that many CTAs do not fit (registers), or when the share does not
+// hold the problem's `fixed` arrays and the step posts.
+struct MultiLaunch {
+  int slot;
+  bool two;
+};
+
+MultiLaunch multi_launch(int num_problems, const void* fn4, const void* fn2, int64_t fixed) {
   const int sms = device_sm_count();
-  if (fn == nullptr || sms < 1 || num_problems < 1 ||
-      static_cast<int64_t>(num_problems) > static_cast<int64_t>(kMultiCtasPerSm) * sms) {
-    return 0;
+  if (sms < 1 || num_problems < 1 ||
+      static_cast<int64_t>(num_problems) > static_cast<int64_t>(kMultiTwoPerSm) * sms) {
+    return {0, false};
   }
   const int per_sm = (num_problems + sms - 1) / sms;
   // whole KB, so that per_sm shares plus their reservations fit the SM
   int smem = (kSmemPerSm / per_sm - kSmemPerCtaReserved) / 1024 * 1024;
   if (smem > kSmemPerBlockMax) smem = kSmemPerBlockMax;
-  if (fixed + kMultiPostBytes > smem) return 0;
-  return resident_ctas(fn, smem) >= per_sm ? smem : 0;
+  if (fixed + kMultiPostBytes > smem) return {0, false};
+  if (per_sm <= kMultiFourPerSm && resident_ctas(fn4, smem, 128) >= per_sm) return {smem, false};
+  if (resident_ctas(fn2, smem, 64) >= per_sm) return {smem, true};
+  return {0, false};
 }
 
-const void* dense_multi_kernel(int cols_per_lane) {
-  if (cols_per_lane == 4) return reinterpret_cast<const void*>(&lsap_kernel<4, true, kVarMultiCopy>);
-  if (cols_per_lane == 10) return reinterpret_cast<const void*>(&lsap_kernel<10, true, kVarMultiCopy>);
+const void* dense_multi_kernel(int cols_per_lane, bool two) {
+  if (cols_per_lane == 4) {
+    return two ? reinterpret_cast<const void*>(&lsap_kernel<4, true, kVarMultiCopyTwo>)
+               : reinterpret_cast<const void*>(&lsap_kernel<4, true, kVarMultiCopy>);
+  }
+  if (cols_per_lane == 10) {
+    return two ? reinterpret_cast<const void*>(&lsap_kernel<10, true, kVarMultiCopyTwo>)
+               : reinterpret_cast<const void*>(&lsap_kernel<10, true, kVarMultiCopy>);
+  }
   return nullptr;
 }
 
@@ -1490,21 +1537,25 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   a.status = status;
   const bool early = plan->max_rows >= kEarlyMinRows;
   if (!persistent) {
-    const int slot = early && plan->cols_per_lane <= 10
-                         ? multi_slot_bytes(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMultiCopy),
-                                            fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
-                         : 0;
-    if (slot > 0) {
+    const MultiLaunch ml =
+        early && plan->cols_per_lane <= 10
+            ? multi_launch(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMultiCopy),
+                           pair_kernel(plan->cols_per_lane, kVarMultiCopyTwo),
+                           fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
+            : MultiLaunch{0, false};
+    if (ml.slot > 0) {
       // a one-wave batch of long problems, some not row-contiguous: MULTI_COPY.
       // Every tile above the plan's cap has scratch, so it runs when its shared
       // memory holds that cap.
       const int64_t room =
-          (slot - fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows) - kMultiPostBytes) / 4;
+          (ml.slot - fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows) - kMultiPostBytes) / 4;
       if (plan->tile_cap_floats <= room) {
-        a.slot = slot;
+        a.slot = ml.slot;
         a.tile_cap = static_cast<int>(room);
-        return launch<false, kVarMultiCopy>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, slot,
-                                            stream);
+        if (ml.two) {
+          return launch<false, kVarMultiCopyTwo>(a, plan->cols_per_lane, plan->num_problems, 2, ml.slot, stream);
+        }
+        return launch<false, kVarMultiCopy>(a, plan->cols_per_lane, plan->num_problems, 4, ml.slot, stream);
       }
     }
     if (early) {
@@ -1518,16 +1569,20 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   // large batches (more problems than 64 per SM) take the wide layout, batches of
   // long problems the early-load variant.
   const int sms = device_sm_count();
-  const int multi_slot = early && plan->cols_per_lane <= 10
-                             ? multi_slot_bytes(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMulti),
-                                                fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
-                             : 0;
-  if (multi_slot > 0) {
+  const MultiLaunch ml = early && plan->cols_per_lane <= 10
+                             ? multi_launch(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMulti),
+                                            pair_kernel(plan->cols_per_lane, kVarMultiTwo),
+                                            fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
+                             : MultiLaunch{0, false};
+  if (ml.slot > 0) {
     // a one-wave batch of long problems: MULTI, its rows staged as far as they fit
-    a.slot = multi_slot;
+    a.slot = ml.slot;
     a.tile_cap = (a.slot - static_cast<int>(fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))) / 4;
-    return launch<false, kVarMulti>(a, plan->cols_per_lane, plan->num_problems, kMaxWarpsPerCta, a.slot, stream,
-                                    counter_zeroed);
+    if (ml.two) {
+      return launch<false, kVarMultiTwo>(a, plan->cols_per_lane, plan->num_problems, 2, a.slot, stream,
+                                         counter_zeroed);
+    }
+    return launch<false, kVarMulti>(a, plan->cols_per_lane, plan->num_problems, 4, a.slot, stream, counter_zeroed);
   }
   const bool wide = plan->cols_per_lane <= 10 &&
                     static_cast<int64_t>(plan->num_problems) > static_cast<int64_t>(kWideProblemsPerSm) * sms;
@@ -1671,15 +1726,17 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   if (dp.max_rows >= kEarlyMinRows && dp.cpl <= 10) {
     // a one-wave batch of long problems: MULTI_COPY when every tile either fits
     // its CTA's shared memory or has scratch
-    const int slot =
-        multi_slot_bytes(num_problems, dense_multi_kernel(dp.cpl), fixed_warp_bytes(32 * dp.cpl, dp.max_rows));
+    const MultiLaunch ml = multi_launch(num_problems, dense_multi_kernel(dp.cpl, false),
+                                        dense_multi_kernel(dp.cpl, true), fixed_warp_bytes(32 * dp.cpl, dp.max_rows));
     const Shape s = solver_shape(num_workers, num_tasks, num_tasks, 1);
-    const int64_t room = slot > 0 ? (slot - fixed_warp_bytes(32 * dp.cpl, dp.max_rows) - kMultiPostBytes) / 4 : 0;
+    const int64_t room =
+        ml.slot > 0 ? (ml.slot - fixed_warp_bytes(32 * dp.cpl, dp.max_rows) - kMultiPostBytes) / 4 : 0;
     // (row-contiguous problems read their unstaged rows from the source)
-    if (slot > 0 && (static_cast<int64_t>(s.nr) * s.nc <= room || s.cs == 1 || dp.scratch_bytes > 0)) {
-      a.slot = slot;
+    if (ml.slot > 0 && (static_cast<int64_t>(s.nr) * s.nc <= room || s.cs == 1 || dp.scratch_bytes > 0)) {
+      a.slot = ml.slot;
       a.tile_cap = static_cast<int>(room);
-      return launch<true, kVarMultiCopy>(a, dp.cpl, num_problems, kMaxWarpsPerCta, slot, stream);
+      if (ml.two) return launch<true, kVarMultiCopyTwo>(a, dp.cpl, num_problems, 2, ml.slot, stream);
+      return launch<true, kVarMultiCopy>(a, dp.cpl, num_problems, 4, ml.slot, stream);
     }
   }
   const int ctas = (num_problems + dp.warps - 1) / dp.warps;

@@ -95,7 +95,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration table (N = 1)")
     ap.add_argument("--config-cpu-seconds", type=float, default=2.0,
                     help="CPU time budget of each CPU leg of the per-configuration table")
-    ap.add_argument("--kernel", choices=["cost", "cost_qm", "lsap", "label", "msda"], default=None,
+    ap.add_argument("--kernel", choices=["cost", "cost_qm", "lsap", "label", "box", "msda"], default=None,
                     help="profiling mode: run only this kernel's workload a few times (for an ncu capture) and exit")
     return ap.parse_args()
 
@@ -1065,9 +1065,9 @@ def emit(line: dict) -> None:
 def run_kernel(name: str, workload: str = "sweep") -> None:
     """A few launches of one kernel on its benchmark workload, for an ncu capture of that kernel:
     cost / lsap (the workload's step, issued as two calls), cost_qm (the drop-in query-major cost
-    matrix, ``compute_compact_detection_cost_matrix``), label (the classification loss forward and
-    backward on the workload's pairs), msda (deformable attention forward and backward, decoder
-    geometry)."""
+    matrix, ``compute_compact_detection_cost_matrix``), label / box (the classification or the
+    matched-box loss, forward and backward, on the workload's pairs), msda (deformable attention
+    forward and backward, decoder geometry)."""
     from rfdetr_training_throughput_b200 import matcher, workloads
 
     dev = torch.device("cuda", 0)
@@ -1080,13 +1080,22 @@ def run_kernel(name: str, workload: str = "sweep") -> None:
             matcher.compute_compact_detection_cost_matrix({"pred_logits": lg, "pred_boxes": bx}, tg,
                                                          weights=wl.weights)
             flush.zero_()
-    elif name in ("cost", "lsap", "label"):
+    elif name in ("cost", "lsap", "label", "box"):
         wl = workloads.make(workload)
         lg, bx = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)
         pk = matcher.PackedTargets.from_list(wl.targets_on(dev), dev)
         for _ in range(4):
             res = matcher.match_packed(lg, bx, pk, wl.group_detr, weights=wl.weights, events={})
             flush.zero_()
+        if name == "box":
+            from rfdetr_training_throughput_b200.loss import matched_box_losses
+
+            b = bx.clone().requires_grad_(True)
+            for _ in range(3):
+                b.grad = None
+                l1, giou = matched_box_losses(b, pk, res)
+                (l1.sum() + giou.sum()).backward()
+                flush.zero_()
         if name == "label":
             from rfdetr_training_throughput_b200.loss import matched_label_losses
 

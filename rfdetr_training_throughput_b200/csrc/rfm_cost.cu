@@ -315,17 +315,24 @@ __device__ __forceinline__ void load_raw(PredRaw<NCLS>& r, const CostArgs& a, in
   }
 }
 
+__device__ __forceinline__ void st_shared(unsigned addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 // Costs of targets [c_begin, c_end) of one image run against the thread's two
 // queries: one 8-byte store per target row of the target-major matrix, or
-// (kQM) two 4-byte stores into the CTA's query-major shared-memory tile.
+// (kQM) two 4-byte stores into the CTA's query-major shared-memory tile, whose
+// thread rows start at the shared-memory byte address `tile` (32-bit shared
+// addressing: the tile's stores need no 64-bit address arithmetic).
 template <int NCLS, bool kUnclamped, bool kTail, bool kQM>
 __device__ __forceinline__ void cost_targets(const TargetRow* s_t, int c_begin, int c_end, float* out_row,
                                              const PredPair& p01, const float2 (&wcls01)[kSmallClasses],
-                                             int q0, int64_t pbase, const CostArgs& a, float* tile, int pitch) {
-  float* dst = kQM ? tile + c_begin : out_row + static_cast<int64_t>(c_begin) * a.ld;
-  const int64_t step = kQM ? 1 : a.ld;
+                                             int q0, int64_t pbase, const CostArgs& a, unsigned tile, int pitch) {
+  float* dst = kQM ? nullptr : out_row + static_cast<int64_t>(c_begin) * a.ld;
+  const int64_t step = kQM ? 0 : a.ld;
+  unsigned sdst = tile + 4u * static_cast<unsigned>(c_begin);
 #pragma unroll 2
-  for (int c = c_begin; c < c_end; ++c, dst += step) {
+  for (int c = c_begin; c < c_end; ++c, dst += step, sdst += 4u) {
     const TargetRow t = s_t[c];
     float2 w01;
     if (NCLS > 0) {
@@ -344,8 +351,8 @@ __device__ __forceinline__ void cost_targets(const TargetRow* s_t, int c_begin, 
     }
     float2 r01 = pair_cost2<kUnclamped>(p01, t, w01, a);
     if (kQM) {  // rows of queries q0 and q0 + 1 of the tile (a query past Q is never written out)
-      dst[0] = r01.x;
-      dst[pitch] = r01.y;
+      st_shared(sdst, r01.x);
+      st_shared(sdst + 4u * static_cast<unsigned>(pitch), r01.y);
     } else {
       if (kTail && q0 + 2 > a.Q) {  // zero the pad queries (q >= Q, up to ld) of the last tile
         if (q0 >= a.Q) r01.x = 0.f;
@@ -453,7 +460,8 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
   const int nseg = (kQM && q0 >= a.Q) ? 0 : s_nseg;  // query-major: queries past Q are not computed
   const bool all_plain = s_all_plain != 0;
   float* out_row = kQM ? nullptr : a.out + (static_cast<int64_t>(layer) * a.S + c_begin) * a.ld + q0;
-  float* tile_row = s_tile + (kQM ? tid * kQpt * kPitch : 0);
+  const unsigned tile_row =
+      static_cast<unsigned>(__cvta_generic_to_shared(s_tile)) + (kQM ? 4u * tid * kQpt * kPitch : 0u);
   for (int sg = 0; sg < nseg; ++sg) {
     const int img = s_t[s_seg[sg]].image;
     const int64_t pbase = (layer_base + img) * a.Q;
@@ -485,12 +493,19 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
     // the tile out, query-major: warp w writes query rows w, w + 4, ...; lane c
     // column c_begin + c (the row's real columns, then its pad columns with 0)
     __syncthreads();
+    static_assert(!kQM || kCols <= 32, "one column per lane");
     const int width = static_cast<int>(min(static_cast<int64_t>(kCols), a.ld - c_begin));
     const int qt0 = blockIdx.y * kTmThreads * kQpt;
     const int lane = tid & 31, warp = tid >> 5;
-    for (int ql = warp; ql < kTmThreads * kQpt && qt0 + ql < a.Q; ql += kTmThreads / 32) {
-      float* dst = a.out + (static_cast<int64_t>(layer) * a.Q + qt0 + ql) * a.ld + c_begin;
-      for (int c = lane; c < width; c += 32) dst[c] = c < n ? s_tile[ql * kPitch + c] : 0.0f;
+    const int rows = min(kTmThreads * kQpt, a.Q - qt0);
+    constexpr int kWarps = kTmThreads / 32;
+    if (lane < width) {
+      float* dst = a.out + (static_cast<int64_t>(layer) * a.Q + qt0 + warp) * a.ld + c_begin + lane;
+      const int64_t row_step = kWarps * a.ld;
+      const float* src = s_tile + warp * kPitch + lane;
+      for (int ql = warp; ql < rows; ql += kWarps, dst += row_step, src += kWarps * kPitch) {
+        *dst = lane < n ? *src : 0.0f;
+      }
     }
   }
 }

@@ -128,6 +128,7 @@ def _target_major_matrix(sizes, width, groups, kind, rng):
     ((99, 80, 64, 70), 100, 4, "ties2"),  # at most 128 columns
     ((220, 150, 90), 300, 2, "inf"),
     (tuple(range(64, 124, 3)), 300, 13, "ties8"),  # 260 problems: two per SM
+    (tuple(range(64, 114)), 300, 13, "uniform"),  # 650 problems: five per SM, two warps each
     ((300, 180, 90), 300, 2, "ties4"),  # square problems: solver rows run across the target-major rows
 ])
 @pytest.mark.parametrize("layout", ["target_major", "query_major"])

@@ -826,8 +826,19 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
     const bool scratch_ok = staged == nr || (scratch_off >= 0 && a.workspace != nullptr);
     const int copied = scratch_ok ? nr : staged;
     bad = !scratch_ok;
-    for (int j = warp; j < nc; j += kMultiWarps) {
-      for (int i = lane; i < copied; i += 32) {
+    // element e = j * copied + i, every thread striding by the CTA's size; the
+    // (i, j) of the next element follow by carrying, without a division
+    constexpr int kStride = 32 * kMultiWarps;
+    if (copied > 0) {
+      const int di = kStride % copied, dj = kStride / copied;
+      int i = static_cast<int>(threadIdx.x) % copied;
+      int j = static_cast<int>(threadIdx.x) / copied;
+      for (; j < nc; i += di, j += dj) {
+        if (i >= copied) {
+          i -= copied;
+          ++j;
+          if (j >= nc) break;
+        }
         const float x = __ldg(src + i * s.rs + j * s.cs);
         if (i < staged) {
           tile[i * nc + j] = x;
@@ -1538,7 +1549,7 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   const bool early = plan->max_rows >= kEarlyMinRows;
   if (!persistent) {
     const MultiLaunch ml =
-        early && plan->cols_per_lane <= 10
+        (early || plan->num_problems <= kMultiFourPerSm * device_sm_count()) && plan->cols_per_lane <= 10
             ? multi_launch(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMultiCopy),
                            pair_kernel(plan->cols_per_lane, kVarMultiCopyTwo),
                            fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
@@ -1569,7 +1580,7 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   // large batches (more problems than 64 per SM) take the wide layout, batches of
   // long problems the early-load variant.
   const int sms = device_sm_count();
-  const MultiLaunch ml = early && plan->cols_per_lane <= 10
+  const MultiLaunch ml = (early || plan->num_problems <= kMultiFourPerSm * sms) && plan->cols_per_lane <= 10
                              ? multi_launch(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMulti),
                                             pair_kernel(plan->cols_per_lane, kVarMultiTwo),
                                             fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
@@ -1723,7 +1734,7 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.q_out = matching;
   a.t_out = nullptr;
   a.status = status;
-  if (dp.max_rows >= kEarlyMinRows && dp.cpl <= 10) {
+  if ((dp.max_rows >= kEarlyMinRows || num_problems <= kMultiFourPerSm * device_sm_count()) && dp.cpl <= 10) {
     // a one-wave batch of long problems: MULTI_COPY when every tile either fits
     // its CTA's shared memory or has scratch
     const MultiLaunch ml = multi_launch(num_problems, dense_multi_kernel(dp.cpl, false),

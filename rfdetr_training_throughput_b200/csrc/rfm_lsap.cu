@@ -826,27 +826,57 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
     const bool scratch_ok = staged == nr || (scratch_off >= 0 && a.workspace != nullptr);
     const int copied = scratch_ok ? nr : staged;
     bad = !scratch_ok;
-    // element e = j * copied + i, every thread striding by the CTA's size; the
-    // (i, j) of the next element follow by carrying, without a division
+    // Each part is walked as elements e = j * rows + i, every thread striding by
+    // the CTA's size; the (i, j) of the next element follow by carrying, without
+    // a division.  Rows [0, on_chip) go to the tile by cp.async (every request
+    // in flight before one wait); rows [on_chip, copied) go to scratch, four
+    // loads in flight per thread.
     constexpr int kStride = 32 * kMultiWarps;
-    if (copied > 0) {
-      const int di = kStride % copied, dj = kStride / copied;
-      int i = static_cast<int>(threadIdx.x) % copied;
-      int j = static_cast<int>(threadIdx.x) / copied;
+    const int on_chip = staged < copied ? staged : copied;
+    if (on_chip > 0) {
+      const int di = kStride % on_chip, dj = kStride / on_chip;
+      int i = static_cast<int>(threadIdx.x) % on_chip;
+      int j = static_cast<int>(threadIdx.x) / on_chip;
       for (; j < nc; i += di, j += dj) {
-        if (i >= copied) {
-          i -= copied;
+        if (i >= on_chip) {
+          i -= on_chip;
           ++j;
           if (j >= nc) break;
         }
-        const float x = __ldg(src + i * s.rs + j * s.cs);
-        if (i < staged) {
-          tile[i * nc + j] = x;
-        } else {
-          scratch[static_cast<int64_t>(i) * nc + j] = x;
+        cp_async4(tile + i * nc + j, src + i * s.rs + j * s.cs);
+      }
+    }
+    const int off_chip = copied - on_chip;
+    if (off_chip > 0) {
+      const int di = kStride % off_chip, dj = kStride / off_chip;
+      int i = static_cast<int>(threadIdx.x) % off_chip;
+      int j = static_cast<int>(threadIdx.x) / off_chip;
+      while (j < nc) {
+        float x[4];
+        int64_t at[4];
+        int count = 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (j < nc) {
+            const int r = on_chip + i;
+            x[u] = __ldg(src + r * s.rs + j * s.cs);
+            at[u] = static_cast<int64_t>(r) * nc + j;
+            count = u + 1;
+          }
+          i += di;
+          j += dj;
+          if (i >= off_chip) {
+            i -= off_chip;
+            ++j;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (u < count) scratch[at[u]] = x[u];
         }
       }
     }
+    cp_async_wait_all();
     __syncthreads();
     for (int i = warp; i < copied; i += kMultiWarps) {
       float x[K];

@@ -33,7 +33,8 @@ def _solve_dense(cost: np.ndarray, **kw) -> np.ndarray:
                                    (3, 600, 40), (5, 40, 1000),
                                    # long problems: one four-warp CTA each at 1, 5 and 3 per SM (the
                                    # last square, rows read in place), then too many for one wave
-                                   (140, 300, 90), (700, 300, 70), (300, 200, 200), (1300, 300, 66)])
+                                   (140, 300, 90), (700, 300, 70), (300, 200, 200), (1300, 300, 66),
+                                   (700, 100, 64)])
 def test_dense_random(shape):
     rng = np.random.default_rng(sum(shape))
     cost = (rng.random(shape, dtype=np.float32) * 10 - 5).astype(np.float32)
@@ -129,6 +130,7 @@ def _target_major_matrix(sizes, width, groups, kind, rng):
     ((220, 150, 90), 300, 2, "inf"),
     (tuple(range(64, 124, 3)), 300, 13, "ties8"),  # 260 problems: two per SM
     (tuple(range(64, 114)), 300, 13, "uniform"),  # 650 problems: five per SM, two warps each
+    (tuple(range(64, 100)), 100, 20, "ties4"),  # 720 problems of at most 128 columns, two warps each
     ((300, 180, 90), 300, 2, "ties4"),  # square problems: solver rows run across the target-major rows
 ])
 @pytest.mark.parametrize("layout", ["target_major", "query_major"])

@@ -11,8 +11,10 @@
  *              (patches.py:123-149).
  *
  *   rfm_lsap   solves a batch of rectangular linear assignment problems read
- *              in place from that matrix, one warp per problem, with the exact
- *              arithmetic and tie-breaking of SciPy's rectangular_lsap, and
+ *              in place from that matrix (one warp per problem for large
+ *              batches; a CTA of two or four warps per problem when the batch
+ *              runs in one wave), with the exact arithmetic and tie-breaking of
+ *              SciPy's rectangular_lsap, and
  *              writes the (query, target) index pairs straight into their
  *              final packed position. Replaces batch_lap / lsap_kernel
  *              (kernels_lap.py:271-305, :332-355) together with the device

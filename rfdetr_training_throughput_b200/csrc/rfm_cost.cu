@@ -29,12 +29,16 @@
 // a packed multiply feeding a packed add into an FMA even with .rn, so every
 // product that is added to something is written as an explicit FMA, in both
 // layouts: union = fma(-iw, ih, area_p + area_t), hull - union, the GIoU
-// difference and the weighted sum.  The L1 and intersection terms follow the
-// reference chain (kernels_matcher.py:98-120); the hull extents use the interval
-// identity max(a1,b1) - min(a0,b0) = (a1-a0) + (b1-b0) - (min(a1,b1) -
-// max(a0,b0)); quotients are a * rcp(b); the focal term uses fast exp/log.  All
-// of it is well inside the 1e-5 relative bar, and both layouts come out of the
-// same code, so they hold bit-identical matrices.
+// difference and the weighted sum.  The L1 term follows the reference chain
+// (kernels_matcher.py:98-120) bit for bit, and so do the boxes' areas.  The
+// intersection and hull extents come from the same centre and half-width
+// differences as L1, by the interval identities min(a1,b1) - max(a0,b0) =
+// ha + hb - max(|ca - cb|, |ha - hb|) and max(a1,b1) - min(a0,b0) = ha + hb +
+// max(|ca - cb|, |ha - hb|) (centres c, half-widths h): the reference's corner
+// min/max, rounded differently (within an ulp of the coordinates).  Quotients
+// are a * rcp(b); the focal term uses fast exp/log.  All of it is well inside
+// the 1e-5 relative bar, and both layouts come out of the same code, so they
+// hold bit-identical matrices.
 #include "rfm_common.cuh"
 
 namespace rfm {
@@ -198,38 +202,30 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
 }
 __device__ __forceinline__ float2 dup2(float x) { return make_float2(x, x); }
 
-// Shared per-target data (48 bytes; read as broadcasts).
+// Shared per-target data of the inner loop (32 bytes, two broadcast loads).
 struct TargetRow {
-  float4 box;  // cx, cy, w, h
-  float4 xy;   // x0, y0, x1, y1
-  float area;
+  float4 box;  // cx, cy, w / 2, h / 2
+  float area;  // of the xyxy corners, as box_area computes it
   int label;
   int image;
   int plain;   // w >= 0, h >= 0 and area >= 2e-7: the clamps are no-ops
-  float tw, th;  // corner extents x1 - x0, y1 - y0
-  float pad0, pad1;
 };
 
-// Prediction data of one pair of queries of one image.
+// Prediction data of one pair of queries of one image: centres, half extents
+// and the corners' area.
 struct PredPair {
-  float2 cx, cy, w, h, x0, y0, x1, y1, area, pw, ph;
+  float2 cx, cy, hw, hh, area;
 };
 
 __device__ __forceinline__ PredPair pred_pair(const float4 a, const float4 b) {
   PredPair p;
   p.cx = make_float2(a.x, b.x);
   p.cy = make_float2(a.y, b.y);
-  p.w = make_float2(a.z, b.z);
-  p.h = make_float2(a.w, b.w);
-  const float2 hw = mul2(dup2(0.5f), p.w);
-  const float2 hh = mul2(dup2(0.5f), p.h);
-  p.x0 = sub2(p.cx, hw);
-  p.y0 = sub2(p.cy, hh);
-  p.x1 = add2(p.cx, hw);
-  p.y1 = add2(p.cy, hh);
-  p.pw = sub2(p.x1, p.x0);
-  p.ph = sub2(p.y1, p.y0);
-  p.area = mul2(p.pw, p.ph);
+  p.hw = mul2(dup2(0.5f), make_float2(a.z, b.z));
+  p.hh = mul2(dup2(0.5f), make_float2(a.w, b.w));
+  const float2 pw = sub2(add2(p.cx, p.hw), sub2(p.cx, p.hw));
+  const float2 ph = sub2(add2(p.cy, p.hh), sub2(p.cy, p.hh));
+  p.area = mul2(pw, ph);
   return p;
 }
 
@@ -265,21 +261,28 @@ __device__ __forceinline__ float2 pair_cost2(const PredPair& p, const TargetRow&
                                              const CostArgs& a) {
   const float2 dcx = sub2(p.cx, dup2(t.box.x));
   const float2 dcy = sub2(p.cy, dup2(t.box.y));
-  const float2 dw = sub2(p.w, dup2(t.box.z));
-  const float2 dh = sub2(p.h, dup2(t.box.w));
-  const float2 l1 = make_float2(((fabsf(dcx.x) + fabsf(dcy.x)) + fabsf(dw.x)) + fabsf(dh.x),
-                                ((fabsf(dcx.y) + fabsf(dcy.y)) + fabsf(dw.y)) + fabsf(dh.y));
-  const float2 iw = sub2(make_float2(fminf(p.x1.x, t.xy.z), fminf(p.x1.y, t.xy.z)),
-                         make_float2(fmaxf(p.x0.x, t.xy.x), fmaxf(p.x0.y, t.xy.x)));
-  const float2 ih = sub2(make_float2(fminf(p.y1.x, t.xy.w), fminf(p.y1.y, t.xy.w)),
-                         make_float2(fmaxf(p.y0.x, t.xy.y), fmaxf(p.y0.y, t.xy.y)));
+  const float2 dhx = sub2(p.hw, dup2(t.box.z));
+  const float2 dhy = sub2(p.hh, dup2(t.box.w));
+  // L1 over cxcywh in the reference's order ((|dcx| + |dcy|) + |dw|) + |dh|;
+  // |dw| = 2 |dw / 2| exactly (halving and doubling are exact for normal floats)
+  const float2 l1 = make_float2(
+      __fmaf_rn(2.0f, fabsf(dhy.x), __fmaf_rn(2.0f, fabsf(dhx.x), __fadd_rn(fabsf(dcx.x), fabsf(dcy.x)))),
+      __fmaf_rn(2.0f, fabsf(dhy.y), __fmaf_rn(2.0f, fabsf(dhx.y), __fadd_rn(fabsf(dcx.y), fabsf(dcy.y)))));
+  // Two intervals of half-widths a and b whose centres are d apart overlap by
+  // a + b - max(|d|, |a - b|) and span a + b + max(|d|, |a - b|) (the min/max
+  // of their corners, rewritten): both extents come from the L1 differences.
+  const float2 mx = make_float2(fmaxf(fabsf(dcx.x), fabsf(dhx.x)), fmaxf(fabsf(dcx.y), fabsf(dhx.y)));
+  const float2 my = make_float2(fmaxf(fabsf(dcy.x), fabsf(dhy.x)), fmaxf(fabsf(dcy.y), fabsf(dhy.y)));
+  const float2 sx = add2(p.hw, dup2(t.box.z));
+  const float2 sy = add2(p.hh, dup2(t.box.w));
+  const float2 iw = sub2(sx, mx);
+  const float2 ih = sub2(sy, my);
   const float2 iwc = make_float2(fmaxf(iw.x, 0.f), fmaxf(iw.y, 0.f));
   const float2 ihc = make_float2(fmaxf(ih.x, 0.f), fmaxf(ih.y, 0.f));
   const float2 inter = mul2(iwc, ihc);
   const float2 uni = fma2(make_float2(-iwc.x, -iwc.y), ihc, add2(p.area, dup2(t.area)));
-  // hull extent = width_p + width_t - intersection extent (an identity for intervals)
-  const float2 ew = sub2(add2(p.pw, dup2(t.tw)), iw);
-  const float2 eh = sub2(add2(p.ph, dup2(t.th)), ih);
+  const float2 ew = add2(sx, mx);  // hull extents
+  const float2 eh = add2(sy, my);
   float2 ewc = ew, ehc = eh, uc = uni;
   if (!kUnclamped) {
     ewc = make_float2(fmaxf(ew.x, 0.f), fmaxf(ew.y, 0.f));
@@ -422,17 +425,12 @@ __global__ void __launch_bounds__(kTmThreads) cost_tmajor_kernel(const CostArgs 
   if (has_target) {
     const int col = c_begin + tid;
     TargetRow t;
-    t.box = tbox;
-    const Corners cn = corners(t.box);
-    t.xy = make_float4(cn.x0, cn.y0, cn.x1, cn.y1);
+    const Corners cn = corners(tbox);
+    t.box = make_float4(tbox.x, tbox.y, __fmul_rn(0.5f, tbox.z), __fmul_rn(0.5f, tbox.w));
     t.area = cn.area;
     t.label = static_cast<int>(tlabel < 0 ? 0 : (tlabel >= a.C ? a.C - 1 : tlabel));
     t.image = image_in_window(s_off, win_lo, a.offsets, a.B, col);
-    t.plain = (t.box.z >= 0.0f && t.box.w >= 0.0f && cn.area >= 2e-7f) ? 1 : 0;
-    t.tw = __fsub_rn(cn.x1, cn.x0);
-    t.th = __fsub_rn(cn.y1, cn.y0);
-    t.pad0 = 0.0f;
-    t.pad1 = 0.0f;
+    t.plain = (tbox.z >= 0.0f && tbox.w >= 0.0f && cn.area >= 2e-7f) ? 1 : 0;
     s_t[tid] = t;
   }
   __syncthreads();

@@ -121,14 +121,16 @@ constexpr int kMultiTwoPerSm = 16;
 // Batches with more than this many problems per SM use the wide layout.
 constexpr int kWideProblemsPerSm = 64;
 // Register budget.  The instantiations up to 320 columns run four CTAs of four
-// warps per SM (at most 128 registers a thread), or six in the wide layout,
-// which keeps the column duals and tie keys in shared memory (at most 85): more
-// resident warps for large batches at a longer chain per problem.  The
-// 1024-column one keeps its per-lane arrays in registers.  (MULTI compiles to
-// 96 registers, five CTAs per SM; capped at 80 or 64 for six or eight CTAs its
-// searches ran 9 % and 22 % longer.)
+// warps per SM (at most 128 registers a thread), or five in the wide layout,
+// which keeps the column duals and tie keys in shared memory (at most 102): more
+// resident warps for large batches at a longer chain per problem (on the
+// 1024-image sweep six wide CTAs per SM ran 1.6 % slower, eight 13 %: the
+// tighter budgets lengthen every warp's chain).  The 1024-column one keeps its
+// per-lane arrays in registers.  (MULTI compiles to 96 registers, five CTAs per
+// SM; capped at 80 or 64 for six or eight CTAs its searches ran 9 % and 22 %
+// longer.)
 __host__ __device__ constexpr int min_ctas_per_sm(int cols_per_lane, int variant) {
-  return cols_per_lane > 10 ? 1 : (variant == kVarWide ? 6 : 4);
+  return cols_per_lane > 10 ? 1 : (variant == kVarWide ? 5 : 4);
 }
 // Shared-memory budget of one CTA: four CTAs of four warps fill an SM.
 constexpr int kCtaBudget = kSmemPerSm / 4 - kSmemPerCtaReserved;

@@ -1,5 +1,8 @@
-// Batched exact rectangular linear assignment with SciPy's semantics; one warp
-// solves one problem (a CTA holds one to four such warps).
+// Batched exact rectangular linear assignment with SciPy's semantics.  For
+// large batches one warp solves one problem (a CTA holds one to four such
+// warps); a batch that runs in one wave of CTAs gets a CTA of four warps per
+// problem (two when more than four problems share an SM), which spread each
+// scan step over the CTA (MULTI, below).
 //
 // Replaces lsap_kernel / batch_lap_cuda (kernels_lap.py:88-305) and the device
 // unpack of the device_indices patch (patches.py:379-418).
@@ -38,7 +41,10 @@
 // comment at the shortcut).  A scan issues all of a lane's loads before the
 // first compare; the EARLY variant (problems with 64 or more rows: long
 // searches) issues the next scan's row as soon as the argmin names it, before
-// the current step's bookkeeping.
+// the current step's bookkeeping.  The MULTI variants keep as many of a
+// problem's rows in shared memory as its CTA's share of the SM holds and run
+// each step as a per-thread scan of a few columns, one warp argmin, a
+// cross-warp combine through shared memory and one barrier.
 //
 // Cost source.  Element (q, t) of a problem is read at
 // cost[cost_offset + q * stride_q + t * stride_t], so the solver reads either
@@ -766,7 +772,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   const int64_t fixed = fixed_warp_bytes(kCols, a.max_rows, kWide);
   float* tile = reinterpret_cast<float*>(base + fixed);
   const int mode = choose_mode(s, a.tile_cap, (slot - fixed) / 4);
-  // STAGE: solver rows [0, staged) are kept in shared memory (all of them when the tile fits)
+  // MULTI: solver rows [0, staged) are kept in shared memory (all of them when the tile fits)
   const int staged =
       kStage ? min(nr, static_cast<int>((slot - fixed - (kMulti ? kMultiPostBytes : 0)) / 4 / nc)) : 0;
   bool bad = false;

@@ -116,12 +116,13 @@ __host__ __device__ constexpr int multi_warps(int v) { return (v == kVarMultiTwo
 __host__ __device__ constexpr bool cta_variant(int v) { return v == kVarCoop || multi_variant(v); }
 __host__ __device__ constexpr bool narrow_only(int v) { return v == kVarWide || cta_variant(v); }
 constexpr int kEarlyMinRows = 64;
-// Batches of long problems (EARLY) that run in one wave of MULTI CTAs (their
+// Batches (of up to 320 columns) that run in one wave of MULTI CTAs (their
 // shared memory divided among the CTAs an SM holds): four warps per problem up
 // to kMultiFourPerSm CTAs per SM, two warps up to kMultiTwoPerSm (or the CTAs
 // that fit, registers permitting).  Past four per SM four-warp problems issue
 // too much to share an SM well; two warps per problem then run their steps
-// faster than one warp does, up to the register file's limit.
+// faster than one warp does, up to the register file's limit.  Larger batches
+// take the one-warp layouts.
 constexpr int kMultiFourPerSm = 4;
 constexpr int kMultiTwoPerSm = 16;
 // Batches with more than this many problems per SM use the wide layout.
@@ -1587,13 +1588,13 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   const bool early = plan->max_rows >= kEarlyMinRows;
   if (!persistent) {
     const MultiLaunch ml =
-        (early || plan->num_problems <= kMultiFourPerSm * device_sm_count()) && plan->cols_per_lane <= 10
+        plan->cols_per_lane <= 10
             ? multi_launch(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMultiCopy),
                            pair_kernel(plan->cols_per_lane, kVarMultiCopyTwo),
                            fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
             : MultiLaunch{0, false};
     if (ml.slot > 0) {
-      // a one-wave batch of long problems, some not row-contiguous: MULTI_COPY.
+      // a batch that runs in one wave, some problems not row-contiguous: MULTI_COPY.
       // Every tile above the plan's cap has scratch, so it runs when its shared
       // memory holds that cap.
       const int64_t room =
@@ -1618,13 +1619,13 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   // large batches (more problems than 64 per SM) take the wide layout, batches of
   // long problems the early-load variant.
   const int sms = device_sm_count();
-  const MultiLaunch ml = (early || plan->num_problems <= kMultiFourPerSm * sms) && plan->cols_per_lane <= 10
+  const MultiLaunch ml = plan->cols_per_lane <= 10
                              ? multi_launch(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMulti),
                                             pair_kernel(plan->cols_per_lane, kVarMultiTwo),
                                             fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
                              : MultiLaunch{0, false};
   if (ml.slot > 0) {
-    // a one-wave batch of long problems: MULTI, its rows staged as far as they fit
+    // a batch that runs in one wave: MULTI, its rows staged as far as they fit
     a.slot = ml.slot;
     a.tile_cap = (a.slot - static_cast<int>(fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))) / 4;
     if (ml.two) {
@@ -1772,8 +1773,8 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.q_out = matching;
   a.t_out = nullptr;
   a.status = status;
-  if ((dp.max_rows >= kEarlyMinRows || num_problems <= kMultiFourPerSm * device_sm_count()) && dp.cpl <= 10) {
-    // a one-wave batch of long problems: MULTI_COPY when every tile either fits
+  if (dp.cpl <= 10) {
+    // a batch that runs in one wave: MULTI_COPY when every tile either fits
     // its CTA's shared memory or has scratch
     const MultiLaunch ml = multi_launch(num_problems, dense_multi_kernel(dp.cpl, false),
                                         dense_multi_kernel(dp.cpl, true), fixed_warp_bytes(32 * dp.cpl, dp.max_rows));

@@ -105,12 +105,15 @@ enum Variant : int {
   kVarMulti = 5,
   kVarMultiCopy = 6,
   kVarMultiTwo = 7,
-  kVarMultiCopyTwo = 8
+  kVarMultiCopyTwo = 8,
+  kVarMultiTwoQueue = 9  // MULTI_TWO with fewer CTAs than problems, claiming from a counter
 };
-__host__ __device__ constexpr bool multi_variant(int v) { return v >= kVarMulti && v <= kVarMultiCopyTwo; }
+__host__ __device__ constexpr bool multi_variant(int v) { return v >= kVarMulti && v <= kVarMultiTwoQueue; }
 __host__ __device__ constexpr bool copy_variant(int v) { return v == kVarMultiCopy || v == kVarMultiCopyTwo; }
 // Warps that share one problem's searches in a MULTI variant.
-__host__ __device__ constexpr int multi_warps(int v) { return (v == kVarMultiTwo || v == kVarMultiCopyTwo) ? 2 : 4; }
+__host__ __device__ constexpr int multi_warps(int v) {
+  return (v == kVarMultiTwo || v == kVarMultiCopyTwo || v == kVarMultiTwoQueue) ? 2 : 4;
+}
 // Variants with one problem per CTA; none exists for the 1024-column layout,
 // and neither does WIDE.
 __host__ __device__ constexpr bool cta_variant(int v) { return v == kVarCoop || multi_variant(v); }
@@ -423,6 +426,9 @@ struct MultiShared {
   int* flag;
 };
 constexpr int kMultiPostBytes = 144;
+// [0, 128): the step posts; 128: the flip flag; kMultiClaimOffset: a persistent
+// MULTI CTA's next problem.
+constexpr int kMultiClaimOffset = 136;
 // A MULTI key also carries the column's matched row plus one (0 when free) in
 // its low kRowBits bits, so the step's argmin names the next row directly.
 // Columns are at most 320 here, and rows at most columns.
@@ -716,7 +722,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
 
   if (nr == 0) {
     grid_dependency_wait();
-    const int next = claim_next(a, lane);
+    const int next = kMulti ? 0 : claim_next(a, lane);  // a MULTI CTA claims in the kernel's loop
     if (kDense) {
       for (int w = lane; w < nq; w += 32) q_out[w] = -1;
     }
@@ -1118,7 +1124,7 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   }
 
   // ---- epilogue: write the result in SciPy's order -------------------------
-  const int next = claim_next(a, lane);
+  const int next = kMulti ? 0 : claim_next(a, lane);
   if (kDense) {
     // matching[w] = task of worker w, -1 if none (kernels_lap.py:336-341)
     if (code != RFM_STATUS_OK) {
@@ -1168,8 +1174,24 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVari
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  if (kVariant == kVarMultiTwoQueue) {
+    // fewer CTAs than problems: CTA c starts on problem c, then claims further
+    // problems (sorted largest first) from the counter until none is left.  The
+    // claim is passed on in a spare word of the step-post area (static shared
+    // memory would not fit beside the SM's shares).
+    int* next_problem = reinterpret_cast<int*>(smem_raw + a.slot - kMultiPostBytes + kMultiClaimOffset);
+    int p = blockIdx.x;
+    while (p < a.num_problems) {
+      solve_problem<K, kDense, kVariant>(a, p, smem_raw, a.slot, lane);
+      __syncthreads();  // every warp is done with the problem's shared memory
+      if (threadIdx.x == 0) *next_problem = atomicAdd(a.queue, 1) + a.claim_base;
+      __syncthreads();
+      p = *next_problem;
+    }
+    return;
+  }
   if (cta_variant(kVariant)) {
-    // one problem per CTA, all four warps in its load pass
+    // one problem per CTA, all its warps in its load pass
     solve_problem<K, kDense, kVariant>(a, blockIdx.x, smem_raw, a.slot, lane);
     return;
   }
@@ -1222,6 +1244,9 @@ const void* pair_kernel(int cols_per_lane, int variant) {
       if (variant == kVarMultiCopy) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMultiCopy>);
       if (variant == kVarMultiTwo) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMultiTwo>);
       if (variant == kVarMultiCopyTwo) return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMultiCopyTwo>);
+      if (variant == kVarMultiTwoQueue) {
+        return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarMultiTwoQueue>);
+      }
       return reinterpret_cast<const void*>(&lsap_kernel<4, false, kVarRegs>);
     case 10:
       if (variant == kVarWide) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarWide>);
@@ -1231,6 +1256,9 @@ const void* pair_kernel(int cols_per_lane, int variant) {
       if (variant == kVarMultiCopy) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMultiCopy>);
       if (variant == kVarMultiTwo) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMultiTwo>);
       if (variant == kVarMultiCopyTwo) return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMultiCopyTwo>);
+      if (variant == kVarMultiTwoQueue) {
+        return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarMultiTwoQueue>);
+      }
       return reinterpret_cast<const void*>(&lsap_kernel<10, false, kVarRegs>);
     case 32:
       if (narrow_only(variant)) return nullptr;
@@ -1515,22 +1543,38 @@ namespace {
 struct MultiLaunch {
   int slot;
   bool two;
+  int ctas;  // the grid: one CTA per problem, or fewer that claim problems from a counter
 };
 
-MultiLaunch multi_launch(int num_problems, const void* fn4, const void* fn2, int64_t fixed) {
+// Shared memory of each of `per_sm` CTAs sharing an SM: whole KB, so that the
+// shares plus their reservations fit.
+int multi_share(int per_sm) {
+  const int smem = (kSmemPerSm / per_sm - kSmemPerCtaReserved) / 1024 * 1024;
+  return smem > kSmemPerBlockMax ? kSmemPerBlockMax : smem;
+}
+
+// With `fn2_queue` (the claiming two-warp kernel of a persistent plan, whose
+// workspace holds a counter), a batch of up to kMultiTwoPerSm problems per SM
+// whose CTAs do not all fit at once runs as the most such CTAs that do.
+MultiLaunch multi_launch(int num_problems, const void* fn4, const void* fn2, int64_t fixed,
+                         const void* fn2_queue = nullptr) {
   const int sms = device_sm_count();
   if (sms < 1 || num_problems < 1 ||
       static_cast<int64_t>(num_problems) > static_cast<int64_t>(kMultiTwoPerSm) * sms) {
-    return {0, false};
+    return {0, false, 0};
   }
   const int per_sm = (num_problems + sms - 1) / sms;
-  // whole KB, so that per_sm shares plus their reservations fit the SM
-  int smem = (kSmemPerSm / per_sm - kSmemPerCtaReserved) / 1024 * 1024;
-  if (smem > kSmemPerBlockMax) smem = kSmemPerBlockMax;
-  if (fixed + kMultiPostBytes > smem) return {0, false};
-  if (per_sm <= kMultiFourPerSm && resident_ctas(fn4, smem, 128) >= per_sm) return {smem, false};
-  if (resident_ctas(fn2, smem, 64) >= per_sm) return {smem, true};
-  return {0, false};
+  int smem = multi_share(per_sm);
+  if (fixed + kMultiPostBytes <= smem) {
+    if (per_sm <= kMultiFourPerSm && resident_ctas(fn4, smem, 128) >= per_sm) return {smem, false, num_problems};
+    if (resident_ctas(fn2, smem, 64) >= per_sm) return {smem, true, num_problems};
+  }
+  if (fn2_queue == nullptr) return {0, false, 0};
+  for (int n = per_sm - 1; n > kMultiFourPerSm; --n) {
+    smem = multi_share(n);
+    if (fixed + kMultiPostBytes <= smem && resident_ctas(fn2_queue, smem, 64) >= n) return {smem, true, n * sms};
+  }
+  return {0, false, 0};
 }
 
 const void* dense_multi_kernel(int cols_per_lane, bool two) {
@@ -1592,7 +1636,7 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
             ? multi_launch(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMultiCopy),
                            pair_kernel(plan->cols_per_lane, kVarMultiCopyTwo),
                            fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
-            : MultiLaunch{0, false};
+            : MultiLaunch{0, false, 0};
     if (ml.slot > 0) {
       // a batch that runs in one wave, some problems not row-contiguous: MULTI_COPY.
       // Every tile above the plan's cap has scratch, so it runs when its shared
@@ -1622,17 +1666,26 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   const MultiLaunch ml = plan->cols_per_lane <= 10
                              ? multi_launch(plan->num_problems, pair_kernel(plan->cols_per_lane, kVarMulti),
                                             pair_kernel(plan->cols_per_lane, kVarMultiTwo),
-                                            fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))
-                             : MultiLaunch{0, false};
+                                            fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows),
+                                            pair_kernel(plan->cols_per_lane, kVarMultiTwoQueue))
+                             : MultiLaunch{0, false, 0};
   if (ml.slot > 0) {
-    // a batch that runs in one wave: MULTI, its rows staged as far as they fit
+    // MULTI, its rows staged as far as they fit: a batch that runs in one wave,
+    // or (fewer CTAs than problems) CTAs that pull problems from the counter
     a.slot = ml.slot;
     a.tile_cap = (a.slot - static_cast<int>(fixed_warp_bytes(32 * plan->cols_per_lane, plan->max_rows))) / 4;
-    if (ml.two) {
-      return launch<false, kVarMultiTwo>(a, plan->cols_per_lane, plan->num_problems, 2, a.slot, stream,
-                                         counter_zeroed);
+    if (ml.ctas < plan->num_problems) {
+      a.queue = static_cast<int*>(workspace);
+      a.claim_base = ml.ctas;
+      if (!counter_zeroed && cudaMemsetAsync(a.queue, 0, sizeof(int), as_stream(stream)) != cudaSuccess) {
+        return launch_status();
+      }
+      return launch<false, kVarMultiTwoQueue>(a, plan->cols_per_lane, ml.ctas, 2, a.slot, stream, counter_zeroed);
     }
-    return launch<false, kVarMulti>(a, plan->cols_per_lane, plan->num_problems, 4, a.slot, stream, counter_zeroed);
+    if (ml.two) {
+      return launch<false, kVarMultiTwo>(a, plan->cols_per_lane, ml.ctas, 2, a.slot, stream, counter_zeroed);
+    }
+    return launch<false, kVarMulti>(a, plan->cols_per_lane, ml.ctas, 4, a.slot, stream, counter_zeroed);
   }
   const bool wide = plan->cols_per_lane <= 10 &&
                     static_cast<int64_t>(plan->num_problems) > static_cast<int64_t>(kWideProblemsPerSm) * sms;

@@ -131,6 +131,9 @@ def _target_major_matrix(sizes, width, groups, kind, rng):
     (tuple(range(64, 124, 3)), 300, 13, "ties8"),  # 260 problems: two per SM
     (tuple(range(64, 114)), 300, 13, "uniform"),  # 650 problems: five per SM, two warps each
     (tuple(range(64, 100)), 100, 20, "ties4"),  # 720 problems of at most 128 columns, two warps each
+    # more problems than fit one wave: two-warp CTAs claiming problems from a counter (row-contiguous)
+    (tuple(64 + i % 40 for i in range(120)), 300, 13, "ties4"),  # 1,560 long problems
+    (tuple(8 + i % 30 for i in range(150)), 300, 13, "uniform"),  # 1,950 short problems
     ((300, 180, 90), 300, 2, "ties4"),  # square problems: solver rows run across the target-major rows
 ])
 @pytest.mark.parametrize("layout", ["target_major", "query_major"])

@@ -124,10 +124,13 @@ constexpr int kEarlyMinRows = 64;
 // to kMultiFourPerSm CTAs per SM, two warps up to kMultiTwoPerSm (or the CTAs
 // that fit, registers permitting).  Past four per SM four-warp problems issue
 // too much to share an SM well; two warps per problem then run their steps
-// faster than one warp does, up to the register file's limit.  Larger batches
-// take the one-warp layouts.
+// faster than one warp does, up to the register file's limit; beyond that
+// (kVarMultiTwoQueue) the CTAs that fit claim the remaining problems.  On the
+// short problems of the sweep geometry that beat one warp per problem up to
+// about 36 problems per SM and lost at 45; larger batches take the one-warp
+// layouts.
 constexpr int kMultiFourPerSm = 4;
-constexpr int kMultiTwoPerSm = 16;
+constexpr int kMultiTwoPerSm = 40;
 // Batches with more than this many problems per SM use the wide layout.
 constexpr int kWideProblemsPerSm = 64;
 // Register budget.  The instantiations up to 320 columns run four CTAs of four

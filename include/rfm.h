@@ -234,7 +234,10 @@ int rfm_match(const float* pred_logits, const float* pred_boxes, const int64_t* 
  * (kernels_lap.py:336-341): cost [P, W, T] float32 contiguous ->
  * matching [P, W] int64 with the task of each worker, -1 when unassigned.
  * Solved per problem with SciPy's semantics as in rfm_lsap.
- * `workspace` must hold rfm_lsap_dense_workspace_bytes(P, W, T) bytes.
+ * `workspace` must hold rfm_lsap_dense_workspace_bytes(P, W, T) bytes: the
+ * scratch of tiles that are staged off chip, and for batches of 512 or more
+ * problems a 256-byte counter after it (the solver's CTAs may claim problems
+ * from it; it is reset on the stream by every call).
  */
 int64_t rfm_lsap_dense_workspace_bytes(int num_problems, int num_workers, int num_tasks);
 int rfm_lsap_dense(const float* cost, int num_problems, int num_workers, int num_tasks,

@@ -106,13 +106,17 @@ enum Variant : int {
   kVarMultiCopy = 6,
   kVarMultiTwo = 7,
   kVarMultiCopyTwo = 8,
-  kVarMultiTwoQueue = 9  // MULTI_TWO with fewer CTAs than problems, claiming from a counter
+  kVarMultiTwoQueue = 9,      // MULTI_TWO with fewer CTAs than problems, claiming from a counter
+  kVarMultiCopyTwoQueue = 10  // the same for MULTI_COPY_TWO (dense batches)
 };
-__host__ __device__ constexpr bool multi_variant(int v) { return v >= kVarMulti && v <= kVarMultiTwoQueue; }
-__host__ __device__ constexpr bool copy_variant(int v) { return v == kVarMultiCopy || v == kVarMultiCopyTwo; }
+__host__ __device__ constexpr bool multi_variant(int v) { return v >= kVarMulti && v <= kVarMultiCopyTwoQueue; }
+__host__ __device__ constexpr bool copy_variant(int v) {
+  return v == kVarMultiCopy || v == kVarMultiCopyTwo || v == kVarMultiCopyTwoQueue;
+}
+__host__ __device__ constexpr bool queue_variant(int v) { return v == kVarMultiTwoQueue || v == kVarMultiCopyTwoQueue; }
 // Warps that share one problem's searches in a MULTI variant.
 __host__ __device__ constexpr int multi_warps(int v) {
-  return (v == kVarMultiTwo || v == kVarMultiCopyTwo || v == kVarMultiTwoQueue) ? 2 : 4;
+  return (v == kVarMultiTwo || v == kVarMultiCopyTwo || queue_variant(v)) ? 2 : 4;
 }
 // Variants with one problem per CTA; none exists for the 1024-column layout,
 // and neither does WIDE.
@@ -1177,7 +1181,7 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVari
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  if (kVariant == kVarMultiTwoQueue) {
+  if (queue_variant(kVariant)) {
     // fewer CTAs than problems: CTA c starts on problem c, then claims further
     // problems (sorted largest first) from the counter until none is left.  The
     // claim is passed on in a spare word of the step-post area (static shared
@@ -1580,6 +1584,12 @@ MultiLaunch multi_launch(int num_problems, const void* fn4, const void* fn2, int
   return {0, false, 0};
 }
 
+const void* dense_queue_kernel(int cols_per_lane) {
+  if (cols_per_lane == 4) return reinterpret_cast<const void*>(&lsap_kernel<4, true, kVarMultiCopyTwoQueue>);
+  if (cols_per_lane == 10) return reinterpret_cast<const void*>(&lsap_kernel<10, true, kVarMultiCopyTwoQueue>);
+  return nullptr;
+}
+
 const void* dense_multi_kernel(int cols_per_lane, bool two) {
   if (cols_per_lane == 4) {
     return two ? reinterpret_cast<const void*>(&lsap_kernel<4, true, kVarMultiCopyTwo>)
@@ -1764,9 +1774,15 @@ extern "C" int rfm_match(const float* pred_logits, const float* pred_boxes, cons
 }
 
 namespace {
+// Dense batches of at least this many problems reserve a claim counter after
+// their scratch (kQueueBytes), for the queue layout when one wave does not fit.
+constexpr int kDenseQueueMinProblems = 512;
+
 struct DensePlan {
   int cpl, max_rows, warps;
   int64_t slot, tile_cap, scratch_bytes;
+  int64_t queue_offset;     // -1: no counter
+  int64_t workspace_bytes;  // scratch, then the counter
 };
 
 int dense_plan(int num_problems, int num_workers, int num_tasks, DensePlan* out) {
@@ -1787,6 +1803,12 @@ int dense_plan(int num_problems, int num_workers, int num_tasks, DensePlan* out)
   if (s.nr > 0 && choose_mode(s, out->tile_cap, (out->slot - fixed) / 4) == kModeScratch) {
     out->scratch_bytes = static_cast<int64_t>(num_problems) * num_workers * num_tasks * 4;
   }
+  out->queue_offset = -1;
+  out->workspace_bytes = out->scratch_bytes;
+  if (num_problems >= kDenseQueueMinProblems && out->cpl <= 10 && s.nr > 0) {
+    out->queue_offset = (out->scratch_bytes + 255) & ~int64_t(255);
+    out->workspace_bytes = out->queue_offset + kQueueBytes;
+  }
   return RFM_OK;
 }
 }  // namespace
@@ -1796,7 +1818,7 @@ extern "C" int64_t rfm_lsap_dense_workspace_bytes(int num_problems, int num_work
   DensePlan dp;
   const int rc = dense_plan(num_problems, num_workers, num_tasks, &dp);
   if (rc != RFM_OK) return -static_cast<int64_t>(rc);
-  return dp.scratch_bytes;
+  return dp.workspace_bytes;
 }
 
 extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_workers, int num_tasks,
@@ -1807,7 +1829,7 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   if (rc != RFM_OK) return rc;
   if (num_problems == 0 || num_workers == 0) return RFM_OK;
   if (matching == nullptr || (num_tasks > 0 && cost == nullptr) ||
-      (dp.scratch_bytes > 0 && workspace == nullptr)) {
+      (dp.workspace_bytes > 0 && workspace == nullptr)) {
     return RFM_ERR_INVALID_ARGUMENT;
   }
   LsapArgs a;
@@ -1830,10 +1852,13 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.t_out = nullptr;
   a.status = status;
   if (dp.cpl <= 10) {
-    // a batch that runs in one wave: MULTI_COPY when every tile either fits
-    // its CTA's shared memory or has scratch
-    const MultiLaunch ml = multi_launch(num_problems, dense_multi_kernel(dp.cpl, false),
-                                        dense_multi_kernel(dp.cpl, true), fixed_warp_bytes(32 * dp.cpl, dp.max_rows));
+    // MULTI_COPY when every tile either fits its CTA's shared memory or has
+    // scratch: one wave, or (with the workspace's counter) two-warp CTAs that
+    // claim the problems one wave does not hold
+    const MultiLaunch ml =
+        multi_launch(num_problems, dense_multi_kernel(dp.cpl, false), dense_multi_kernel(dp.cpl, true),
+                     fixed_warp_bytes(32 * dp.cpl, dp.max_rows),
+                     dp.queue_offset >= 0 ? dense_queue_kernel(dp.cpl) : nullptr);
     const Shape s = solver_shape(num_workers, num_tasks, num_tasks, 1);
     const int64_t room =
         ml.slot > 0 ? (ml.slot - fixed_warp_bytes(32 * dp.cpl, dp.max_rows) - kMultiPostBytes) / 4 : 0;
@@ -1841,6 +1866,12 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
     if (ml.slot > 0 && (static_cast<int64_t>(s.nr) * s.nc <= room || s.cs == 1 || dp.scratch_bytes > 0)) {
       a.slot = ml.slot;
       a.tile_cap = static_cast<int>(room);
+      if (ml.ctas < num_problems) {
+        a.queue = reinterpret_cast<int*>(static_cast<char*>(workspace) + dp.queue_offset);
+        a.claim_base = ml.ctas;
+        if (cudaMemsetAsync(a.queue, 0, sizeof(int), as_stream(stream)) != cudaSuccess) return launch_status();
+        return launch<true, kVarMultiCopyTwoQueue>(a, dp.cpl, ml.ctas, 2, ml.slot, stream);
+      }
       if (ml.two) return launch<true, kVarMultiCopyTwo>(a, dp.cpl, num_problems, 2, ml.slot, stream);
       return launch<true, kVarMultiCopy>(a, dp.cpl, num_problems, 4, ml.slot, stream);
     }

@@ -139,6 +139,7 @@ def test_planner_modes_and_workspace():
 
 def test_dense_workspace_bytes():
     lib = _lib.load()
-    assert lib.rfm_lsap_dense_workspace_bytes(520, 300, 12) == 0
+    assert lib.rfm_lsap_dense_workspace_bytes(520, 300, 12) == 256  # the claim counter of batches of 512+
+    assert lib.rfm_lsap_dense_workspace_bytes(511, 300, 12) == 0
     assert lib.rfm_lsap_dense_workspace_bytes(40, 300, 250) == 40 * 300 * 250 * 4
     assert lib.rfm_lsap_dense_workspace_bytes(40, 300, 300) == 0

@@ -34,7 +34,9 @@ def _solve_dense(cost: np.ndarray, **kw) -> np.ndarray:
                                    # long problems: one four-warp CTA each at 1, 5 and 3 per SM (the
                                    # last square, rows read in place), then too many for one wave
                                    (140, 300, 90), (700, 300, 70), (300, 200, 200), (1300, 300, 66),
-                                   (700, 100, 64)])
+                                   (700, 100, 64),
+                                   # more than one wave: two-warp CTAs claiming problems from the counter
+                                   (2000, 300, 60), (1600, 300, 12)])
 def test_dense_random(shape):
     rng = np.random.default_rng(sum(shape))
     cost = (rng.random(shape, dtype=np.float32) * 10 - 5).astype(np.float32)

@@ -1560,9 +1560,11 @@ int multi_share(int per_sm) {
   return smem > kSmemPerBlockMax ? kSmemPerBlockMax : smem;
 }
 
-// With `fn2_queue` (the claiming two-warp kernel of a persistent plan, whose
-// workspace holds a counter), a batch of up to kMultiTwoPerSm problems per SM
-// whose CTAs do not all fit at once runs as the most such CTAs that do.
+// With `fn2_queue` (the claiming two-warp kernel, given when the workspace
+// holds a counter: persistent plans, dense batches of 512+ problems), a batch
+// of up to kMultiTwoPerSm problems per SM whose CTAs do not all fit at once
+// runs as the most such CTAs that do (fewer than the problems, so every CTA
+// has its own first problem).
 MultiLaunch multi_launch(int num_problems, const void* fn4, const void* fn2, int64_t fixed,
                          const void* fn2_queue = nullptr) {
   const int sms = device_sm_count();

@@ -1062,7 +1062,7 @@ def emit(line: dict) -> None:
         os.write(fd, text.encode())
 
 
-def run_kernel(name: str, workload: str = "sweep") -> None:
+def run_kernel(name: str, workload: str = "sweep", images: int | None = None) -> None:
     """A few launches of one kernel on its benchmark workload, for an ncu capture of that kernel:
     cost / lsap (the workload's step, issued as two calls), cost_qm (the drop-in query-major cost
     matrix, ``compute_compact_detection_cost_matrix``), label / box (the classification or the
@@ -1073,7 +1073,7 @@ def run_kernel(name: str, workload: str = "sweep") -> None:
     dev = torch.device("cuda", 0)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     if name == "cost_qm":
-        wl = workloads.make(workload)
+        wl = workloads.make(workload, images=images)
         lg, bx = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)
         tg = wl.targets_on(dev)
         for _ in range(4):
@@ -1081,7 +1081,7 @@ def run_kernel(name: str, workload: str = "sweep") -> None:
                                                          weights=wl.weights)
             flush.zero_()
     elif name in ("cost", "lsap", "label", "box"):
-        wl = workloads.make(workload)
+        wl = workloads.make(workload, images=images)
         lg, bx = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)
         pk = matcher.PackedTargets.from_list(wl.targets_on(dev), dev)
         for _ in range(4):
@@ -1122,7 +1122,7 @@ def run_kernel(name: str, workload: str = "sweep") -> None:
 def main() -> None:
     args = parse()
     if args.kernel is not None:
-        run_kernel(args.kernel, args.workload)
+        run_kernel(args.kernel, args.workload, args.images)
         return
     # Everything else anything in the process writes to stdout (library banners such as NCCL's
     # version line under torchrun) goes to stderr, so stdout carries the JSON line alone.

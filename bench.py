@@ -516,8 +516,24 @@ def run_rfm(args) -> None:
     # ---- sharded sweep: ONE batch split across the ranks + NCCL all-gather of the pairs
     sharded_info = None
     if world > 1 or args.sharded:
-        sharded_info = [run_sharded_sweep(args, world, rank, device, barrier, images)
-                        for images in args.sharded_images]
+        # one process: a one-rank group of its own, so the same code path runs
+        own_group = world == 1 and not torch.distributed.is_initialized()
+        if own_group:
+            import socket
+
+            with socket.socket() as sock:
+                sock.bind(("127.0.0.1", 0))
+                port = sock.getsockname()[1]
+            os.environ["MASTER_ADDR"] = "127.0.0.1"
+            os.environ["MASTER_PORT"] = str(port)
+            torch.distributed.init_process_group("nccl", rank=0, world_size=1, timeout=timedelta(seconds=120),
+                                                 device_id=device)
+        try:
+            sharded_info = [run_sharded_sweep(args, world, rank, device, barrier, images)
+                            for images in args.sharded_images]
+        finally:
+            if own_group:
+                torch.distributed.destroy_process_group()
 
     # ---- roofline of the cost kernel (HBM-bound) and the solver figures
     peak, peak_kind = peak_hbm()
@@ -1032,10 +1048,31 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier, images: int)
     parts = {"step": mean_ms(step), "replay": mean_ms(sm.graph.replay), "all_gather": mean_ms(lambda: sm.gather(True)),
              "flat_concat": mean_ms(lambda: sm.gather(True).flat()), "eager_step": mean_ms(eager)}
     same = bool(torch.equal(step().flat(), eager().flat()))
-    t = torch.tensor(list(parts.values()), dtype=torch.float64, device=device)
+
+    # the same step with the pushed exchange: the solver stores every pair into every rank's
+    # gathered buffer, a one-warp barrier ends the step; one graph replay, no collective
+    sp = sharded.ShardedMatcher(sizes, wl.layers, wl.queries, wl.classes, wl.group_detr, weights=wl.weights,
+                                device=device, exchange="push")
+    sp.graph.logits.copy_(logits)
+    sp.graph.boxes.copy_(boxes)
+    sp.graph.labels.copy_(labels)
+    sp.graph.tgt_boxes.copy_(tboxes)
+
+    def push_step():
+        sp.replay()
+        return sp.gather(padded=True)
+
+    parts["push_step"] = mean_ms(push_step)
+    same_push = bool(torch.equal(push_step().flat(), step().flat()))
+    push_error = sp.exchange.error()
+    sp.close()
+    t = torch.tensor(list(parts.values()) + [0.0 if same_push else 1.0, float(push_error)], dtype=torch.float64,
+                     device=device)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms = dict(zip(parts.keys(), t.tolist()))
+    vals = t.tolist()
+    ms = dict(zip(parts.keys(), vals))
+    push_mismatch, push_error = vals[-2] > 0, int(vals[-1])
     gathered_pairs = int(sum(sm.shard.counts))
     del sm  # its graph holds no collective, but release it before the process group goes
     return {"images": wl.images, "problems_per_step": wl.num_problems, "steps": steps,
@@ -1044,6 +1081,11 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier, images: int)
                              "all_gather_plus_flat_concat": ms["flat_concat"]},
             "eager_ms_per_step": ms["eager_step"], "eager_problems_per_s": wl.num_problems / (ms["eager_step"] / 1e3),
             "graph_equals_eager": same, "gathered_pairs": gathered_pairs, "scaling": "strong",
+            "push": {"ms_per_step": ms["push_step"], "problems_per_s": wl.num_problems / (ms["push_step"] / 1e3),
+                     "equals_all_gather_on_every_rank": not push_mismatch, "barrier_gave_up": bool(push_error),
+                     "exchange": "the solver stores every pair into every rank's gathered buffer (CUDA IPC peer "
+                                 "mappings, plain stores over NVLink), then a one-warp flag barrier; one graph "
+                                 "replay per step, no collective"},
             "result": "GatheredPairs (the all-gather's buffer, per-image views at host-known offsets)",
             "collective": "all_gather_into_tensor of int64 [2, width] per rank" if world > 1 else "none (1 rank)"}
 

@@ -32,7 +32,9 @@
  * Conventions shared by every entry point:
  *   - All tensor arguments are DEVICE pointers owned by the caller, except
  *     where a comment says "host".  No entry point allocates device memory,
- *     synchronises the stream or the device, or copies to the host.
+ *     synchronises the stream or the device, or copies to the host, except
+ *     the setup calls of the sharded sweep's exchange (rfm_peer_alloc,
+ *     rfm_peer_free, rfm_pair_push_store), which say so.
  *   - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is
  *     the legacy default stream) on the current device.
  *   - The return value reports argument and launch errors synchronously
@@ -381,6 +383,85 @@ int rfm_msda_backward(const float* value, const int64_t* spatial_shapes, const i
                       const float* sampling_locations, const float* attention_weights, const float* grad_out,
                       int batch, int sequence, int heads, int head_dim, int queries, int levels, int points,
                       float* grad_value, float* grad_locations, float* grad_weights, void* stream);
+
+/*
+ * ---- The sharded sweep's exchange: pairs pushed into every rank's memory ----
+ *
+ * No counterpart in the reference, which matches on one GPU.  A batch split by
+ * image over R ranks (one process per GPU) needs every rank's pairs on every
+ * rank.  Instead of a separate all-gather, the solver's epilogue writes each
+ * pair it produces into each rank's gathered buffer (peer memory over NVLink,
+ * mapped into this process with CUDA IPC; plain stores, no multicast), so the
+ * transfer overlaps the solve problem by problem.  A one-warp kernel then
+ * raises this rank's flag on every rank and waits (bounded) for every rank's
+ * flag.  Each gathered buffer is double-buffered by step parity, so a rank
+ * that runs ahead writes the buffer of the step after the one its peers may
+ * still be reading.
+ */
+#define RFM_MAX_PUSH 8
+
+/*
+ * Destinations that also receive every pair of rfm_lsap_push / rfm_match_push.
+ * Pair k of a problem goes to query_out[d][o + k] and target_out[d][o + k] for
+ * each d < count, with o = out_offset + (*epoch & 1) * parity_stride.  The
+ * solver reads the list from device memory (rfm_pair_push_store puts it there),
+ * so a captured launch picks up a list stored after the capture.
+ */
+typedef struct rfm_pair_push {
+  int32_t count;                     /* destinations, 0..RFM_MAX_PUSH */
+  int32_t reserved;                  /* must be 0 */
+  int64_t parity_stride;             /* int64 elements between a destination's two buffers */
+  const uint32_t* epoch;             /* DEVICE step counter of this rank (rfm_peer_sync advances it) */
+  int64_t* query_out[RFM_MAX_PUSH];  /* DEVICE (peer-mapped) pointers */
+  int64_t* target_out[RFM_MAX_PUSH];
+} rfm_pair_push;
+
+/* Checks `push` on the host and copies it to device_dst (DEVICE, 16-byte
+ * aligned, sizeof(rfm_pair_push) bytes), synchronously. */
+int rfm_pair_push_store(const rfm_pair_push* push, void* device_dst);
+
+/* rfm_lsap / rfm_match whose pairs also go to the destinations of the push
+ * list at device_push (DEVICE, stored by rfm_pair_push_store; NULL: none).
+ * Pair plans only; dense batches are not pushed. */
+int rfm_lsap_push(const float* cost, const rfm_problem* problems, const int32_t* ctas,
+                  const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out, int32_t* status,
+                  void* workspace, const rfm_pair_push* device_push, void* stream);
+int rfm_match_push(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+                   const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
+                   int num_queries, int num_classes, int sum_targets, int64_t ld, float cost_class,
+                   float cost_bbox, float cost_giou, float focal_alpha, float* cost,
+                   const rfm_problem* problems, const int32_t* ctas, const rfm_lsap_plan* plan,
+                   int64_t* query_out, int64_t* target_out, int32_t* status, void* workspace,
+                   const rfm_pair_push* device_push, void* stream);
+
+/* Device memory another process on this node can map: `bytes` zeroed bytes on
+ * the current device (*ptr), exportable through the 64-byte `handle`.  Free
+ * with rfm_peer_free once every importer has closed it. */
+int rfm_peer_alloc(int64_t bytes, void** ptr, unsigned char* handle);
+/* Map another process's rfm_peer_alloc memory (its handle) into this one. */
+int rfm_peer_open(const unsigned char* handle, void** ptr);
+int rfm_peer_close(void* ptr);
+int rfm_peer_free(void* ptr);
+
+/*
+ * One step's barrier across the ranks.  Every lane j < world stores
+ * epoch + 1 into arrive[j] (this rank's flag on rank j, after a system-scope
+ * fence that orders this GPU's earlier pushes before it), then waits until
+ * flags[j] (rank j's flag on this rank) reaches epoch + 1, polling at most
+ * spin_limit times; a wait that gives up sets *error to 1 and the kernel
+ * returns.  *epoch is then advanced.
+ */
+typedef struct rfm_peer_sync_args {
+  int32_t world;                   /* ranks, 1..RFM_MAX_PUSH */
+  int32_t rank;
+  int64_t spin_limit;              /* polls per wait, >= 1 */
+  uint32_t* arrive[RFM_MAX_PUSH];  /* DEVICE (peer-mapped): this rank's flag word on rank j */
+  const uint32_t* flags;           /* DEVICE: the world flag words of this rank */
+  uint32_t* epoch;                 /* DEVICE: this rank's step counter */
+  int32_t* error;                  /* DEVICE: set to 1 when a wait gives up */
+} rfm_peer_sync_args;
+
+int rfm_peer_sync(const rfm_peer_sync_args* args, void* stream);
 
 #ifdef __cplusplus
 }

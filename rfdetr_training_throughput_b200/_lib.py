@@ -46,7 +46,20 @@ EXPORTS = (
     "rfm_label_loss_backward",
     "rfm_msda_forward",
     "rfm_msda_backward",
+    "rfm_pair_push_store",
+    "rfm_lsap_push",
+    "rfm_match_push",
+    "rfm_peer_alloc",
+    "rfm_peer_open",
+    "rfm_peer_close",
+    "rfm_peer_free",
+    "rfm_peer_sync",
 )
+
+#: RFM_MAX_PUSH: destinations of one pushed solve, ranks of one pushed exchange.
+MAX_PUSH = 8
+#: Bytes of a CUDA IPC handle (rfm_peer_alloc / rfm_peer_open).
+IPC_HANDLE_BYTES = 64
 
 #: Size of the built-in scratch of rfm_lsap_dense_noalloc (RFM_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 16 << 20
@@ -92,6 +105,36 @@ class LsapPlan(ctypes.Structure):
         ("stride_t", ctypes.c_int64),
         ("workspace_bytes", ctypes.c_int64),
     ]
+
+
+class PairPush(ctypes.Structure):
+    """Mirror of ``struct rfm_pair_push``."""
+
+    _fields_ = [
+        ("count", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("parity_stride", ctypes.c_int64),
+        ("epoch", ctypes.c_void_p),
+        ("query_out", ctypes.c_void_p * MAX_PUSH),
+        ("target_out", ctypes.c_void_p * MAX_PUSH),
+    ]
+
+
+class PeerSyncArgs(ctypes.Structure):
+    """Mirror of ``struct rfm_peer_sync_args``."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("spin_limit", ctypes.c_int64),
+        ("arrive", ctypes.c_void_p * MAX_PUSH),
+        ("flags", ctypes.c_void_p),
+        ("epoch", ctypes.c_void_p),
+        ("error", ctypes.c_void_p),
+    ]
+
+
+assert ctypes.sizeof(PairPush) == 152 and ctypes.sizeof(PeerSyncArgs) == 104
 
 
 class RfmError(RuntimeError):
@@ -161,6 +204,23 @@ def load() -> ctypes.CDLL:
                                       _p]
     lib.rfm_lsap_dense_noalloc.restype = _i32
     lib.rfm_lsap_dense_noalloc.argtypes = [_p, _i32, _i32, _i32, _p, _p, _p]
+    lib.rfm_pair_push_store.restype = _i32
+    lib.rfm_pair_push_store.argtypes = [ctypes.POINTER(PairPush), _p]
+    lib.rfm_lsap_push.restype = _i32
+    lib.rfm_lsap_push.argtypes = [_p, _p, _p, ctypes.POINTER(LsapPlan), _p, _p, _p, _p, _p, _p]
+    lib.rfm_match_push.restype = _i32
+    lib.rfm_match_push.argtypes = [_p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _i64, _f32, _f32, _f32, _f32,
+                                   _p, _p, _p, ctypes.POINTER(LsapPlan), _p, _p, _p, _p, _p, _p]
+    lib.rfm_peer_alloc.restype = _i32
+    lib.rfm_peer_alloc.argtypes = [_i64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]
+    lib.rfm_peer_open.restype = _i32
+    lib.rfm_peer_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]
+    lib.rfm_peer_close.restype = _i32
+    lib.rfm_peer_close.argtypes = [_p]
+    lib.rfm_peer_free.restype = _i32
+    lib.rfm_peer_free.argtypes = [_p]
+    lib.rfm_peer_sync.restype = _i32
+    lib.rfm_peer_sync.argtypes = [ctypes.POINTER(PeerSyncArgs), _p]
     _lib = lib
     return lib
 

@@ -170,8 +170,15 @@ struct LsapArgs {
   const rfm_problem* problems;  // pair mode
   const int4* ctas;             // pair mode: {first problem, warps, slot bytes, 0} per CTA
   int num_problems;
-  int dense_w, dense_t;  // dense mode: uniform [P, W, T] problems
-  int dense_warps;
+  int dense_w;  // dense mode: uniform [P, W, T] problems
+  // the two modes' own fields share these 8 bytes (the parameter block keeps its size)
+  union {
+    struct {
+      int t;      // dense mode: tasks per problem
+      int warps;  // dense mode: warps per CTA
+    } dense;
+    const rfm_pair_push* push;  // pair mode: push list in device memory (rfm_pair_push_store), or null
+  } mode;
   int slot;              // dense and persistent modes: uniform shared-memory slot per warp
   int* queue;            // persistent mode: next-problem counter (zeroed before the launch)
   int claim_base;        // persistent mode: warps launched; warp w starts on problem w and
@@ -707,8 +714,8 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
   int nq, nt, qbase;
   if (kDense) {
     nq = a.dense_w;
-    nt = a.dense_t;
-    cost_off = static_cast<int64_t>(p) * a.dense_w * a.dense_t;
+    nt = a.mode.dense.t;
+    cost_off = static_cast<int64_t>(p) * a.dense_w * a.mode.dense.t;
     out_off = static_cast<int64_t>(p) * a.dense_w;
     scratch_off = cost_off;
     qbase = 0;
@@ -1172,6 +1179,22 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
       t_out[r] = col4row_s[r];
     }
   }
+  if (!kDense && a.mode.push != nullptr) {
+    // the problem's nr pairs (just written by this warp) also to every push
+    // destination (peers' gathered buffers), in the buffer of this step's parity
+    __syncwarp();
+    const rfm_pair_push* pl = a.mode.push;
+    const int count = min(pl->count, RFM_MAX_PUSH);  // checked when the list was stored
+    const int64_t off = out_off + static_cast<int64_t>(*pl->epoch & 1u) * pl->parity_stride;
+    for (int k = lane; k < nr; k += 32) {
+      const int64_t qv = q_out[k];
+      const int64_t tv = t_out[k];
+      for (int d = 0; d < count; ++d) {
+        pl->query_out[d][off + k] = qv;
+        pl->target_out[d][off + k] = tv;
+      }
+    }
+  }
   if (a.status != nullptr && lane == 0) a.status[p] = code;
   return next;
 }
@@ -1203,7 +1226,7 @@ __global__ void __launch_bounds__(32 * kMaxWarpsPerCta, min_ctas_per_sm(K, kVari
     return;
   }
   if (kDense) {
-    const int p = blockIdx.x * a.dense_warps + warp;
+    const int p = blockIdx.x * a.mode.dense.warps + warp;
     if (p < a.num_problems) {
       solve_problem<K, kDense, kVariant>(a, p, smem_raw + static_cast<int64_t>(warp) * a.slot, a.slot, lane);
     }
@@ -1604,12 +1627,27 @@ const void* dense_multi_kernel(int cols_per_lane, bool two) {
   return nullptr;
 }
 
+// A push list the solver accepts: none, or 1..RFM_MAX_PUSH destinations with
+// both rows and the step counter given.
+bool push_valid(const rfm_pair_push* push) {
+  if (push->count < 0 || push->count > RFM_MAX_PUSH || push->reserved != 0 || push->parity_stride < 0) {
+    return false;
+  }
+  if (push->count == 0) return true;
+  if (push->epoch == nullptr) return false;
+  for (int d = 0; d < push->count; ++d) {
+    if (push->query_out[d] == nullptr || push->target_out[d] == nullptr) return false;
+  }
+  return true;
+}
+
 // rfm_lsap; with `counter_zeroed` the persistent counter was reset by the cost
 // kernel that runs just before on the stream, so there is no memset and the
 // persistent launch overlaps that kernel's end.
 int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas, const rfm_lsap_plan* plan,
              int64_t* query_out, int64_t* target_out, int32_t* status, void* workspace, void* stream,
-             bool counter_zeroed) {
+             bool counter_zeroed, const rfm_pair_push* device_push) {
+  if ((reinterpret_cast<uintptr_t>(device_push) & 15u) != 0) return RFM_ERR_INVALID_ARGUMENT;
   if (plan == nullptr || plan->num_problems < 0 || plan->num_ctas < 0 || plan->max_rows < 1 ||
       plan->workspace_bytes < 0 || plan->stride_q < 0 || plan->stride_t < 0 ||
       plan->tile_cap_floats < 0 || plan->cta_smem_bytes < 0 || plan->cta_smem_bytes > kSmemPerBlockMax ||
@@ -1633,8 +1671,7 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
   a.ctas = reinterpret_cast<const int4*>(ctas);
   a.num_problems = plan->num_problems;
   a.dense_w = 0;
-  a.dense_t = 0;
-  a.dense_warps = 0;
+  a.mode.push = device_push;
   a.slot = 0;
   a.queue = nullptr;
   a.claim_base = 0;
@@ -1744,17 +1781,38 @@ int lsap_run(const float* cost, const rfm_problem* problems, const int32_t* ctas
 extern "C" int rfm_lsap(const float* cost, const rfm_problem* problems, const int32_t* ctas,
                         const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out,
                         int32_t* status, void* workspace, void* stream) {
-  return rfm::lsap_run(cost, problems, ctas, plan, query_out, target_out, status, workspace, stream, false);
+  return rfm::lsap_run(cost, problems, ctas, plan, query_out, target_out, status, workspace, stream, false, nullptr);
 }
 
-extern "C" int rfm_match(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
-                         const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
-                         int num_queries, int num_classes, int sum_targets, int64_t ld, float cost_class,
-                         float cost_bbox, float cost_giou, float focal_alpha, float* cost,
-                         const rfm_problem* problems, const int32_t* ctas, const rfm_lsap_plan* plan,
-                         int64_t* query_out, int64_t* target_out, int32_t* status, void* workspace,
-                         void* stream) {
+extern "C" int rfm_lsap_push(const float* cost, const rfm_problem* problems, const int32_t* ctas,
+                             const rfm_lsap_plan* plan, int64_t* query_out, int64_t* target_out,
+                             int32_t* status, void* workspace, const rfm_pair_push* device_push,
+                             void* stream) {
+  return rfm::lsap_run(cost, problems, ctas, plan, query_out, target_out, status, workspace, stream, false,
+                       device_push);
+}
+
+extern "C" int rfm_pair_push_store(const rfm_pair_push* push, void* device_dst) {
+  if (push == nullptr || device_dst == nullptr || (reinterpret_cast<uintptr_t>(device_dst) & 15u) != 0 ||
+      !rfm::push_valid(push)) {
+    return RFM_ERR_INVALID_ARGUMENT;
+  }
+  if (cudaMemcpy(device_dst, push, sizeof(rfm_pair_push), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    return RFM_ERR_LAUNCH;
+  }
+  return RFM_OK;
+}
+
+extern "C" int rfm_match_push(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+                              const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
+                              int num_queries, int num_classes, int sum_targets, int64_t ld, float cost_class,
+                              float cost_bbox, float cost_giou, float focal_alpha, float* cost,
+                              const rfm_problem* problems, const int32_t* ctas, const rfm_lsap_plan* plan,
+                              int64_t* query_out, int64_t* target_out, int32_t* status, void* workspace,
+                              const rfm_pair_push* device_push, void* stream) {
   using namespace rfm;
+  if ((reinterpret_cast<uintptr_t>(device_push) & 15u) != 0) return RFM_ERR_INVALID_ARGUMENT;
   // the solver must read the matrix this call writes: target-major, row stride ld
   if (plan == nullptr || plan->stride_q != 1 || plan->stride_t != ld ||
       (plan->num_problems > 0 && sum_targets < 1)) {
@@ -1772,7 +1830,20 @@ extern "C" int rfm_match(const float* pred_logits, const float* pred_boxes, cons
                           cost_bbox, cost_giou, focal_alpha, cost, reset ? static_cast<int*>(workspace) : nullptr,
                           stream);
   if (rc != RFM_OK) return rc;
-  return lsap_run(cost, problems, ctas, plan, query_out, target_out, status, workspace, stream, reset);
+  return lsap_run(cost, problems, ctas, plan, query_out, target_out, status, workspace, stream, reset,
+                  device_push);
+}
+
+extern "C" int rfm_match(const float* pred_logits, const float* pred_boxes, const int64_t* tgt_labels,
+                         const float* tgt_boxes, const int32_t* tgt_offsets, int num_layers, int num_images,
+                         int num_queries, int num_classes, int sum_targets, int64_t ld, float cost_class,
+                         float cost_bbox, float cost_giou, float focal_alpha, float* cost,
+                         const rfm_problem* problems, const int32_t* ctas, const rfm_lsap_plan* plan,
+                         int64_t* query_out, int64_t* target_out, int32_t* status, void* workspace,
+                         void* stream) {
+  return rfm_match_push(pred_logits, pred_boxes, tgt_labels, tgt_boxes, tgt_offsets, num_layers, num_images,
+                        num_queries, num_classes, sum_targets, ld, cost_class, cost_bbox, cost_giou, focal_alpha,
+                        cost, problems, ctas, plan, query_out, target_out, status, workspace, nullptr, stream);
 }
 
 namespace {
@@ -1842,8 +1913,8 @@ extern "C" int rfm_lsap_dense(const float* cost, int num_problems, int num_worke
   a.ctas = nullptr;
   a.num_problems = num_problems;
   a.dense_w = num_workers;
-  a.dense_t = num_tasks;
-  a.dense_warps = dp.warps;
+  a.mode.dense.t = num_tasks;
+  a.mode.dense.warps = dp.warps;
   a.slot = static_cast<int>(dp.slot);
   a.queue = nullptr;
   a.claim_base = 0;

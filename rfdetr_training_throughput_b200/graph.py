@@ -35,7 +35,7 @@ class MatchGraph:
 
     def __init__(self, sizes: Sequence[int], layers: int, queries: int, num_classes: int, group_detr: int, *,
                  weights: dict | None = None, device: torch.device | None = None, warmup: int = 2,
-                 out: torch.Tensor | None = None):
+                 out: torch.Tensor | None = None, push=None, post=None):
         if not torch.cuda.is_available():
             raise RuntimeError("MatchGraph needs a CUDA device (there is no CPU path)")
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
@@ -51,6 +51,8 @@ class MatchGraph:
         self.tgt_boxes = torch.full((total, 4), 0.25, dtype=torch.float32, device=device)
         self._targets = PackedTargets.from_checked_sizes(self.labels, self.tgt_boxes, self.sizes, total)
         self._out = out  # optional caller buffer the pairs are written into (e.g. a collective's send buffer)
+        self._push = push  # optional rfm_pair_push list the solver also writes every pair to
+        self._post = post  # optional callable enqueued after the step (captured with it)
 
         side = torch.cuda.Stream(device)
         side.wait_stream(torch.cuda.current_stream(device))
@@ -64,8 +66,11 @@ class MatchGraph:
         self.pairs = self.result.pairs
 
     def _step(self) -> MatchResult:
-        return match_packed(self.logits, self.boxes, self._targets, self.group_detr, weights=self.weights,
-                            out=self._out)
+        res = match_packed(self.logits, self.boxes, self._targets, self.group_detr, weights=self.weights,
+                           out=self._out, push=self._push)
+        if self._post is not None:
+            self._post()
+        return res
 
     def replay(self) -> MatchResult:
         """Re-run the captured step on the current contents of the input buffers."""

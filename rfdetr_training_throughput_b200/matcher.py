@@ -357,35 +357,47 @@ def launch_cost(logits: torch.Tensor, boxes: torch.Tensor, labels: torch.Tensor,
 
 
 def launch_lsap(cost: torch.Tensor, plan: StepPlan, pairs: torch.Tensor, status: torch.Tensor | None,
-                stream: ctypes.c_void_p | None = None) -> None:
-    """Enqueue ``rfm_lsap`` over a planned step; ``pairs`` is int64 [2, total_pairs]."""
+                stream: ctypes.c_void_p | None = None, push: int | None = None) -> None:
+    """Enqueue ``rfm_lsap`` over a planned step; ``pairs`` is int64 [2, total_pairs].  With ``push`` (the
+    device address of a stored ``rfm_pair_push``; ``rfm_lsap_push``) every pair also goes to the push
+    list's destinations."""
     lib = _lib.load()
     ws = None
     if plan.plan.workspace_bytes > 0:
         ws = torch.empty(int(plan.plan.workspace_bytes), dtype=torch.uint8, device=cost.device)
-    _lib.check("rfm_lsap", lib.rfm_lsap(
-        _ptr(cost), ctypes.c_void_p(plan.problems_ptr), ctypes.c_void_p(plan.ctas_ptr), ctypes.byref(plan.plan),
-        _ptr(pairs[0]), _ptr(pairs[1]), _ptr(status), _ptr(ws),
-        _stream_handle(cost.device) if stream is None else stream))
+    args = (_ptr(cost), ctypes.c_void_p(plan.problems_ptr), ctypes.c_void_p(plan.ctas_ptr), ctypes.byref(plan.plan),
+            _ptr(pairs[0]), _ptr(pairs[1]), _ptr(status), _ptr(ws))
+    st = _stream_handle(cost.device) if stream is None else stream
+    if push is None:
+        _lib.check("rfm_lsap", lib.rfm_lsap(*args, st))
+    else:
+        _lib.check("rfm_lsap_push", lib.rfm_lsap_push(*args, ctypes.c_void_p(push), st))
 
 
 def launch_match(logits: torch.Tensor, boxes: torch.Tensor, labels: torch.Tensor, tgt_boxes: torch.Tensor,
                  plan: StepPlan, sum_t: int, weights: dict, cost: torch.Tensor, pairs: torch.Tensor,
-                 status: torch.Tensor | None, stream: ctypes.c_void_p | None = None) -> None:
+                 status: torch.Tensor | None, stream: ctypes.c_void_p | None = None,
+                 push: int | None = None) -> None:
     """Enqueue ``rfm_match``: the cost kernel into the target-major ``cost`` [L, S, ld] and the solver over
-    it, overlapped at their boundary (no memset between them, programmatic launch of the solver)."""
+    it, overlapped at their boundary (no memset between them, programmatic launch of the solver).  With
+    ``push`` (the device address of a stored ``rfm_pair_push``; ``rfm_match_push``) every pair also goes
+    to the push list's destinations."""
     layers, nimg, queries, ncls = logits.shape
     lib = _lib.load()
     ws = None
     if plan.plan.workspace_bytes > 0:
         ws = torch.empty(int(plan.plan.workspace_bytes), dtype=torch.uint8, device=cost.device)
-    _lib.check("rfm_match", lib.rfm_match(
-        _ptr(logits), _ptr(boxes), _ptr(labels), _ptr(tgt_boxes), ctypes.c_void_p(plan.offsets_ptr),
-        layers, nimg, queries, ncls, sum_t, plan.ld,
-        float(weights["cost_class"]), float(weights["cost_bbox"]), float(weights["cost_giou"]),
-        float(weights["focal_alpha"]), _ptr(cost), ctypes.c_void_p(plan.problems_ptr), ctypes.c_void_p(plan.ctas_ptr),
-        ctypes.byref(plan.plan), _ptr(pairs[0]), _ptr(pairs[1]), _ptr(status), _ptr(ws),
-        _stream_handle(cost.device) if stream is None else stream))
+    args = (_ptr(logits), _ptr(boxes), _ptr(labels), _ptr(tgt_boxes), ctypes.c_void_p(plan.offsets_ptr),
+            layers, nimg, queries, ncls, sum_t, plan.ld,
+            float(weights["cost_class"]), float(weights["cost_bbox"]), float(weights["cost_giou"]),
+            float(weights["focal_alpha"]), _ptr(cost), ctypes.c_void_p(plan.problems_ptr),
+            ctypes.c_void_p(plan.ctas_ptr), ctypes.byref(plan.plan), _ptr(pairs[0]), _ptr(pairs[1]), _ptr(status),
+            _ptr(ws))
+    st = _stream_handle(cost.device) if stream is None else stream
+    if push is None:
+        _lib.check("rfm_match", lib.rfm_match(*args, st))
+    else:
+        _lib.check("rfm_match_push", lib.rfm_match_push(*args, ctypes.c_void_p(push), st))
 
 
 def raise_on_status(status: torch.Tensor) -> None:
@@ -412,11 +424,13 @@ def _record(events: dict | None, name: str) -> None:
 def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: PackedTargets,
                  group_detr: int = 1, *, weights: dict | None = None, check_status: bool = False,
                  extras: dict | None = None, events: dict | None = None,
-                 out: torch.Tensor | None = None) -> MatchResult:
+                 out: torch.Tensor | None = None, push: int | None = None) -> MatchResult:
     """One matcher step over logits ``[L, B, Q, C]`` and boxes ``[L, B, Q, 4]``, two launches.
 
     ``out``, when given, is an int64 ``[2, total_pairs]`` tensor (rows contiguous, e.g. a view
-    into a collective's send buffer) the pairs are written into.
+    into a collective's send buffer) the pairs are written into.  ``push``, when given, is the
+    device address of a stored ``rfm_pair_push`` list of further destinations (other ranks'
+    gathered buffers, see ``sharded.PeerExchange``) the solver writes every pair into as well.
     ``extras``, when given, receives the target-major cost buffer ``[L, S, ld]``
     (``"cost"``), its row stride and the step plan.  ``events``, when given,
     collects CUDA events recorded on the launching stream around each kernel
@@ -446,7 +460,7 @@ def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: P
     stream = _stream_handle(device)
     if events is None and sum_t > 0 and plan.problems.shape[0] > 0:
         # one call: the cost kernel and the solver overlapped at their boundary
-        launch_match(logits, boxes, tg.labels, tg.boxes, plan, sum_t, w, cost, pairs, status, stream)
+        launch_match(logits, boxes, tg.labels, tg.boxes, plan, sum_t, w, cost, pairs, status, stream, push)
     else:
         # two calls, so that events can be recorded around each kernel
         if sum_t > 0:
@@ -455,7 +469,7 @@ def match_packed(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, targets: P
             _record(events, "cost")
         if plan.problems.shape[0] > 0:
             _record(events, "lsap")
-            launch_lsap(cost, plan, pairs, status, stream)
+            launch_lsap(cost, plan, pairs, status, stream, push)
             _record(events, "lsap")
     if status is not None:
         raise_on_status(status)

@@ -11,10 +11,17 @@ rank's chunk is padded to the largest rank's pair count.  With ``padded=True``
 the result is the gathered buffer itself (``GatheredPairs``: per-image views at
 host-known offsets, no copy); otherwise the padding is squeezed out with one
 concatenation into a flat ``[2, total]`` tensor.
+
+``ShardedMatcher(exchange="push")`` replaces the all-gather on GPUs: the solver
+itself stores every pair into every rank's gathered buffer (``PeerExchange``:
+CUDA IPC mappings of the other ranks' buffers, plain stores over NVLink), and a
+one-warp barrier kernel ends the step, so the exchange overlaps the solve and
+the whole step is one graph replay.
 """
 
 from __future__ import annotations
 
+import ctypes
 from functools import lru_cache
 from typing import Callable, Sequence
 
@@ -136,6 +143,145 @@ class GatheredPairs:
         return out
 
 
+def exchange_layout(world: int, width: int) -> dict[str, int]:
+    """Byte layout of one rank's ``PeerExchange`` buffer: two ``[world, 2, width]`` int64 gathered
+    buffers (step parity 0 and 1; rank ``r``'s pairs in row ``r``), then a 256-byte block of
+    ``MAX_PUSH`` uint32 flags (flag ``j`` raised by rank ``j``), the step counter, the error word
+    and (at +64) this rank's ``rfm_pair_push`` list."""
+    from . import _lib
+
+    if not 1 <= world <= _lib.MAX_PUSH:
+        raise ValueError(f"a pushed exchange takes 1..{_lib.MAX_PUSH} ranks, not {world}")
+    if width < 0:
+        raise ValueError("width must be >= 0")
+    parity_elems = world * 2 * width
+    flags = (2 * parity_elems * 8 + 255) // 256 * 256
+    return {"parity_elems": parity_elems, "flags": flags, "epoch": flags + 4 * _lib.MAX_PUSH,
+            "error": flags + 4 * _lib.MAX_PUSH + 4, "push": flags + 64, "bytes": flags + 256}
+
+
+class _DeviceWords:
+    """``__cuda_array_interface__`` of ``n`` words at a raw device address, for ``torch.as_tensor``."""
+
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 2,
+                                         "strides": None}
+
+
+class PeerExchange:
+    """The gathered buffers of a pushed exchange, mapped on every rank of ``group``.
+
+    Each rank allocates one buffer (``exchange_layout``) with ``rfm_peer_alloc``, the ranks swap
+    the 64-byte IPC handles with ``all_gather_object``, and each rank maps the others' buffers
+    (``rfm_peer_open``).  ``push`` is the ``rfm_pair_push`` list that sends this rank's pairs into
+    row ``rank`` of every rank's buffer (itself included); ``sync`` enqueues the step's barrier
+    (``rfm_peer_sync``), which also advances the step counter that picks the buffer parity.  The
+    result of the last step stays readable until the step after the next one.  Waits are bounded
+    (``spin_limit`` polls, about a second by default); ``check`` reports a wait that gave up.
+    Call ``close`` on every rank (collectively) before the process group goes.
+    """
+
+    DEFAULT_SPIN_LIMIT = 1 << 19
+
+    def __init__(self, width: int, group=None, device: torch.device | None = None,
+                 spin_limit: int = DEFAULT_SPIN_LIMIT):
+        from . import _lib
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.width = int(width)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        lay = exchange_layout(self.world, self.width)
+        self.layout = lay
+        lib = _lib.load()
+        ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+        with torch.cuda.device(self.device):
+            _lib.check("rfm_peer_alloc", lib.rfm_peer_alloc(lay["bytes"], ctypes.byref(ptr), handle))
+        self.base = int(ptr.value)
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened: list[int] = []
+        peers = []
+        with torch.cuda.device(self.device):
+            for j, h in enumerate(handles):
+                if j == self.rank:
+                    peers.append(self.base)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check("rfm_peer_open", lib.rfm_peer_open(h, ctypes.byref(p)))
+                self._opened.append(int(p.value))
+                peers.append(int(p.value))
+        self.peers = peers
+        words = torch.as_tensor(_DeviceWords(self.base, 2 * lay["parity_elems"], "<i8"), device=self.device)
+        self.recv = [words[k * lay["parity_elems"]:(k + 1) * lay["parity_elems"]].view(self.world, 2, self.width)
+                     for k in (0, 1)]
+        self._control = torch.as_tensor(_DeviceWords(self.base + lay["flags"], 64, "<i4"), device=self.device)
+        row = self.rank * 2 * self.width * 8
+        plist = _lib.PairPush(count=self.world, reserved=0, parity_stride=lay["parity_elems"],
+                              epoch=self.base + lay["epoch"])
+        self.sync_args = _lib.PeerSyncArgs(world=self.world, rank=self.rank, spin_limit=int(spin_limit),
+                                           flags=self.base + lay["flags"], epoch=self.base + lay["epoch"],
+                                           error=self.base + lay["error"])
+        for j, p in enumerate(peers):
+            plist.query_out[j] = p + row
+            plist.target_out[j] = p + row + self.width * 8
+            self.sync_args.arrive[j] = p + lay["flags"] + 4 * self.rank
+        with torch.cuda.device(self.device):
+            _lib.check("rfm_pair_push_store", lib.rfm_pair_push_store(ctypes.byref(plist),
+                                                                      ctypes.c_void_p(self.base + lay["push"])))
+        self.push_list = plist
+        self.push = self.base + lay["push"]  # device address of the stored list, for the solver
+        self.steps = 0  # barriers executed (not counting captured ones)
+        self._closed = False
+        dist.barrier(group=group)  # every buffer mapped before any rank pushes
+
+    def sync(self) -> None:
+        """Enqueue the step's barrier on the current stream (captured into a graph when capturing)."""
+        from . import _lib
+        from .matcher import _stream_handle
+
+        _lib.check("rfm_peer_sync", _lib.load().rfm_peer_sync(ctypes.byref(self.sync_args),
+                                                              _stream_handle(self.device)))
+        if not torch.cuda.is_current_stream_capturing():
+            self.steps += 1
+
+    def parity(self) -> int:
+        """Buffer parity of the last step run (its barrier counted in ``steps``)."""
+        if self.steps == 0:
+            raise RuntimeError("no step has run on this exchange")
+        return (self.steps - 1) & 1
+
+    def result(self, counts: Sequence[int], per_rank: Sequence[tuple[int, ...]], layers: int) -> "GatheredPairs":
+        return GatheredPairs(self.recv[self.parity()], counts, per_rank, layers)
+
+    def error(self) -> int:
+        """The error word (synchronises): 1 when a barrier wait gave up."""
+        return int(self._control[(self.layout["error"] - self.layout["flags"]) // 4].item())
+
+    def check(self) -> None:
+        if self.error():
+            raise RuntimeError("pushed exchange: a rank did not reach the barrier in time")
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's, after every rank is done with them."""
+        from . import _lib
+
+        if self._closed:
+            return
+        self._closed = True
+        lib = _lib.load()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _lib.check("rfm_peer_close", lib.rfm_peer_close(ctypes.c_void_p(p)))
+        dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
+        self.recv, self._control = [], None
+        with torch.cuda.device(self.device):
+            _lib.check("rfm_peer_free", lib.rfm_peer_free(ctypes.c_void_p(self.base)))
+
+
 def gather_pairs(local_pairs: torch.Tensor, counts: Sequence[int], group=None) -> torch.Tensor:
     """All-gather ``[2, counts[rank]]`` int64 chunks; returns ``[2, sum(counts)]`` in rank order.
     Chunks are padded to the largest count; the padding is never read."""
@@ -204,33 +350,62 @@ def sharded_match(pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: t
 
 
 class ShardedMatcher:
-    """``sharded_match`` for a batch shape that repeats: this rank's step is a captured
-    ``MatchGraph`` writing straight into the all-gather's send buffer, so a call is one graph
-    replay and one ``all_gather_into_tensor`` (plus one concatenation unless the caller takes the
-    padded ``GatheredPairs``).  Inputs are this rank's
-    image range (``pred_logits`` ``[L, hi - lo, Q, C]`` etc.); construct it on every rank of
-    ``group`` with the same arguments."""
+    """``sharded_match`` for a batch shape that repeats.  Inputs are this rank's image range
+    (``pred_logits`` ``[L, hi - lo, Q, C]`` etc.); construct it on every rank of ``group`` with the
+    same arguments.
+
+    ``exchange="nccl"``: this rank's step is a captured ``MatchGraph`` writing straight into the
+    all-gather's send buffer, so a call is one graph replay and one ``all_gather_into_tensor``
+    (plus one concatenation unless the caller takes the padded ``GatheredPairs``).
+
+    ``exchange="push"`` (CUDA devices, up to 8 ranks): the captured step's solver stores every
+    pair into every rank's gathered buffer itself and the step ends with ``PeerExchange``'s
+    barrier kernel, so a call is one graph replay and no collective.  Results alternate between
+    two buffers; the one a call returns stays valid until the call after the next.  Call
+    ``close`` on every rank when done."""
 
     def __init__(self, sizes: Sequence[int], layers: int, queries: int, num_classes: int, group_detr: int, *,
-                 weights: dict | None = None, group=None, device: torch.device | None = None):
+                 weights: dict | None = None, group=None, device: torch.device | None = None,
+                 exchange: str = "nccl", spin_limit: int = PeerExchange.DEFAULT_SPIN_LIMIT):
         from .graph import MatchGraph
 
+        if exchange not in ("nccl", "push"):
+            raise ValueError(f"exchange must be 'nccl' or 'push', not {exchange!r}")
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.mode = exchange
         sizes = tuple(int(s) for s in sizes)
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.shard = _shard(sizes, layers, queries, group_detr, self.world, self.rank)
-        self.send, self.recv = self.shard.gather_buffers(device, self.world)
         n = self.shard.counts[self.rank]
-        self.graph = MatchGraph(self.shard.local_sizes, layers, queries, num_classes, group_detr, weights=weights,
-                                device=device, out=self.send[0, :, :n])
+        self.exchange = None
+        if exchange == "push":
+            self.exchange = PeerExchange(self.shard.width, group=group, device=device, spin_limit=spin_limit)
+            self.local = torch.empty((2, n), dtype=torch.int64, device=device)  # the solver's own copy
+            self.graph = MatchGraph(self.shard.local_sizes, layers, queries, num_classes, group_detr,
+                                    weights=weights, device=device, out=self.local, push=self.exchange.push,
+                                    post=self.exchange.sync)
+        else:
+            self.send, self.recv = self.shard.gather_buffers(device, self.world)
+            self.graph = MatchGraph(self.shard.local_sizes, layers, queries, num_classes, group_detr,
+                                    weights=weights, device=device, out=self.send[0, :, :n])
         self.bounds = (self.shard.lo, self.shard.hi)
         self.per_image = self.shard.per
 
+    def replay(self) -> None:
+        """Run the captured step on the graph's input buffers (push: the exchange included)."""
+        self.graph.replay()
+        if self.exchange is not None:
+            self.exchange.steps += 1
+
     def gather(self, padded: bool = False) -> torch.Tensor | GatheredPairs:
-        """All-gather the pairs the last replay wrote: ``[2, total]`` in rank order, or with
-        ``padded`` the gathered buffer itself (no concatenation)."""
+        """The whole batch's pairs of the last replay: ``[2, total]`` in rank order, or with
+        ``padded`` the gathered buffer itself (no concatenation).  ``nccl`` runs the all-gather
+        here; ``push`` has exchanged them already."""
+        if self.exchange is not None:
+            res = self.exchange.result(self.shard.counts, self.shard.per_rank, self.shard.layers)
+            return res if padded else res.flat()
         dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
         if padded:
             return GatheredPairs(self.recv, self.shard.counts, self.shard.per_rank, self.shard.layers)
@@ -239,4 +414,18 @@ class ShardedMatcher:
     def __call__(self, pred_logits: torch.Tensor, pred_boxes: torch.Tensor, labels: torch.Tensor,
                  tgt_boxes: torch.Tensor, padded: bool = False) -> torch.Tensor | GatheredPairs:
         self.graph(pred_logits, pred_boxes, labels, tgt_boxes)
+        if self.exchange is not None:
+            self.exchange.steps += 1
         return self.gather(padded)
+
+    def check(self) -> None:
+        """Raise if a pushed exchange's barrier gave up waiting (synchronises)."""
+        if self.exchange is not None:
+            self.exchange.check()
+
+    def close(self) -> None:
+        """Release the pushed exchange's mappings (collective over ``group``); the graph goes too."""
+        self.graph = None
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None

@@ -82,6 +82,63 @@ def test_invalid_arguments_are_rejected_before_any_cuda_call():
     assert lib.rfm_lsap_dense_workspace_bytes(-1, 3, 3) < 0
 
 
+def test_push_structs_match_header(tmp_path):
+    """ctypes mirrors of rfm_pair_push / rfm_peer_sync_args against the header, compiled with gcc."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no gcc")
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "rfm.h"\nint main(void) {\n'
+                   '  printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(rfm_pair_push), offsetof(rfm_pair_push, epoch),\n'
+                   '         offsetof(rfm_pair_push, target_out), sizeof(rfm_peer_sync_args),\n'
+                   '         offsetof(rfm_peer_sync_args, flags), offsetof(rfm_peer_sync_args, error));\n'
+                   '  return 0;\n}\n')
+    exe = tmp_path / "sz"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert got == [ctypes.sizeof(_lib.PairPush), _lib.PairPush.epoch.offset, _lib.PairPush.target_out.offset,
+                   ctypes.sizeof(_lib.PeerSyncArgs), _lib.PeerSyncArgs.flags.offset, _lib.PeerSyncArgs.error.offset]
+
+
+def test_push_and_peer_arguments_are_rejected_before_any_cuda_call():
+    lib = _lib.load()
+    fake = 1 << 40  # never dereferenced: every call below fails its checks first
+    for bad in (dict(count=9), dict(count=-1), dict(count=1, reserved=1), dict(count=1, epoch=None),
+                dict(count=2, epoch=fake, parity_stride=-1)):
+        push = _lib.PairPush(**{"count": 1, "epoch": fake, **bad})
+        for d in range(_lib.MAX_PUSH):
+            push.query_out[d] = fake
+            push.target_out[d] = fake
+        assert lib.rfm_pair_push_store(ctypes.byref(push), fake) == 1, bad
+    push = _lib.PairPush(count=2, epoch=fake)
+    push.query_out[0] = push.target_out[0] = push.query_out[1] = fake  # target_out[1] missing
+    assert lib.rfm_pair_push_store(ctypes.byref(push), fake) == 1
+    push.target_out[1] = fake
+    assert lib.rfm_pair_push_store(ctypes.byref(push), fake + 8) == 1  # destination not 16-byte aligned
+    assert lib.rfm_pair_push_store(None, fake) == 1 and lib.rfm_pair_push_store(ctypes.byref(push), None) == 1
+    plan = _lib.LsapPlan(cols_per_lane=10, max_rows=1, num_problems=3, num_ctas=1, cta_smem_bytes=4096,
+                         tile_cap_floats=0, flags=0, reserved=0, stride_q=1, stride_t=8, workspace_bytes=0)
+    assert lib.rfm_lsap_push(fake, fake, fake, ctypes.byref(plan), fake, fake, None, None, fake + 4, None) == 1
+    assert lib.rfm_peer_sync(None, None) == 1
+    for bad in (dict(world=0), dict(world=9), dict(rank=2), dict(rank=-1), dict(spin_limit=0), dict(flags=None),
+                dict(error=None), dict(epoch=None)):
+        args = _lib.PeerSyncArgs(**{"world": 2, "rank": 0, "spin_limit": 10, "flags": fake, "epoch": fake,
+                                    "error": fake, **bad})
+        args.arrive[0] = args.arrive[1] = fake
+        assert lib.rfm_peer_sync(ctypes.byref(args), None) == 1, bad
+    args = _lib.PeerSyncArgs(world=2, rank=0, spin_limit=10, flags=fake, epoch=fake, error=fake)
+    args.arrive[0] = fake  # arrive[1] missing
+    assert lib.rfm_peer_sync(ctypes.byref(args), None) == 1
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
+    assert lib.rfm_peer_alloc(0, ctypes.byref(ptr), handle) == 1
+    assert lib.rfm_peer_alloc(256, None, handle) == 1
+    assert lib.rfm_peer_open(None, ctypes.byref(ptr)) == 1
+    assert lib.rfm_peer_close(None) == 1 and lib.rfm_peer_free(None) == 1
+
+
 def _cta_cover(ctas, n):
     """The CTA table covers problems 0..n-1 once, in order, with 1-4 warps each."""
     nxt = 0

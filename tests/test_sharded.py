@@ -103,3 +103,18 @@ def test_sharded_match_on_two_gloo_ranks(tmp_path):
             off = sum(counts[: l * n])
             pieces.append(pairs_r[:, off:off + sum(counts[l * n:(l + 1) * n])])
         assert np.array_equal(got["views"][l], np.concatenate(pieces, axis=1)), l
+
+
+def test_exchange_layout():
+    """Two [world, 2, width] int64 buffers, then the flag block on a 256-byte boundary."""
+    for world, width in ((1, 0), (1, 7), (2, 100), (8, 13_000)):
+        lay = sharded.exchange_layout(world, width)
+        assert lay["parity_elems"] == world * 2 * width
+        assert lay["flags"] % 256 == 0 and lay["flags"] >= 2 * lay["parity_elems"] * 8
+        assert lay["epoch"] == lay["flags"] + 32 and lay["error"] == lay["flags"] + 36
+        assert lay["bytes"] == lay["flags"] + 256
+    for world in (0, 9):
+        with pytest.raises(ValueError):
+            sharded.exchange_layout(world, 4)
+    with pytest.raises(ValueError):
+        sharded.ShardedMatcher((3, 4), 1, 300, 2, 1, exchange="ring")

@@ -1180,18 +1180,27 @@ __device__ __forceinline__ int solve_problem(const LsapArgs& a, int p, unsigned 
     }
   }
   if (!kDense && a.mode.push != nullptr) {
-    // the problem's nr pairs (just written by this warp) also to every push
-    // destination (peers' gathered buffers), in the buffer of this step's parity
-    __syncwarp();
+    // the problem's nr pairs also to every push destination (peers' gathered
+    // buffers), in the buffer of this step's parity, rebuilt from shared memory
+    // as above (the transposed list is still in `remaining`)
+    // (the list and the step counter do not change during the launch: read-only loads)
     const rfm_pair_push* pl = a.mode.push;
-    const int count = min(pl->count, RFM_MAX_PUSH);  // checked when the list was stored
-    const int64_t off = out_off + static_cast<int64_t>(*pl->epoch & 1u) * pl->parity_stride;
-    for (int k = lane; k < nr; k += 32) {
-      const int64_t qv = q_out[k];
-      const int64_t tv = t_out[k];
-      for (int d = 0; d < count; ++d) {
-        pl->query_out[d][off + k] = qv;
-        pl->target_out[d][off + k] = tv;
+    const int count = min(__ldg(&pl->count), RFM_MAX_PUSH);  // checked when the list was stored
+    const int64_t off = out_off + static_cast<int64_t>(__ldg(pl->epoch) & 1u) * __ldg(&pl->parity_stride);
+    for (int d = 0; d < count; ++d) {
+      int64_t* const qd = reinterpret_cast<int64_t*>(__ldg(reinterpret_cast<const unsigned long long*>(
+                              &pl->query_out[d]))) + off;
+      int64_t* const td = reinterpret_cast<int64_t*>(__ldg(reinterpret_cast<const unsigned long long*>(
+                              &pl->target_out[d]))) + off;
+      for (int k = lane; k < nr; k += 32) {
+        int64_t qv = -1, tv = -1;
+        if (code == RFM_STATUS_OK) {
+          const int j = s.transposed ? rem_s[k] : k;
+          qv = j + qbase;
+          tv = s.transposed ? row4col_s[j] : col4row_s[k];
+        }
+        qd[k] = qv;
+        td[k] = tv;
       }
     }
   }

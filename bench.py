@@ -58,6 +58,7 @@ METRIC = "matched problems/s (cost+LSAP) at 1/2/4/8 B200; cost-kernel HBM GB/s v
 UNIT = "problems/s"
 FALLBACK_HBM_GBS = 6650.0
 L2_FLUSH_BYTES = 256 << 20
+PEER_COPY_GBS = 770.0  # measured peer copy over NVLink on these B200s, per direction per GPU
 LEAD_FILLS = 25  # writes of a 256 MiB buffer (~1 ms of device-side work) before each timed region
 _LEAD_BUF: dict = {}
 
@@ -1074,15 +1075,22 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier, images: int)
     ms = dict(zip(parts.keys(), vals))
     push_mismatch, push_error = vals[-2] > 0, int(vals[-1])
     gathered_pairs = int(sum(sm.shard.counts))
+    # bytes one rank's pushes send over NVLink (16 per pair to each other rank), the largest rank's
+    nvlink_bytes = max(16 * int(c) * (world - 1) for c in sm.shard.counts)
     del sm  # its graph holds no collective, but release it before the process group goes
     return {"images": wl.images, "problems_per_step": wl.num_problems, "steps": steps,
             "ms_per_step": ms["step"], "problems_per_s": wl.num_problems / (ms["step"] / 1e3),
             "breakdown_ms": {"replay": ms["replay"], "all_gather": ms["all_gather"],
                              "all_gather_plus_flat_concat": ms["flat_concat"]},
+            "best_exchange": "push" if ms["push_step"] < ms["step"] else "nccl",
+            "best_problems_per_s": wl.num_problems / (min(ms["push_step"], ms["step"]) / 1e3),
             "eager_ms_per_step": ms["eager_step"], "eager_problems_per_s": wl.num_problems / (ms["eager_step"] / 1e3),
             "graph_equals_eager": same, "gathered_pairs": gathered_pairs, "scaling": "strong",
             "push": {"ms_per_step": ms["push_step"], "problems_per_s": wl.num_problems / (ms["push_step"] / 1e3),
                      "equals_all_gather_on_every_rank": not push_mismatch, "barrier_gave_up": bool(push_error),
+                     "nvlink_bytes_per_rank": nvlink_bytes,
+                     "nvlink_floor_ms": nvlink_bytes / (PEER_COPY_GBS * 1e9) * 1e3,
+                     "over_replay_ms": ms["push_step"] - ms["replay"],
                      "exchange": "the solver stores every pair into every rank's gathered buffer (CUDA IPC peer "
                                  "mappings, plain stores over NVLink), then a one-warp flag barrier; one graph "
                                  "replay per step, no collective"},

@@ -1052,21 +1052,27 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier, images: int)
 
     # the same step with the pushed exchange: the solver stores every pair into every rank's
     # gathered buffer, a one-warp barrier ends the step; one graph replay, no collective
-    sp = sharded.ShardedMatcher(sizes, wl.layers, wl.queries, wl.classes, wl.group_detr, weights=wl.weights,
-                                device=device, exchange="push")
-    sp.graph.logits.copy_(logits)
-    sp.graph.boxes.copy_(boxes)
-    sp.graph.labels.copy_(labels)
-    sp.graph.tgt_boxes.copy_(tboxes)
+    push_unavailable = None
+    try:  # every rank raises together if any rank cannot map the others' buffers
+        sp = sharded.ShardedMatcher(sizes, wl.layers, wl.queries, wl.classes, wl.group_detr, weights=wl.weights,
+                                    device=device, exchange="push")
+    except RuntimeError as e:
+        sp, push_unavailable = None, str(e)
+    same_push, push_error = True, 0
+    if sp is not None:
+        sp.graph.logits.copy_(logits)
+        sp.graph.boxes.copy_(boxes)
+        sp.graph.labels.copy_(labels)
+        sp.graph.tgt_boxes.copy_(tboxes)
 
-    def push_step():
-        sp.replay()
-        return sp.gather(padded=True)
+        def push_step():
+            sp.replay()
+            return sp.gather(padded=True)
 
-    parts["push_step"] = mean_ms(push_step)
-    same_push = bool(torch.equal(push_step().flat(), step().flat()))
-    push_error = sp.exchange.error()
-    sp.close()
+        parts["push_step"] = mean_ms(push_step)
+        same_push = bool(torch.equal(push_step().flat(), step().flat()))
+        push_error = sp.exchange.error()
+        sp.close()
     t = torch.tensor(list(parts.values()) + [0.0 if same_push else 1.0, float(push_error)], dtype=torch.float64,
                      device=device)
     if world > 1:
@@ -1078,22 +1084,26 @@ def run_sharded_sweep(args, world: int, rank: int, device, barrier, images: int)
     # bytes one rank's pushes send over NVLink (16 per pair to each other rank), the largest rank's
     nvlink_bytes = max(16 * int(c) * (world - 1) for c in sm.shard.counts)
     del sm  # its graph holds no collective, but release it before the process group goes
-    return {"images": wl.images, "problems_per_step": wl.num_problems, "steps": steps,
-            "ms_per_step": ms["step"], "problems_per_s": wl.num_problems / (ms["step"] / 1e3),
-            "breakdown_ms": {"replay": ms["replay"], "all_gather": ms["all_gather"],
-                             "all_gather_plus_flat_concat": ms["flat_concat"]},
-            "best_exchange": "push" if ms["push_step"] < ms["step"] else "nccl",
-            "best_problems_per_s": wl.num_problems / (min(ms["push_step"], ms["step"]) / 1e3),
-            "eager_ms_per_step": ms["eager_step"], "eager_problems_per_s": wl.num_problems / (ms["eager_step"] / 1e3),
-            "graph_equals_eager": same, "gathered_pairs": gathered_pairs, "scaling": "strong",
-            "push": {"ms_per_step": ms["push_step"], "problems_per_s": wl.num_problems / (ms["push_step"] / 1e3),
+    if push_unavailable is not None:
+        push_info = {"unavailable": push_unavailable}
+    else:
+        push_info = {"ms_per_step": ms["push_step"], "problems_per_s": wl.num_problems / (ms["push_step"] / 1e3),
                      "equals_all_gather_on_every_rank": not push_mismatch, "barrier_gave_up": bool(push_error),
                      "nvlink_bytes_per_rank": nvlink_bytes,
                      "nvlink_floor_ms": nvlink_bytes / (PEER_COPY_GBS * 1e9) * 1e3,
                      "over_replay_ms": ms["push_step"] - ms["replay"],
                      "exchange": "the solver stores every pair into every rank's gathered buffer (CUDA IPC peer "
                                  "mappings, plain stores over NVLink), then a one-warp flag barrier; one graph "
-                                 "replay per step, no collective"},
+                                 "replay per step, no collective"}
+    return {"images": wl.images, "problems_per_step": wl.num_problems, "steps": steps,
+            "ms_per_step": ms["step"], "problems_per_s": wl.num_problems / (ms["step"] / 1e3),
+            "breakdown_ms": {"replay": ms["replay"], "all_gather": ms["all_gather"],
+                             "all_gather_plus_flat_concat": ms["flat_concat"]},
+            "best_exchange": "push" if ms.get("push_step", float("inf")) < ms["step"] else "nccl",
+            "best_problems_per_s": wl.num_problems / (min(ms.get("push_step", float("inf")), ms["step"]) / 1e3),
+            "eager_ms_per_step": ms["eager_step"], "eager_problems_per_s": wl.num_problems / (ms["eager_step"] / 1e3),
+            "graph_equals_eager": same, "gathered_pairs": gathered_pairs, "scaling": "strong",
+            "push": push_info,
             "result": "GatheredPairs (the all-gather's buffer, per-image views at host-known offsets)",
             "collective": "all_gather_into_tensor of int64 [2, width] per rank" if world > 1 else "none (1 rank)"}
 

@@ -194,24 +194,38 @@ class PeerExchange:
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         lay = exchange_layout(self.world, self.width)
         self.layout = lay
+        self.recv, self._control, self._opened, self.base, self._closed = [], None, [], 0, False
         lib = _lib.load()
         ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(_lib.IPC_HANDLE_BYTES)
         with torch.cuda.device(self.device):
-            _lib.check("rfm_peer_alloc", lib.rfm_peer_alloc(lay["bytes"], ctypes.byref(ptr), handle))
-        self.base = int(ptr.value)
+            rc = lib.rfm_peer_alloc(lay["bytes"], ctypes.byref(ptr), handle)
+        self.base = int(ptr.value) if rc == _lib.RFM_OK else 0
         handles: list = [None] * self.world
-        dist.all_gather_object(handles, handle.raw, group=group)
-        self._opened: list[int] = []
+        dist.all_gather_object(handles, handle.raw if self.base else None, group=group)
         peers = []
+        failure = None if self.base else f"rfm_peer_alloc: {_lib.error_string(rc)}"
         with torch.cuda.device(self.device):
             for j, h in enumerate(handles):
-                if j == self.rank:
+                if failure is not None:
+                    break
+                if h is None:
+                    failure = f"rank {j} has no buffer"
+                elif j == self.rank:
                     peers.append(self.base)
-                    continue
-                p = ctypes.c_void_p()
-                _lib.check("rfm_peer_open", lib.rfm_peer_open(h, ctypes.byref(p)))
-                self._opened.append(int(p.value))
-                peers.append(int(p.value))
+                else:
+                    p = ctypes.c_void_p()
+                    rc = lib.rfm_peer_open(h, ctypes.byref(p))
+                    if rc != _lib.RFM_OK:
+                        failure = f"rfm_peer_open of rank {j}: {_lib.error_string(rc)}"
+                        break
+                    self._opened.append(int(p.value))
+                    peers.append(int(p.value))
+        # every rank learns whether every rank mapped every buffer, so all of them go on or none does
+        ok = torch.tensor([0 if failure else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not bool(ok.item()):
+            self._release(lib)
+            raise RuntimeError(f"pushed exchange unavailable on rank {self.rank}: {failure or 'a peer failed'}")
         self.peers = peers
         words = torch.as_tensor(_DeviceWords(self.base, 2 * lay["parity_elems"], "<i8"), device=self.device)
         self.recv = [words[k * lay["parity_elems"]:(k + 1) * lay["parity_elems"]].view(self.world, 2, self.width)
@@ -233,7 +247,6 @@ class PeerExchange:
         self.push_list = plist
         self.push = self.base + lay["push"]  # device address of the stored list, for the solver
         self.steps = 0  # barriers executed (not counting captured ones)
-        self._closed = False
         dist.barrier(group=group)  # every buffer mapped before any rank pushes
 
     def sync(self) -> None:
@@ -263,6 +276,23 @@ class PeerExchange:
         if self.error():
             raise RuntimeError("pushed exchange: a rank did not reach the barrier in time")
 
+    def _release(self, lib) -> None:
+        """Collective teardown: every rank unmaps, then (nobody mapping them any more) frees."""
+        from . import _lib
+
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _lib.check("rfm_peer_close", lib.rfm_peer_close(ctypes.c_void_p(p)))
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.recv, self._control = [], None
+        if self.base:
+            with torch.cuda.device(self.device):
+                _lib.check("rfm_peer_free", lib.rfm_peer_free(ctypes.c_void_p(self.base)))
+            self.base = 0
+
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's, after every rank is done with them."""
         from . import _lib
@@ -270,16 +300,7 @@ class PeerExchange:
         if self._closed:
             return
         self._closed = True
-        lib = _lib.load()
-        torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
-        with torch.cuda.device(self.device):
-            for p in self._opened:
-                _lib.check("rfm_peer_close", lib.rfm_peer_close(ctypes.c_void_p(p)))
-        dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
-        self.recv, self._control = [], None
-        with torch.cuda.device(self.device):
-            _lib.check("rfm_peer_free", lib.rfm_peer_free(ctypes.c_void_p(self.base)))
+        self._release(_lib.load())
 
 
 def gather_pairs(local_pairs: torch.Tensor, counts: Sequence[int], group=None) -> torch.Tensor:

@@ -45,7 +45,7 @@ __global__ void peer_sync_kernel(const __grid_constant__ rfm_peer_sync_args a) {
         break;
       }
       __nanosleep(ns);
-      if (ns < 2048) ns <<= 1;
+      if (ns < 256) ns <<= 1;  // short sleeps: an arrival is seen within a fraction of a microsecond
     }
   }
   __syncwarp();

@@ -181,7 +181,7 @@ class PeerExchange:
     Call ``close`` on every rank (collectively) before the process group goes.
     """
 
-    DEFAULT_SPIN_LIMIT = 1 << 19
+    DEFAULT_SPIN_LIMIT = 1 << 22  # polls of at most 256 ns each: about a second
 
     def __init__(self, width: int, group=None, device: torch.device | None = None,
                  spin_limit: int = DEFAULT_SPIN_LIMIT):

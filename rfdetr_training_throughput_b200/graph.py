@@ -15,9 +15,10 @@ The graph reads its inputs from its own device buffers (``logits``, ``boxes``,
 ``pairs`` buffer (its own, or the ``out`` tensor given at construction): copy
 new inputs in (``__call__`` does) and read or copy the result before the next
 replay.  Stream capture covers the cost kernel (which also resets the
-solver's counter) and the solver kernel; plans and launch parameters are
-host-side values fixed at capture time, which is exactly what a fixed shape
-pins.
+solver's counter) and the solver kernel, plus whatever the optional ``post``
+hook enqueues after them (the pushed exchange's barrier kernel in
+``sharded.ShardedMatcher``); plans and launch parameters are host-side values
+fixed at capture time, which is exactly what a fixed shape pins.
 """
 
 from __future__ import annotations

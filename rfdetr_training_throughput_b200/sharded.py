@@ -201,7 +201,8 @@ class PeerExchange:
             rc = lib.rfm_peer_alloc(lay["bytes"], ctypes.byref(ptr), handle)
         self.base = int(ptr.value) if rc == _lib.RFM_OK else 0
         handles: list = [None] * self.world
-        dist.all_gather_object(handles, handle.raw if self.base else None, group=group)
+        with torch.cuda.device(self.device):  # NCCL's object gather stages on the current device
+            dist.all_gather_object(handles, handle.raw if self.base else None, group=group)
         peers = []
         failure = None if self.base else f"rfm_peer_alloc: {_lib.error_string(rc)}"
         with torch.cuda.device(self.device):
@@ -222,7 +223,8 @@ class PeerExchange:
                     peers.append(int(p.value))
         # every rank learns whether every rank mapped every buffer, so all of them go on or none does
         ok = torch.tensor([0 if failure else 1], dtype=torch.int32, device=self.device)
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        with torch.cuda.device(self.device):
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
         if not bool(ok.item()):
             self._release(lib)
             raise RuntimeError(f"pushed exchange unavailable on rank {self.rank}: {failure or 'a peer failed'}")
@@ -247,7 +249,8 @@ class PeerExchange:
         self.push_list = plist
         self.push = self.base + lay["push"]  # device address of the stored list, for the solver
         self.steps = 0  # barriers executed (not counting captured ones)
-        dist.barrier(group=group)  # every buffer mapped before any rank pushes
+        with torch.cuda.device(self.device):
+            dist.barrier(group=group)  # every buffer mapped before any rank pushes
 
     def sync(self) -> None:
         """Enqueue the step's barrier on the current stream (captured into a graph when capturing)."""
@@ -281,12 +284,12 @@ class PeerExchange:
         from . import _lib
 
         torch.cuda.synchronize(self.device)
-        dist.barrier(group=self.group)
         with torch.cuda.device(self.device):
+            dist.barrier(group=self.group)
             for p in self._opened:
                 _lib.check("rfm_peer_close", lib.rfm_peer_close(ctypes.c_void_p(p)))
-        self._opened = []
-        dist.barrier(group=self.group)
+            self._opened = []
+            dist.barrier(group=self.group)
         self.recv, self._control = [], None
         if self.base:
             with torch.cuda.device(self.device):

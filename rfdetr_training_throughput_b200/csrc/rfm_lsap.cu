@@ -59,6 +59,14 @@
 // with cp.async (SHARED), a larger one read in place (DIRECT) or first
 // transposed into the caller's workspace (SCRATCH).
 //
+// Pushed pairs (rfm_lsap_push / rfm_match_push, the sharded sweep's exchange):
+// the epilogue also stores each problem's pairs into every destination of a
+// push list in device memory (other ranks' gathered buffers, peer memory over
+// NVLink), rebuilt from shared memory after the local stores.  The list's
+// pointer travels in the argument words only dense batches use, so the
+// parameter block, and the code of every kernel that is not pushing, is
+// unchanged.
+//
 // Termination: every inner step removes one column from `remaining`, so each
 // augmentation is bounded by num_cols steps (kernels_lap.py:78-84,147-148);
 // the path flip is bounded by num_rows + 1 steps.  There are no spin-waits.

@@ -96,7 +96,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-configs", action="store_true", help="skip the per-configuration table (N = 1)")
     ap.add_argument("--config-cpu-seconds", type=float, default=2.0,
                     help="CPU time budget of each CPU leg of the per-configuration table")
-    ap.add_argument("--kernel", choices=["cost", "cost_qm", "lsap", "label", "box", "msda"], default=None,
+    ap.add_argument("--kernel", choices=["cost", "cost_qm", "lsap", "lsap_push", "label", "box", "msda"],
+                    default=None,
                     help="profiling mode: run only this kernel's workload a few times (for an ncu capture) and exit")
     return ap.parse_args()
 
@@ -1127,11 +1128,42 @@ def run_kernel(name: str, workload: str = "sweep", images: int | None = None) ->
     cost / lsap (the workload's step, issued as two calls), cost_qm (the drop-in query-major cost
     matrix, ``compute_compact_detection_cost_matrix``), label / box (the classification or the
     matched-box loss, forward and backward, on the workload's pairs), msda (deformable attention
-    forward and backward, decoder geometry)."""
+    forward and backward, decoder geometry), lsap_push (the sharded step with the pushed exchange on
+    a one-rank group: the solver with its push epilogue, replayed as a graph)."""
     from rfdetr_training_throughput_b200 import matcher, workloads
 
     dev = torch.device("cuda", 0)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    if name == "lsap_push":
+        import socket
+
+        from rfdetr_training_throughput_b200 import sharded
+
+        with socket.socket() as sock:
+            sock.bind(("127.0.0.1", 0))
+            port = sock.getsockname()[1]
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        torch.distributed.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
+        try:
+            wl = workloads.make(workload, images=images)
+            sm = sharded.ShardedMatcher(wl.sizes, wl.layers, wl.queries, wl.classes, wl.group_detr,
+                                        weights=wl.weights, device=dev, exchange="push")
+            sm.graph.logits.copy_(wl.pred_logits.to(dev))
+            sm.graph.boxes.copy_(wl.pred_boxes.to(dev))
+            pk = matcher.PackedTargets.from_list(wl.targets_on(dev), dev)
+            sm.graph.labels.copy_(pk.labels)
+            sm.graph.tgt_boxes.copy_(pk.boxes)
+            for _ in range(4):
+                sm.replay()
+                flush.zero_()
+            torch.cuda.synchronize()
+            sm.check()
+            sm.close()
+        finally:
+            torch.distributed.destroy_process_group()
+        print("kernel lsap_push: ok")
+        return
     if name == "cost_qm":
         wl = workloads.make(workload, images=images)
         lg, bx = wl.pred_logits.to(dev), wl.pred_boxes.to(dev)

@@ -385,7 +385,8 @@ class ShardedMatcher:
     ``exchange="push"`` (CUDA devices, up to 8 ranks): the captured step's solver stores every
     pair into every rank's gathered buffer itself and the step ends with ``PeerExchange``'s
     barrier kernel, so a call is one graph replay and no collective.  Results alternate between
-    two buffers; the one a call returns stays valid until the call after the next.  Call
+    two buffers; the one a call returns stays valid until the call after the next.  Run steps through
+    ``__call__`` or ``replay`` (not ``graph.replay``), which keep count of the buffer parity.  Call
     ``close`` on every rank when done."""
 
     def __init__(self, sizes: Sequence[int], layers: int, queries: int, num_classes: int, group_detr: int, *,
